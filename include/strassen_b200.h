@@ -1,0 +1,157 @@
+/*
+ * strassen_b200.h -- C ABI of the B200 (sm_100a) tile-local Strassen GEMM.
+ *
+ * Every entry point takes plain device pointers, sizes and a CUDA stream and
+ * returns an sb_status code; nothing throws and nothing traps.  Argument
+ * errors are detected on the host before any launch.  The caller owns every
+ * buffer: the library never allocates device memory.  Scratch space that an
+ * epilogue needs (norm_residual_add) is passed in as `workspace`, sized by
+ * sb_workspace_bytes().
+ *
+ * The single operator mirrors strassen_pallas.strassen_matmul
+ * (reference: strassen_pallas.py:882-1221).  Matrix semantics follow the
+ * reference exactly: C = A·B with A row-major [M,K], B row-major [K,N], and a
+ * one-level Strassen split applied inside every (bm, bn, bk) block, i.e. the
+ * ten operand sums pair element (r, c) of a block with (r + bm/2, c + bk/2)
+ * and (r + bk/2, c + bn/2) exactly as the reference's in-VMEM quadrant split
+ * does (strassen_pallas.py:188-204).
+ */
+#ifndef STRASSEN_B200_H_
+#define STRASSEN_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define SB_API __attribute__((visibility("default")))
+#else
+#define SB_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* cudaStream_t without pulling in the CUDA headers. */
+typedef void* sb_stream_t;
+
+/* ---- status codes (map 1:1 onto the reference's ValueError conditions) --- */
+typedef enum sb_status {
+  SB_OK = 0,
+  SB_ERR_RANK = 1,            /* strassen_pallas.py:927-928 rank-2 inputs       */
+  SB_ERR_INNER_DIM = 2,       /* :931-932 inner dimensions disagree              */
+  SB_ERR_DTYPE = 3,           /* :933-936 input dtype must be BF16 (B200 path)   */
+  SB_ERR_DIVISIBILITY = 4,    /* :1044-1046 M/N/K not divisible by bm/bn/bk      */
+  SB_ERR_TILING = 5,          /* :127-140 check_tiling alignment                  */
+  SB_ERR_EPILOGUE = 6,        /* :944-1002 epilogue argument contract            */
+  SB_ERR_OUTPUT_DTYPE = 7,    /* :955-958, :1048-1050 output dtype                */
+  SB_ERR_UNSUPPORTED = 8,     /* valid for the reference, not built for B200     */
+  SB_ERR_ALIGNMENT = 9,       /* pointer / leading-dimension alignment (TMA)     */
+  SB_ERR_WORKSPACE = 10,      /* workspace missing or too small                  */
+  SB_ERR_CUDA = 11,           /* a CUDA runtime call failed                      */
+  SB_ERR_DEVICE = 12,         /* device is not sm_100 (B200)                     */
+  SB_ERR_DEVICE_TIMEOUT = 13  /* a bounded in-kernel wait gave up                */
+} sb_status;
+
+/* ---- dtypes ------------------------------------------------------------- */
+typedef enum sb_dtype { SB_BF16 = 0, SB_F32 = 1 } sb_dtype;
+
+/* ---- fused epilogues (strassen_pallas.py:739-879) ------------------------ */
+typedef enum sb_epilogue_kind {
+  SB_EPI_NONE = 0,
+  SB_EPI_SWIGLU = 1,            /* :762-777, silu(gate)*up, output [M, N/2]   */
+  SB_EPI_GEGLU = 2,             /* :143-153, gelu_tanh(gate)*up               */
+  SB_EPI_RESIDUAL_ADD = 3,      /* :778-792                                   */
+  SB_EPI_BIAS_ADD = 4,          /* :867-874                                   */
+  SB_EPI_QK_NORM_ROPE = 5,      /* :793-835, per-head RMSNorm + RoPE          */
+  SB_EPI_NORM_RESIDUAL_ADD = 6  /* :836-866, row RMSNorm * scale + residual   */
+} sb_epilogue_kind;
+
+typedef struct sb_epilogue {
+  int32_t kind;               /* sb_epilogue_kind                                  */
+  /* residual_add / norm_residual_add: [M, N], leading dimension ld_residual     */
+  const void* residual;
+  int64_t ld_residual;
+  int32_t residual_dtype;     /* sb_dtype                                          */
+  /* dtype of bias, rope tables, rope scale and norm scale                       */
+  int32_t aux_dtype;          /* sb_dtype                                          */
+  const void* bias;           /* bias_add: [N]                                     */
+  const void* rope_cos;       /* qk_norm_rope: [M, bn/2] (rope_layout_tables)      */
+  const void* rope_sin;       /* qk_norm_rope: [M, bn/2]                           */
+  int64_t ld_rope;            /* leading dimension of rope_cos / rope_sin          */
+  const void* rope_scale;     /* qk_norm_rope: [bn] (rope_scale_layout)            */
+  int32_t rope_head_dim;      /* default 128                                       */
+  float rope_eps;             /* default 1e-6                                      */
+  const void* norm_scale;     /* norm_residual_add: [N]                            */
+  float norm_eps;             /* default 1e-6                                      */
+} sb_epilogue;
+
+/*
+ * sb_strassen_gemm -- C = epilogue(A·B) with one tile-local Strassen level.
+ *
+ * Replaces strassen_pallas.strassen_matmul (strassen_pallas.py:882-1221) for
+ * bf16 inputs.  bm/bn/bk are the reference's tile arguments and define the
+ * Strassen block, so results follow the reference's pairing of operands.
+ * Shapes: A [M,K] (lda), B [K,N] (ldb), C [M,N] (ldc) -- or [M, N/2] for the
+ * swiglu/geglu epilogues.  out_dtype: SB_BF16 or SB_F32 (SB_F32 only without
+ * an epilogue, as in the reference).  `ep` may be NULL for no epilogue.
+ * workspace / workspace_bytes: caller-owned scratch, required only when
+ * sb_workspace_bytes() returns a non-zero size.  Asynchronous on `stream`.
+ */
+SB_API int sb_strassen_gemm(sb_stream_t stream,
+                     const void* a, const void* b, void* c,
+                     int64_t m, int64_t n, int64_t k,
+                     int64_t lda, int64_t ldb, int64_t ldc,
+                     int32_t bm, int32_t bn, int32_t bk,
+                     int32_t out_dtype, const sb_epilogue* ep,
+                     void* workspace, size_t workspace_bytes);
+
+/* Scratch bytes sb_strassen_gemm needs for this problem (0 for most).
+ * Replaces the reference's VMEM scratch_shapes sizing (strassen_pallas.py:1074-1078). */
+SB_API size_t sb_workspace_bytes(int64_t m, int64_t n, int64_t k, int32_t epilogue_kind);
+
+/*
+ * sb_classical_gemm -- the matched-tile cubic control: the same kernel
+ * skeleton, tile and pipeline as sb_strassen_gemm but eight classical
+ * sub-block products and no operand sums.  Replaces the reference's Pallas
+ * cubic control (experiments/qwen3/benchmark_cubic_control.py:57-237,
+ * variant="blocked").  bf16 in, bf16/f32 out, no epilogue.
+ */
+SB_API int sb_classical_gemm(sb_stream_t stream,
+                      const void* a, const void* b, void* c,
+                      int64_t m, int64_t n, int64_t k,
+                      int64_t lda, int64_t ldb, int64_t ldc,
+                      int32_t bm, int32_t bn, int32_t bk, int32_t out_dtype);
+
+/*
+ * sb_rms_norm -- y = bf16(x * rsqrt(mean(x^2) + eps) * w), fp32 math.
+ * Replaces the reference's rms_norm
+ * (experiments/qwen3/benchmark_qwen3_32b_layer.py:270-276).  x, y: [rows, n]
+ * bf16 (ld = n), w: [n] in w_dtype.
+ */
+SB_API int sb_rms_norm(sb_stream_t stream, const void* x, const void* w, void* y,
+                int64_t rows, int64_t n, int32_t w_dtype, float eps);
+
+/* Internal tile shape of the kernel (product rows, product cols, k-chunk). */
+SB_API void sb_query_tile(int32_t* block_m, int32_t* block_n, int32_t* block_k);
+
+/* Human-readable text for a status code (static storage). */
+SB_API const char* sb_status_string(int32_t status);
+
+/* Detailed message of the last failing call on this host thread. */
+SB_API const char* sb_last_error_message(void);
+
+/*
+ * Reads (and with reset != 0 clears) the device-side error word that bounded
+ * in-kernel waits set when they give up.  Synchronises the current device.
+ */
+SB_API int sb_device_status(int32_t* device_error, int32_t reset);
+
+/* Library version string. */
+SB_API const char* sb_version(void);
+
+#ifdef __cplusplus
+}  /* extern "C" */
+#endif
+
+#endif  /* STRASSEN_B200_H_ */

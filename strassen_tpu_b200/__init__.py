@@ -1,0 +1,34 @@
+"""B200-native (sm_100a) tile-local Strassen GEMM with fused Qwen3 epilogues.
+
+Drop-in for the reference operator API ``strassen_pallas`` (sarsid/strassen-tpu):
+``strassen_matmul``, ``native_matmul``, ``check_tiling`` and the weight/table
+layout helpers.  The kernels live in ``csrc/`` behind the C ABI declared in
+``include/strassen_b200.h``.
+"""
+
+from .layouts import (
+    rope_layout_tables,
+    rope_layout_to_heads,
+    rope_scale_layout,
+    rope_weight_layout,
+    swiglu_weight_layout,
+)
+from .strassen import (
+    TUNED_BK,
+    TUNED_BM,
+    TUNED_BN,
+    check_tiling,
+    classical_matmul,
+    native_matmul,
+    rms_norm,
+    strassen_matmul,
+    workspace_bytes,
+)
+
+__all__ = [
+    "TUNED_BM", "TUNED_BN", "TUNED_BK",
+    "check_tiling", "classical_matmul", "native_matmul", "rms_norm", "strassen_matmul",
+    "workspace_bytes",
+    "rope_layout_tables", "rope_layout_to_heads", "rope_scale_layout", "rope_weight_layout",
+    "swiglu_weight_layout",
+]

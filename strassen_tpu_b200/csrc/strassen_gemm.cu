@@ -1,0 +1,1019 @@
+// strassen_gemm.cu -- tile-local one-level Strassen GEMM for B200 (sm_100a).
+//
+// Algorithm (reference: strassen_pallas.py:156-880).  The reference splits
+// every (bm, bk) A tile and (bk, bn) B tile into 2x2 quadrants, forms ten
+// bf16 operand sums, runs seven half-size products P1..P7 and accumulates four
+// fp32 quadrant accumulators over the K panels.  Because the quadrant
+// recombination is linear, the same result (up to fp32 summation order) is
+// obtained by accumulating each product over the whole K range first and
+// recombining once at the end.  Seen that way, each product Pi is an ordinary
+// GEMM of size (M/2) x (N/2) x (K/2) over "product coordinates": product row t
+// is row r' of block I = t / (bm/2), product column u is column c' of block
+// J = u / (bn/2), and product depth kappa is column k' of panel
+// P = kappa / (bk/2).  The reference's quadrant q of block (I, J) is the
+// matrix element (I*bm + qr*bm/2 + r', J*bn + qc*bn/2 + c').
+//
+// B200 mapping (one CTA per SM, persistent over nothing -- one output tile):
+//   * CTA tile: 128 product rows x 64 product columns, i.e. a 256 x 128 patch
+//     of C made of four 128 x 64 quadrant pieces.
+//   * TMEM: seven fp32 accumulators M1..M7 of 128 lanes x 64 columns
+//     (448 of the 512 columns).
+//   * Warp 0: TMA producer.  Per K-chunk it loads the four raw A quadrant
+//     tiles (128 x 32, K-major, 64B swizzle) and four raw B quadrant tiles
+//     (32 x 64, N-major, 128B swizzle) into one pipeline stage.
+//   * Warps 4..11: operand-sum warps.  They form the five A sums and five B
+//     sums in place in shared memory with bf16x2 adds (round-to-nearest-even,
+//     exactly the reference's bf16 pre-add rounding).  All tiles of a stage
+//     share one shape and swizzle, so the sums are plain elementwise ops over
+//     the raw 16-byte chunks.
+//   * Warp 1: TMEM allocator and single-thread tcgen05.mma issuer (7 products
+//     x BLOCK_K/16 MMAs of 128x64x16 per chunk), committing to mbarriers.
+//   * Warps 4..11 again, after the K loop: epilogue.  Each thread owns one
+//     TMEM lane (= one product row), reads M1..M7 with tcgen05.ld, recombines
+//     C11 = M1+M4-M5+M7, C12 = M3+M5, C21 = M2+M4, C22 = M1-M2+M3+M6 in fp32,
+//     applies the fused epilogue and stores bf16 (or fp32).
+//
+// The same skeleton also runs the matched-tile classical control (eight
+// sub-block products into four accumulators, no operand sums), which mirrors
+// the reference's blocked cubic Pallas control
+// (experiments/qwen3/benchmark_cubic_control.py:57-237).
+
+#include "sm100_primitives.cuh"
+#include "strassen_b200.h"
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <cuda_bf16.h>
+
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+
+namespace sb {
+
+// ------------------------------------------------------------------ shape
+constexpr int kBlockM = 128;  // product rows per CTA = TMEM lanes
+constexpr int kBlockN = 64;   // product columns per CTA = TMEM columns per product
+constexpr int kBlockK = 32;   // product depth per pipeline stage
+constexpr int kStages = 2;
+constexpr int kSlots = 7;     // operand tiles per side and stage
+constexpr int kASlotBytes = kBlockM * kBlockK * 2;              // 8192
+constexpr int kBSlotBytes = kBlockK * kBlockN * 2;              // 4096
+constexpr int kStageBytes = kSlots * (kASlotBytes + kBSlotBytes);  // 86016
+constexpr int kRawTxBytes = 4 * (kASlotBytes + kBSlotBytes);      // 49152
+constexpr int kFirstSumWarp = 4;
+constexpr int kSumWarps = 8;
+constexpr int kThreads = (kFirstSumWarp + kSumWarps) * 32;  // 384
+constexpr uint32_t kTmemCols = 512;
+constexpr int kBarrierBytes = 256;
+constexpr int kSmemBytes = kStages * kStageBytes + kBarrierBytes + 1024;  // + alignment slack
+
+static_assert(kBlockK == 32, "A-operand swizzle below assumes 64-byte K rows");
+static_assert(kStageBytes % 1024 == 0, "stages must keep 1024-byte alignment");
+static_assert(7 * kBlockN <= (int)kTmemCols, "seven accumulators must fit in TMEM");
+
+// A: K-major, 64-byte rows -> 64B swizzle, 8-row core groups 512 bytes apart.
+constexpr uint32_t kALayout = kLayoutSwizzle64B;
+constexpr uint32_t kASbo = 8 * kBlockK * 2;  // 512
+constexpr uint32_t kALbo = 16;               // unused for swizzled K-major
+// B: N-major, 128-byte rows (64 columns) -> 128B swizzle, 8 k-rows per 1024 B.
+constexpr uint32_t kBLayout = kLayoutSwizzle128B;
+constexpr uint32_t kBSbo = 1024;
+constexpr uint32_t kBLbo = kBlockK * 128;    // next 64-column chunk (never used: N tile = 64)
+constexpr uint32_t kIdesc = umma_idesc_bf16_f32(kBlockM, kBlockN, false, true);
+
+// Operand slots inside a stage.  Raw tiles land in slots 0..3
+// (a0=A[top,left] a1=A[top,right] a2=A[bottom,left] a3=A[bottom,right];
+//  b0=B[top,left] b1=B[top,right] b2=B[bottom,left] b3=B[bottom,right]).
+// The sum warps then overwrite a1/a2/b1/b2 (not needed raw) and fill 4..6:
+//   A: s1 <- a0+a1 (P5)  s2 <- a2-a0 (P6)  s4 <- a0+a3 (P1)  s5 <- a2+a3 (P2)  s6 <- a1-a3 (P7)
+//   B: s1 <- b1-b3 (P3)  s2 <- b2-b0 (P4)  s4 <- b0+b3 (P1)  s5 <- b0+b1 (P6)  s6 <- b2+b3 (P7)
+// Product Pi (strassen_pallas.py:324-379) reads A slot kASlot[i-1], B slot kBSlot[i-1]:
+//   P1=(a0+a3)(b0+b3)  P2=(a2+a3)b0  P3=a0(b1-b3)  P4=a3(b2-b0)
+//   P5=(a0+a1)b3       P6=(a2-a0)(b0+b1)           P7=(a1-a3)(b2+b3)
+__constant__ int kASlot[7] = {4, 5, 0, 3, 1, 2, 6};
+__constant__ int kBSlot[7] = {4, 0, 1, 2, 3, 5, 6};
+// Classical control: C0+=a0b0, C0+=a1b2, C1+=a0b1, C1+=a1b3, C2+=a2b0, C2+=a3b2,
+// C3+=a2b1, C3+=a3b3 (strassen_pallas.py:575-586 order).
+__constant__ int kCAslot[8] = {0, 1, 0, 1, 2, 3, 2, 3};
+__constant__ int kCBslot[8] = {0, 2, 1, 3, 0, 2, 1, 3};
+
+struct GemmParams {
+  int32_t M, N, K;
+  int32_t bm, bn, bk;
+  int32_t half_bm, half_bn, half_bk;
+  int32_t Mp, Np;
+  int32_t num_chunks;
+  int32_t tiles_m, tiles_n;
+  void* C;
+  int64_t ldc;
+  const void* residual;
+  int64_t ldr;
+  int32_t residual_f32;
+  int32_t aux_f32;
+  const void* bias;
+  const void* rope_cos;
+  const void* rope_sin;
+  int64_t ld_rope;
+  const void* rope_scale;
+  int32_t half_head;
+  float inv_head_dim;
+  float eps;
+  int* err;
+};
+
+__device__ int g_device_error = 0;
+
+enum : int {
+  kErrWaitRaw = 1,
+  kErrWaitSums = 2,
+  kErrWaitEmpty = 3,
+  kErrWaitAcc = 4,
+};
+
+__device__ __forceinline__ float load_aux(const void* p, int64_t idx, int f32) {
+  if (f32) return __ldg(reinterpret_cast<const float*>(p) + idx);
+  return __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(p)[idx]);
+}
+
+__device__ __forceinline__ void load8(const void* base, int64_t idx, int f32, float (&v)[8]) {
+  if (f32) {
+    const float4* q = reinterpret_cast<const float4*>(reinterpret_cast<const float*>(base) + idx);
+    float4 x = q[0], y = q[1];
+    v[0] = x.x; v[1] = x.y; v[2] = x.z; v[3] = x.w;
+    v[4] = y.x; v[5] = y.y; v[6] = y.z; v[7] = y.w;
+  } else {
+    uint4 u = *reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(base) + idx);
+    const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      float2 f = __bfloat1622float2(h[i]);
+      v[2 * i] = f.x;
+      v[2 * i + 1] = f.y;
+    }
+  }
+}
+
+template <bool kOutF32>
+__device__ __forceinline__ void store8(void* base, int64_t idx, const float (&v)[8]) {
+  if (kOutF32) {
+    float4* q = reinterpret_cast<float4*>(reinterpret_cast<float*>(base) + idx);
+    q[0] = make_float4(v[0], v[1], v[2], v[3]);
+    q[1] = make_float4(v[4], v[5], v[6], v[7]);
+  } else {
+    uint4 u = make_uint4(pack_bf16x2(v[0], v[1]), pack_bf16x2(v[2], v[3]), pack_bf16x2(v[4], v[5]),
+                         pack_bf16x2(v[6], v[7]));
+    *reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(base) + idx) = u;
+  }
+}
+
+__device__ __forceinline__ float silu_f32(float x) { return x / (1.0f + expf(-x)); }
+__device__ __forceinline__ float gelu_tanh_f32(float x) {
+  const float k0 = 0.7978845608028654f;  // sqrt(2/pi)
+  const float k1 = 0.044715f;
+  return 0.5f * x * (1.0f + tanhf(k0 * (x + k1 * x * x * x)));
+}
+
+// Recombined quadrant values for 8 consecutive product columns of this
+// thread's product row.
+struct Quad8 {
+  float c[4][8];
+};
+
+template <bool kStrassen>
+__device__ __forceinline__ void read_quadrants(uint32_t tmem_row, int col, Quad8& out) {
+  if constexpr (kStrassen) {
+    float m[7][8];
+#pragma unroll
+    for (int i = 0; i < 7; ++i) tmem_load_8(tmem_row + i * kBlockN + col, m[i]);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      // strassen_pallas.py:324-379 quadrant updates, summed once.
+      out.c[0][e] = ((m[0][e] + m[3][e]) - m[4][e]) + m[6][e];
+      out.c[1][e] = m[2][e] + m[4][e];
+      out.c[2][e] = m[1][e] + m[3][e];
+      out.c[3][e] = ((m[0][e] - m[1][e]) + m[2][e]) + m[5][e];
+    }
+  } else {
+#pragma unroll
+    for (int q = 0; q < 4; ++q) tmem_load_8(tmem_row + q * kBlockN + col, out.c[q]);
+  }
+}
+
+template <bool kStrassen, int kEpi, bool kOutF32>
+__global__ void __launch_bounds__(kThreads, 1)
+    strassen_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a,
+                         const __grid_constant__ CUtensorMap tmap_b, const GemmParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw_addr = smem_addr(smem_raw);
+  uint8_t* smem = smem_raw + ((1024u - (raw_addr & 1023u)) & 1023u);
+  const uint32_t smem_base = smem_addr(smem);
+
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kStages * kStageBytes);
+  const uint32_t full_bar = smem_addr(bars);                 // [kStages] TMA landed
+  const uint32_t sums_bar = smem_addr(bars + kStages);       // [kStages] operand sums ready
+  const uint32_t empty_bar = smem_addr(bars + 2 * kStages);  // [kStages] MMAs done reading
+  const uint32_t acc_bar = smem_addr(bars + 3 * kStages);    // accumulators final
+  const uint32_t qss_bar = smem_addr(bars + 3 * kStages + 1);  // q/k partial sums written
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 3 * kStages + 2);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  // Grouped rasterisation: walk 8 product-row tiles per column sweep for L2 reuse.
+  const int tile = blockIdx.x;
+  const int group_rows = 8;
+  const int per_group = group_rows * p.tiles_n;
+  const int group = tile / per_group;
+  const int first_m = group * group_rows;
+  const int rows_in_group = min(p.tiles_m - first_m, group_rows);
+  const int in_group = tile - group * per_group;
+  const int tm = first_m + in_group % rows_in_group;
+  const int tn = in_group / rows_in_group;
+  const int t0 = tm * kBlockM;  // first product row
+  const int u0 = tn * kBlockN;  // first product column
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(full_bar + 8 * s, 1);
+      mbar_init(sums_bar + 8 * s, kSumWarps);
+      mbar_init(empty_bar + 8 * s, 1);
+    }
+    mbar_init(acc_bar, 1);
+    mbar_init(qss_bar, kSumWarps);
+    *abort_flag = 0;
+    fence_mbar_init();
+    fence_proxy_async_smem();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmap_a);
+    tma_prefetch_desc(&tmap_b);
+  }
+  if (warp == 1) tmem_alloc<kTmemCols>(smem_addr(tmem_holder));
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_holder;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      int last_issued[kStages];
+#pragma unroll
+      for (int s = 0; s < kStages; ++s) last_issued[s] = -1;
+      const int a_row_base = t0 % p.half_bm;  // 0 when a tile spans several blocks
+      const int a_block = t0 / p.half_bm;
+      const int j_block = u0 / p.half_bn;
+      const int b_col0 = j_block * p.bn + (u0 % p.half_bn);
+      for (int c = 0; c < p.num_chunks; ++c) {
+        const int s = c % kStages;
+        const uint32_t ph = (c / kStages) & 1u;
+        if (!mbar_wait(empty_bar + 8 * s, ph ^ 1u, abort_flag, p.err, kErrWaitEmpty)) break;
+        const uint32_t fb = full_bar + 8 * s;
+        mbar_arrive_expect_tx(fb, kRawTxBytes);
+        const int kap = c * kBlockK;
+        const int panel = kap / p.half_bk;
+        const int kin = kap - panel * p.half_bk;
+        const uint32_t stage = smem_base + s * kStageBytes;
+#pragma unroll
+        for (int qk = 0; qk < 2; ++qk) {
+          const int kcol = panel * p.bk + qk * p.half_bk + kin;
+#pragma unroll
+          for (int qr = 0; qr < 2; ++qr) {
+            tma_load_3d(stage + (2 * qr + qk) * kASlotBytes, &tmap_a, fb, kcol,
+                        qr * p.half_bm + a_row_base, a_block);
+          }
+#pragma unroll
+          for (int qc = 0; qc < 2; ++qc) {
+            tma_load_2d(stage + kSlots * kASlotBytes + (2 * qk + qc) * kBSlotBytes, &tmap_b, fb,
+                        b_col0 + qc * p.half_bn, kcol);
+          }
+        }
+        last_issued[s] = c;
+      }
+      // Drain: never leave a TMA write in flight past teardown.
+#pragma unroll
+      for (int s = 0; s < kStages; ++s) {
+        if (last_issued[s] >= 0) mbar_wait_drain(full_bar + 8 * s, (last_issued[s] / kStages) & 1u);
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      for (int c = 0; c < p.num_chunks; ++c) {
+        const int s = c % kStages;
+        const uint32_t ph = (c / kStages) & 1u;
+        if (!mbar_wait(full_bar + 8 * s, ph, abort_flag, p.err, kErrWaitRaw)) break;
+        if constexpr (kStrassen) {
+          if (!mbar_wait(sums_bar + 8 * s, ph, abort_flag, p.err, kErrWaitSums)) break;
+        }
+        tc_fence_after();
+        const uint32_t a_stage = smem_base + s * kStageBytes;
+        const uint32_t b_stage = a_stage + kSlots * kASlotBytes;
+#pragma unroll
+        for (int kk = 0; kk < kBlockK / 16; ++kk) {
+          if constexpr (kStrassen) {
+#pragma unroll
+            for (int i = 0; i < 7; ++i) {
+              const uint64_t ad =
+                  umma_smem_desc(a_stage + kASlot[i] * kASlotBytes + kk * 32, kALbo, kASbo, kALayout);
+              const uint64_t bd = umma_smem_desc(b_stage + kBSlot[i] * kBSlotBytes + kk * 2048,
+                                                 kBLbo, kBSbo, kBLayout);
+              umma_bf16_ss(tmem_base + i * kBlockN, ad, bd, kIdesc, (c | kk) != 0 ? 1u : 0u);
+            }
+          } else {
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+              const uint64_t ad = umma_smem_desc(a_stage + kCAslot[i] * kASlotBytes + kk * 32, kALbo,
+                                                 kASbo, kALayout);
+              const uint64_t bd = umma_smem_desc(b_stage + kCBslot[i] * kBSlotBytes + kk * 2048,
+                                                 kBLbo, kBSbo, kBLayout);
+              const bool first = (c == 0) && (kk == 0) && ((i & 1) == 0);
+              umma_bf16_ss(tmem_base + (i >> 1) * kBlockN, ad, bd, kIdesc, first ? 0u : 1u);
+            }
+          }
+        }
+        umma_commit(empty_bar + 8 * s);
+      }
+      // Always commit: the epilogue (or the teardown drain) waits on it.
+      umma_commit(acc_bar);
+    }
+  } else if (warp >= kFirstSumWarp) {
+    const int sum_tid = threadIdx.x - kFirstSumWarp * 32;  // 0..255
+    bool ok = true;
+    // ------------------------------------------------------------ operand sums
+    if constexpr (kStrassen) {
+      for (int c = 0; c < p.num_chunks; ++c) {
+        const int s = c % kStages;
+        const uint32_t ph = (c / kStages) & 1u;
+        if (!warp_wait(full_bar + 8 * s, ph, abort_flag, p.err, kErrWaitRaw)) {
+          ok = false;
+          break;
+        }
+        const uint32_t a_stage = smem_base + s * kStageBytes;
+        const uint32_t b_stage = a_stage + kSlots * kASlotBytes;
+#pragma unroll
+        for (int r = 0; r < kASlotBytes / 16 / (kSumWarps * 32); ++r) {
+          const uint32_t off = (sum_tid + r * kSumWarps * 32) * 16;
+          const uint4 a0 = lds128(a_stage + 0 * kASlotBytes + off);
+          const uint4 a1 = lds128(a_stage + 1 * kASlotBytes + off);
+          const uint4 a2 = lds128(a_stage + 2 * kASlotBytes + off);
+          const uint4 a3 = lds128(a_stage + 3 * kASlotBytes + off);
+          sts128(a_stage + 4 * kASlotBytes + off, add4(a0, a3));
+          sts128(a_stage + 5 * kASlotBytes + off, add4(a2, a3));
+          sts128(a_stage + 6 * kASlotBytes + off, sub4(a1, a3));
+          sts128(a_stage + 1 * kASlotBytes + off, add4(a0, a1));
+          sts128(a_stage + 2 * kASlotBytes + off, sub4(a2, a0));
+        }
+#pragma unroll
+        for (int r = 0; r < kBSlotBytes / 16 / (kSumWarps * 32); ++r) {
+          const uint32_t off = (sum_tid + r * kSumWarps * 32) * 16;
+          const uint4 b0 = lds128(b_stage + 0 * kBSlotBytes + off);
+          const uint4 b1 = lds128(b_stage + 1 * kBSlotBytes + off);
+          const uint4 b2 = lds128(b_stage + 2 * kBSlotBytes + off);
+          const uint4 b3 = lds128(b_stage + 3 * kBSlotBytes + off);
+          sts128(b_stage + 4 * kBSlotBytes + off, add4(b0, b3));
+          sts128(b_stage + 5 * kBSlotBytes + off, add4(b0, b1));
+          sts128(b_stage + 6 * kBSlotBytes + off, add4(b2, b3));
+          sts128(b_stage + 1 * kBSlotBytes + off, sub4(b1, b3));
+          sts128(b_stage + 2 * kBSlotBytes + off, sub4(b2, b0));
+        }
+        // Make the generic-proxy writes visible to the tensor core, then signal.
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(sums_bar + 8 * s);
+      }
+    }
+
+    // ------------------------------------------------------------ epilogue
+    if (ok && warp_wait(acc_bar, 0, abort_flag, p.err, kErrWaitAcc)) {
+      tc_fence_after();
+      const int q = warp & 3;                  // TMEM lane quarter this warp may read
+      const int h = (warp - kFirstSumWarp) >> 2;  // which 32-column half of the tile
+      const int row_in_tile = 32 * q + lane;
+      const int t = t0 + row_in_tile;
+      const bool row_ok = t < p.Mp;
+      const int blk_i = t / p.half_bm;
+      const int rp = t - blk_i * p.half_bm;
+      const int64_t row_top = (int64_t)blk_i * p.bm + rp;
+      const int64_t row_bot = row_top + p.half_bm;
+      const int j_block = u0 / p.half_bn;
+      const int cp_base = u0 - j_block * p.half_bn;  // column inside the half block
+      const int64_t col_left0 = (int64_t)j_block * p.bn + cp_base;
+      const uint32_t tmem_row = tmem_base + ((uint32_t)(32 * q) << 16);
+
+      if constexpr (kEpi == SB_EPI_QK_NORM_ROPE) {
+        // Per-head sum of squares over both halves of every head
+        // (strassen_pallas.py:793-835).  A head's a-half lies in quadrant 0/2,
+        // its b-half at the same offset in quadrant 1/3.  Pass 1 writes this
+        // thread's partial sums per head slot, pass 2 normalises and rotates.
+        float* qss = reinterpret_cast<float*>(smem);  // stage memory is idle now
+        bool return_early = false;
+        auto qidx = [&](int hh, int tb, int slot) { return ((hh * 2 + tb) * kBlockM + row_in_tile) * 8 + slot; };
+#pragma unroll
+        for (int slot = 0; slot < 8; ++slot) {
+          qss[qidx(h, 0, slot)] = 0.f;
+          qss[qidx(h, 1, slot)] = 0.f;
+        }
+#pragma unroll 1
+        for (int j = 0; j < 4; ++j) {
+          const int col = 32 * h + 8 * j;
+          Quad8 v;
+          read_quadrants<kStrassen>(tmem_row, col, v);
+          const int slot = col / p.half_head;
+          float st = 0.f, sbm = 0.f;
+#pragma unroll
+          for (int e = 0; e < 8; ++e) {
+            st += v.c[0][e] * v.c[0][e] + v.c[1][e] * v.c[1][e];
+            sbm += v.c[2][e] * v.c[2][e] + v.c[3][e] * v.c[3][e];
+          }
+          qss[qidx(h, 0, slot)] += st;
+          qss[qidx(h, 1, slot)] += sbm;
+        }
+        // Exchange partial sums between the two column halves (bounded wait).
+        __syncwarp();
+        if (lane == 0) mbar_arrive(qss_bar);
+        if (!warp_wait(qss_bar, 0, abort_flag, p.err, kErrWaitAcc)) return_early = true;
+        if (!return_early) {
+#pragma unroll 1
+        for (int j = 0; j < 4; ++j) {
+          const int col = 32 * h + 8 * j;
+          Quad8 v;
+          read_quadrants<kStrassen>(tmem_row, col, v);
+          const int slot = col / p.half_head;
+          const int cp = cp_base + col;
+#pragma unroll
+          for (int tb = 0; tb < 2; ++tb) {
+            const float sums = qss[qidx(0, tb, slot)] + qss[qidx(1, tb, slot)];
+            const float recip = 1.0f / sqrtf(sums * p.inv_head_dim + p.eps);
+            const int64_t row = tb ? row_bot : row_top;
+            float outa[8], outb[8];
+#pragma unroll
+            for (int e = 0; e < 8; ++e) {
+              const float sa = load_aux(p.rope_scale, cp + e, p.aux_f32);
+              const float sbv = load_aux(p.rope_scale, p.half_bn + cp + e, p.aux_f32);
+              const float cs = row_ok ? load_aux(p.rope_cos, row * p.ld_rope + cp + e, p.aux_f32) : 0.f;
+              const float sn = row_ok ? load_aux(p.rope_sin, row * p.ld_rope + cp + e, p.aux_f32) : 0.f;
+              const float na = v.c[2 * tb][e] * recip * sa;
+              const float nb = v.c[2 * tb + 1][e] * recip * sbv;
+              outa[e] = na * cs - nb * sn;
+              outb[e] = nb * cs + na * sn;
+            }
+            if (row_ok) {
+              store8<kOutF32>(p.C, row * p.ldc + col_left0 + col, outa);
+              store8<kOutF32>(p.C, row * p.ldc + col_left0 + p.half_bn + col, outb);
+            }
+          }
+        }
+        }
+      } else {
+#pragma unroll 1
+        for (int j = 0; j < 4; ++j) {
+          const int col = 32 * h + 8 * j;
+          Quad8 v;
+          read_quadrants<kStrassen>(tmem_row, col, v);
+          if (!row_ok) continue;
+          const int64_t cl = col_left0 + col;
+          const int64_t cr = cl + p.half_bn;
+          if constexpr (kEpi == SB_EPI_SWIGLU || kEpi == SB_EPI_GEGLU) {
+            // strassen_pallas.py:762-777: quadrants 0/2 gate, 1/3 up; output
+            // column J*bn/2 + c'.
+            float top[8], bot[8];
+#pragma unroll
+            for (int e = 0; e < 8; ++e) {
+              if constexpr (kEpi == SB_EPI_SWIGLU) {
+                top[e] = silu_f32(v.c[0][e]) * v.c[1][e];
+                bot[e] = silu_f32(v.c[2][e]) * v.c[3][e];
+              } else {
+                top[e] = gelu_tanh_f32(v.c[0][e]) * v.c[1][e];
+                bot[e] = gelu_tanh_f32(v.c[2][e]) * v.c[3][e];
+              }
+            }
+            const int64_t oc = (int64_t)j_block * p.half_bn + cp_base + col;
+            store8<kOutF32>(p.C, row_top * p.ldc + oc, top);
+            store8<kOutF32>(p.C, row_bot * p.ldc + oc, bot);
+          } else {
+            if constexpr (kEpi == SB_EPI_RESIDUAL_ADD) {
+              // strassen_pallas.py:778-792
+              float r[8];
+              load8(p.residual, row_top * p.ldr + cl, p.residual_f32, r);
+#pragma unroll
+              for (int e = 0; e < 8; ++e) v.c[0][e] += r[e];
+              load8(p.residual, row_top * p.ldr + cr, p.residual_f32, r);
+#pragma unroll
+              for (int e = 0; e < 8; ++e) v.c[1][e] += r[e];
+              load8(p.residual, row_bot * p.ldr + cl, p.residual_f32, r);
+#pragma unroll
+              for (int e = 0; e < 8; ++e) v.c[2][e] += r[e];
+              load8(p.residual, row_bot * p.ldr + cr, p.residual_f32, r);
+#pragma unroll
+              for (int e = 0; e < 8; ++e) v.c[3][e] += r[e];
+            } else if constexpr (kEpi == SB_EPI_BIAS_ADD) {
+              // strassen_pallas.py:867-874
+#pragma unroll
+              for (int e = 0; e < 8; ++e) {
+                const float bl = load_aux(p.bias, cl + e, p.aux_f32);
+                const float br = load_aux(p.bias, cr + e, p.aux_f32);
+                v.c[0][e] += bl;
+                v.c[2][e] += bl;
+                v.c[1][e] += br;
+                v.c[3][e] += br;
+              }
+            }
+            store8<kOutF32>(p.C, row_top * p.ldc + cl, v.c[0]);
+            store8<kOutF32>(p.C, row_top * p.ldc + cr, v.c[1]);
+            store8<kOutF32>(p.C, row_bot * p.ldc + cl, v.c[2]);
+            store8<kOutF32>(p.C, row_bot * p.ldc + cr, v.c[3]);
+          }
+        }
+      }
+    }
+  }
+
+  // ------------------------------------------------------------ teardown
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    if (lane == 0) mbar_wait_drain(acc_bar, 0);  // every issued MMA has retired
+    __syncwarp();
+    tmem_dealloc<kTmemCols>(tmem_base);
+  }
+}
+
+// Row pass of norm_residual_add (strassen_pallas.py:836-866): the GEMM has
+// written fp32 pre-norm rows to `x`; one CTA normalises one row:
+// out = bf16(x * rsqrt((sum(left^2) + sum(right^2)) / n + eps) * scale + residual).
+__global__ void __launch_bounds__(256) norm_residual_rows_kernel(
+    const float* __restrict__ x, int64_t n, const void* __restrict__ scale, int scale_f32,
+    const void* __restrict__ residual, int64_t ldr, int residual_f32, float eps,
+    __nv_bfloat16* __restrict__ out, int64_t ldo) {
+  const int64_t row = blockIdx.x;
+  const float* xr = x + row * n;
+  const int64_t half = n / 2;
+  float sl = 0.f, sr = 0.f;
+  for (int64_t i = threadIdx.x; i < half; i += blockDim.x) {
+    const float a = xr[i], b = xr[half + i];
+    sl += a * a;
+    sr += b * b;
+  }
+  __shared__ float red[2][32];
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    sl += __shfl_xor_sync(0xffffffffu, sl, o);
+    sr += __shfl_xor_sync(0xffffffffu, sr, o);
+  }
+  const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+  if (l == 0) {
+    red[0][w] = sl;
+    red[1][w] = sr;
+  }
+  __syncthreads();
+  if (w == 0) {
+    const int nw = blockDim.x >> 5;
+    sl = l < nw ? red[0][l] : 0.f;
+    sr = l < nw ? red[1][l] : 0.f;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      sl += __shfl_xor_sync(0xffffffffu, sl, o);
+      sr += __shfl_xor_sync(0xffffffffu, sr, o);
+    }
+    if (l == 0) {
+      red[0][0] = sl;
+      red[1][0] = sr;
+    }
+  }
+  __syncthreads();
+  const float squares = red[0][0] + red[1][0];
+  const float recip = 1.0f / sqrtf(squares * (1.0f / (float)n) + eps);
+  for (int64_t i = threadIdx.x; i < n; i += blockDim.x) {
+    const float s = scale_f32 ? reinterpret_cast<const float*>(scale)[i]
+                              : __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(scale)[i]);
+    const float r = residual_f32
+                        ? reinterpret_cast<const float*>(residual)[row * ldr + i]
+                        : __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(residual)[row * ldr + i]);
+    out[row * ldo + i] = __float2bfloat16_rn(xr[i] * recip * s + r);
+  }
+}
+
+// Standalone RMSNorm (experiments/qwen3/benchmark_qwen3_32b_layer.py:270-276):
+// y = bf16(x * rsqrt(mean(x^2) + eps) * w), fp32 math.  One CTA per row,
+// 16-byte vector loads.
+__global__ void __launch_bounds__(256) rms_norm_kernel(const __nv_bfloat16* __restrict__ x,
+                                                       const void* __restrict__ w, int w_f32,
+                                                       __nv_bfloat16* __restrict__ y, int64_t n,
+                                                       float eps) {
+  const int64_t row = blockIdx.x;
+  const __nv_bfloat16* xr = x + row * n;
+  float ss = 0.f;
+  const int64_t nvec = n / 8;
+  for (int64_t v = threadIdx.x; v < nvec; v += blockDim.x) {
+    uint4 u = reinterpret_cast<const uint4*>(xr)[v];
+    const __nv_bfloat162* hp = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      float2 f = __bfloat1622float2(hp[i]);
+      ss += f.x * f.x + f.y * f.y;
+    }
+  }
+  __shared__ float red[32];
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+  const int wi = threadIdx.x >> 5, l = threadIdx.x & 31;
+  if (l == 0) red[wi] = ss;
+  __syncthreads();
+  if (wi == 0) {
+    ss = l < (int)(blockDim.x >> 5) ? red[l] : 0.f;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    if (l == 0) red[0] = ss;
+  }
+  __syncthreads();
+  const float recip = 1.0f / sqrtf(red[0] / (float)n + eps);
+  for (int64_t v = threadIdx.x; v < nvec; v += blockDim.x) {
+    uint4 u = reinterpret_cast<const uint4*>(xr)[v];
+    const __nv_bfloat162* hp = reinterpret_cast<const __nv_bfloat162*>(&u);
+    float o[8];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      float2 f = __bfloat1622float2(hp[i]);
+      o[2 * i] = f.x;
+      o[2 * i + 1] = f.y;
+    }
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int64_t c = v * 8 + i;
+      const float wv = w_f32 ? reinterpret_cast<const float*>(w)[c]
+                             : __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(w)[c]);
+      o[i] = (o[i] * recip) * wv;
+    }
+    uint4 r = make_uint4(pack_bf16x2(o[0], o[1]), pack_bf16x2(o[2], o[3]), pack_bf16x2(o[4], o[5]),
+                         pack_bf16x2(o[6], o[7]));
+    reinterpret_cast<uint4*>(y + row * n)[v] = r;
+  }
+}
+
+// ====================================================================== host
+namespace {
+
+thread_local std::string t_last_error;
+
+int fail(int status, const std::string& msg) {
+  t_last_error = msg;
+  return status;
+}
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                   const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                   const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = []() -> EncodeTiledFn {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) !=
+            cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      return nullptr;
+    return reinterpret_cast<EncodeTiledFn>(ptr);
+  }();
+  return fn;
+}
+
+bool is_pow2(int64_t v) { return v > 0 && (v & (v - 1)) == 0; }
+bool aligned16(const void* ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15u) == 0; }
+
+template <bool kStrassen, int kEpi, bool kOutF32>
+int launch_typed(cudaStream_t stream, const CUtensorMap& ta, const CUtensorMap& tb,
+                 const GemmParams& p) {
+  auto kernel = strassen_gemm_kernel<kStrassen, kEpi, kOutF32>;
+  static std::once_flag once;
+  static cudaError_t attr_err = cudaSuccess;
+  std::call_once(once, [&]() {
+    attr_err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+  });
+  if (attr_err != cudaSuccess)
+    return fail(SB_ERR_CUDA, std::string("cudaFuncSetAttribute: ") + cudaGetErrorString(attr_err));
+  const unsigned grid = (unsigned)(p.tiles_m * p.tiles_n);
+  kernel<<<grid, kThreads, kSmemBytes, stream>>>(ta, tb, p);
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return fail(SB_ERR_CUDA, std::string("kernel launch: ") + cudaGetErrorString(e));
+  return SB_OK;
+}
+
+int dispatch(bool strassen, int epi, bool out_f32, cudaStream_t stream, const CUtensorMap& ta,
+             const CUtensorMap& tb, const GemmParams& p) {
+  if (!strassen) {
+    return out_f32 ? launch_typed<false, SB_EPI_NONE, true>(stream, ta, tb, p)
+                   : launch_typed<false, SB_EPI_NONE, false>(stream, ta, tb, p);
+  }
+  switch (epi) {
+    case SB_EPI_NONE:
+      return out_f32 ? launch_typed<true, SB_EPI_NONE, true>(stream, ta, tb, p)
+                     : launch_typed<true, SB_EPI_NONE, false>(stream, ta, tb, p);
+    case SB_EPI_SWIGLU: return launch_typed<true, SB_EPI_SWIGLU, false>(stream, ta, tb, p);
+    case SB_EPI_GEGLU: return launch_typed<true, SB_EPI_GEGLU, false>(stream, ta, tb, p);
+    case SB_EPI_RESIDUAL_ADD: return launch_typed<true, SB_EPI_RESIDUAL_ADD, false>(stream, ta, tb, p);
+    case SB_EPI_BIAS_ADD: return launch_typed<true, SB_EPI_BIAS_ADD, false>(stream, ta, tb, p);
+    case SB_EPI_QK_NORM_ROPE: return launch_typed<true, SB_EPI_QK_NORM_ROPE, false>(stream, ta, tb, p);
+    default: return fail(SB_ERR_EPILOGUE, "unknown epilogue kind");
+  }
+}
+
+int check_device() {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return fail(SB_ERR_CUDA, std::string("cudaGetDevice: ") + cudaGetErrorString(e));
+  static int cached_major[64];
+  static int cached_minor[64];
+  static std::once_flag flags[64];
+  if (dev < 0 || dev >= 64) return fail(SB_ERR_DEVICE, "device ordinal out of range");
+  std::call_once(flags[dev], [&]() {
+    cudaDeviceGetAttribute(&cached_major[dev], cudaDevAttrComputeCapabilityMajor, dev);
+    cudaDeviceGetAttribute(&cached_minor[dev], cudaDevAttrComputeCapabilityMinor, dev);
+  });
+  if (cached_major[dev] != 10 || cached_minor[dev] != 0)
+    return fail(SB_ERR_DEVICE, "the Strassen kernel is built for sm_100a (B200); device is sm_" +
+                                   std::to_string(cached_major[dev]) + std::to_string(cached_minor[dev]));
+  return SB_OK;
+}
+
+// Validation shared by the Strassen and classical entry points; mirrors the
+// reference's host-side checks (strassen_pallas.py:927-1047, :127-140).
+int validate_core(const void* a, const void* b, const void* c, int64_t m, int64_t n, int64_t k,
+                  int64_t lda, int64_t ldb, int64_t ldc, int32_t bm, int32_t bn, int32_t bk,
+                  int32_t out_dtype) {
+  if (!a || !b || !c) return fail(SB_ERR_RANK, "null matrix pointer");
+  if (m <= 0 || n <= 0 || k <= 0) return fail(SB_ERR_RANK, "matrix dimensions must be positive");
+  if (bm <= 0 || bn <= 0 || bk <= 0) return fail(SB_ERR_TILING, "tile sizes must be positive");
+  const char* names[3] = {"M", "N", "K"};
+  const int64_t dims[3] = {m, n, k};
+  const int32_t blocks[3] = {bm, bn, bk};
+  for (int i = 0; i < 3; ++i) {
+    if (dims[i] % blocks[i])
+      return fail(SB_ERR_DIVISIBILITY, std::string(names[i]) + "=" + std::to_string(dims[i]) +
+                                           " is not divisible by " + std::to_string(blocks[i]));
+  }
+  std::string tiling;
+  if (bm % 16) tiling += "\n  bm=" + std::to_string(bm) + " must be a multiple of 16";
+  if (bn % 256) tiling += "\n  bn=" + std::to_string(bn) + " must be a multiple of 256";
+  if (bk % 256) tiling += "\n  bk=" + std::to_string(bk) + " must be a multiple of 256";
+  if (!tiling.empty()) return fail(SB_ERR_TILING, "tile breaks TPU v5e alignment:" + tiling);
+  if (out_dtype != SB_BF16 && out_dtype != SB_F32)
+    return fail(SB_ERR_OUTPUT_DTYPE, "output_dtype must be BF16 or FP32");
+  const int half_bm = bm / 2;
+  if (!(half_bm % kBlockM == 0 || (is_pow2(half_bm) && half_bm < kBlockM)))
+    return fail(SB_ERR_UNSUPPORTED,
+                "bm=" + std::to_string(bm) +
+                    ": the B200 kernel needs bm/2 to be a multiple of 128 or a power of two below 128");
+  if (m > (int64_t)INT32_MAX || n > (int64_t)INT32_MAX || k > (int64_t)INT32_MAX)
+    return fail(SB_ERR_UNSUPPORTED, "dimensions above 2^31-1 are not supported");
+  if (!aligned16(a) || !aligned16(b) || !aligned16(c))
+    return fail(SB_ERR_ALIGNMENT, "A, B and C must be 16-byte aligned");
+  if (lda % 8 || ldb % 8 || ldc % 8 || lda < k || ldb < n)
+    return fail(SB_ERR_ALIGNMENT,
+                "leading dimensions must be multiples of 8 elements and cover the rows");
+  return SB_OK;
+}
+
+int make_maps(const void* a, const void* b, int64_t m, int64_t n, int64_t k, int64_t lda,
+              int64_t ldb, int32_t bm, CUtensorMap* ta, CUtensorMap* tb) {
+  EncodeTiledFn enc = encode_fn();
+  if (!enc) return fail(SB_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
+  const int half_bm = bm / 2;
+  const uint32_t rows = half_bm >= kBlockM ? kBlockM : half_bm;
+  const uint32_t blocks = half_bm >= kBlockM ? 1 : kBlockM / half_bm;
+  {
+    // A viewed as [M/bm][bm][K]; a box is BLOCK_K columns of `rows` rows in each
+    // of `blocks` consecutive Strassen blocks = one 128-row product tile.
+    cuuint64_t dims[3] = {(cuuint64_t)k, (cuuint64_t)bm, (cuuint64_t)(m / bm)};
+    cuuint64_t strides[2] = {(cuuint64_t)lda * 2, (cuuint64_t)lda * 2 * bm};
+    cuuint32_t box[3] = {(cuuint32_t)kBlockK, rows, blocks};
+    cuuint32_t estr[3] = {1, 1, 1};
+    CUresult r = enc(ta, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(a), dims, strides, box,
+                     estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B,
+                     CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(SB_ERR_CUDA, "cuTensorMapEncodeTiled(A) failed: " + std::to_string((int)r));
+  }
+  {
+    cuuint64_t dims[2] = {(cuuint64_t)n, (cuuint64_t)k};
+    cuuint64_t strides[1] = {(cuuint64_t)ldb * 2};
+    cuuint32_t box[2] = {(cuuint32_t)kBlockN, (cuuint32_t)kBlockK};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = enc(tb, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(b), dims, strides, box,
+                     estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                     CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(SB_ERR_CUDA, "cuTensorMapEncodeTiled(B) failed: " + std::to_string((int)r));
+  }
+  return SB_OK;
+}
+
+GemmParams base_params(int64_t m, int64_t n, int64_t k, int32_t bm, int32_t bn, int32_t bk, void* c,
+                       int64_t ldc) {
+  GemmParams p;
+  std::memset(&p, 0, sizeof(p));
+  p.M = (int32_t)m;
+  p.N = (int32_t)n;
+  p.K = (int32_t)k;
+  p.bm = bm;
+  p.bn = bn;
+  p.bk = bk;
+  p.half_bm = bm / 2;
+  p.half_bn = bn / 2;
+  p.half_bk = bk / 2;
+  p.Mp = (int32_t)(m / 2);
+  p.Np = (int32_t)(n / 2);
+  p.num_chunks = (int32_t)(k / 2 / kBlockK);
+  p.tiles_m = (p.Mp + kBlockM - 1) / kBlockM;
+  p.tiles_n = p.Np / kBlockN;
+  p.C = c;
+  p.ldc = ldc;
+  p.eps = 1e-6f;
+  p.half_head = 64;
+  p.inv_head_dim = 1.0f / 128.0f;
+  int* err = nullptr;
+  cudaGetSymbolAddress(reinterpret_cast<void**>(&err), g_device_error);
+  p.err = err;
+  return p;
+}
+
+}  // namespace
+}  // namespace sb
+
+using namespace sb;
+
+extern "C" {
+
+size_t sb_workspace_bytes(int64_t m, int64_t n, int64_t k, int32_t epilogue_kind) {
+  (void)k;
+  if (epilogue_kind == SB_EPI_NORM_RESIDUAL_ADD && m > 0 && n > 0) return (size_t)m * (size_t)n * 4u;
+  return 0;
+}
+
+int sb_strassen_gemm(sb_stream_t stream_, const void* a, const void* b, void* c, int64_t m,
+                     int64_t n, int64_t k, int64_t lda, int64_t ldb, int64_t ldc, int32_t bm,
+                     int32_t bn, int32_t bk, int32_t out_dtype, const sb_epilogue* ep,
+                     void* workspace, size_t workspace_bytes) {
+  cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_);
+  const int epi = ep ? ep->kind : SB_EPI_NONE;
+  int st = validate_core(a, b, c, m, n, k, lda, ldb, ldc, bm, bn, bk, out_dtype);
+  if (st != SB_OK) return st;
+  if (epi < SB_EPI_NONE || epi > SB_EPI_NORM_RESIDUAL_ADD)
+    return fail(SB_ERR_EPILOGUE, "unknown epilogue kind " + std::to_string(epi));
+  if (epi != SB_EPI_NONE && out_dtype != SB_BF16)
+    return fail(SB_ERR_OUTPUT_DTYPE, "fused epilogues write a BF16 output tile");
+  if ((epi == SB_EPI_SWIGLU || epi == SB_EPI_GEGLU) && (bn % 2))
+    return fail(SB_ERR_EPILOGUE, "gated epilogue needs an even bn");
+  if ((epi == SB_EPI_RESIDUAL_ADD || epi == SB_EPI_NORM_RESIDUAL_ADD) &&
+      (!ep->residual || !aligned16(ep->residual) || ep->ld_residual % 8 || ep->ld_residual < n))
+    return fail(SB_ERR_EPILOGUE, "residual must be a 16-byte aligned [M, N] array with ld % 8 == 0");
+  if (epi == SB_EPI_BIAS_ADD && !ep->bias) return fail(SB_ERR_EPILOGUE, "bias_add epilogue requires bias=");
+  if (epi == SB_EPI_NORM_RESIDUAL_ADD) {
+    if (!ep->norm_scale) return fail(SB_ERR_EPILOGUE, "norm_residual_add requires residual= and norm_scale=");
+    if (bn != n)
+      return fail(SB_ERR_EPILOGUE, "norm_residual_add normalises over the whole output row, so the tile must "
+                                   "span it: bn=" + std::to_string(bn) + " must equal n=" + std::to_string(n));
+    if (!workspace || workspace_bytes < sb_workspace_bytes(m, n, k, epi) || !aligned16(workspace))
+      return fail(SB_ERR_WORKSPACE, "norm_residual_add needs a 16-byte aligned workspace of " +
+                                        std::to_string(sb_workspace_bytes(m, n, k, epi)) + " bytes");
+  }
+  if (epi == SB_EPI_QK_NORM_ROPE) {
+    if (!ep->rope_cos || !ep->rope_sin || !ep->rope_scale)
+      return fail(SB_ERR_EPILOGUE, "qk_norm_rope epilogue requires rope_cos=, rope_sin= and rope_scale= "
+                                   "(use rope_layout_tables and rope_scale_layout)");
+    const int hd = ep->rope_head_dim;
+    if (hd <= 0 || bn % (2 * hd))
+      return fail(SB_ERR_EPILOGUE, "qk_norm_rope needs bn a multiple of 2*head_dim=" + std::to_string(2 * hd) +
+                                       " so a tile half holds whole heads, got bn=" + std::to_string(bn));
+    if (!(hd / 2 == 8 || hd / 2 == 16 || hd / 2 == 32 || hd / 2 == 64))
+      return fail(SB_ERR_UNSUPPORTED, "qk_norm_rope on B200 supports head_dim in {16, 32, 64, 128}");
+    if (ep->ld_rope < bn / 2) return fail(SB_ERR_EPILOGUE, "rope tables must have bn/2 columns");
+  }
+  if (epi == SB_EPI_SWIGLU || epi == SB_EPI_GEGLU) {
+    if (ldc < n / 2 || ldc % 8) return fail(SB_ERR_ALIGNMENT, "swiglu output leading dimension must be >= N/2 and a multiple of 8");
+  } else if (ldc < n) {
+    return fail(SB_ERR_ALIGNMENT, "ldc must be >= N");
+  }
+  st = check_device();
+  if (st != SB_OK) return st;
+
+  CUtensorMap ta, tb;
+  st = make_maps(a, b, m, n, k, lda, ldb, bm, &ta, &tb);
+  if (st != SB_OK) return st;
+
+  if (epi == SB_EPI_NORM_RESIDUAL_ADD) {
+    // Pass 1: fp32 pre-norm rows into the caller's workspace; pass 2: row norm.
+    GemmParams p = base_params(m, n, k, bm, bn, bk, workspace, n);
+    st = dispatch(true, SB_EPI_NONE, true, stream, ta, tb, p);
+    if (st != SB_OK) return st;
+    norm_residual_rows_kernel<<<(unsigned)m, 256, 0, stream>>>(
+        reinterpret_cast<const float*>(workspace), n, ep->norm_scale, ep->aux_dtype == SB_F32,
+        ep->residual, ep->ld_residual, ep->residual_dtype == SB_F32, ep->norm_eps,
+        reinterpret_cast<__nv_bfloat16*>(c), ldc);
+    const cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return fail(SB_ERR_CUDA, std::string("norm rows launch: ") + cudaGetErrorString(e));
+    return SB_OK;
+  }
+
+  GemmParams p = base_params(m, n, k, bm, bn, bk, c, ldc);
+  if (ep) {
+    p.residual = ep->residual;
+    p.ldr = ep->ld_residual;
+    p.residual_f32 = ep->residual_dtype == SB_F32;
+    p.aux_f32 = ep->aux_dtype == SB_F32;
+    p.bias = ep->bias;
+    p.rope_cos = ep->rope_cos;
+    p.rope_sin = ep->rope_sin;
+    p.ld_rope = ep->ld_rope;
+    p.rope_scale = ep->rope_scale;
+    if (epi == SB_EPI_QK_NORM_ROPE) {
+      p.half_head = ep->rope_head_dim / 2;
+      p.inv_head_dim = 1.0f / (float)ep->rope_head_dim;
+      p.eps = ep->rope_eps;
+    }
+  }
+  return dispatch(true, epi, out_dtype == SB_F32, stream, ta, tb, p);
+}
+
+int sb_classical_gemm(sb_stream_t stream_, const void* a, const void* b, void* c, int64_t m,
+                      int64_t n, int64_t k, int64_t lda, int64_t ldb, int64_t ldc, int32_t bm,
+                      int32_t bn, int32_t bk, int32_t out_dtype) {
+  cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_);
+  int st = validate_core(a, b, c, m, n, k, lda, ldb, ldc, bm, bn, bk, out_dtype);
+  if (st != SB_OK) return st;
+  if (ldc < n) return fail(SB_ERR_ALIGNMENT, "ldc must be >= N");
+  st = check_device();
+  if (st != SB_OK) return st;
+  CUtensorMap ta, tb;
+  st = make_maps(a, b, m, n, k, lda, ldb, bm, &ta, &tb);
+  if (st != SB_OK) return st;
+  GemmParams p = base_params(m, n, k, bm, bn, bk, c, ldc);
+  return dispatch(false, SB_EPI_NONE, out_dtype == SB_F32, stream, ta, tb, p);
+}
+
+int sb_rms_norm(sb_stream_t stream_, const void* x, const void* w, void* y, int64_t rows, int64_t n,
+                int32_t w_dtype, float eps) {
+  cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_);
+  if (!x || !w || !y) return fail(SB_ERR_RANK, "null pointer");
+  if (rows <= 0 || n <= 0) return fail(SB_ERR_RANK, "rows and n must be positive");
+  if (n % 8 || !aligned16(x) || !aligned16(y))
+    return fail(SB_ERR_ALIGNMENT, "rms_norm needs n % 8 == 0 and 16-byte aligned rows");
+  if (rows > (int64_t)INT32_MAX) return fail(SB_ERR_UNSUPPORTED, "too many rows");
+  rms_norm_kernel<<<(unsigned)rows, 256, 0, stream>>>(reinterpret_cast<const __nv_bfloat16*>(x), w,
+                                                      w_dtype == SB_F32,
+                                                      reinterpret_cast<__nv_bfloat16*>(y), n, eps);
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return fail(SB_ERR_CUDA, std::string("rms_norm launch: ") + cudaGetErrorString(e));
+  return SB_OK;
+}
+
+void sb_query_tile(int32_t* block_m, int32_t* block_n, int32_t* block_k) {
+  if (block_m) *block_m = kBlockM;
+  if (block_n) *block_n = kBlockN;
+  if (block_k) *block_k = kBlockK;
+}
+
+const char* sb_status_string(int32_t status) {
+  switch (status) {
+    case SB_OK: return "ok";
+    case SB_ERR_RANK: return "bad rank or shape";
+    case SB_ERR_INNER_DIM: return "inner dimensions disagree";
+    case SB_ERR_DTYPE: return "unsupported input dtype";
+    case SB_ERR_DIVISIBILITY: return "dimension not divisible by tile";
+    case SB_ERR_TILING: return "tile breaks alignment";
+    case SB_ERR_EPILOGUE: return "epilogue argument error";
+    case SB_ERR_OUTPUT_DTYPE: return "unsupported output dtype";
+    case SB_ERR_UNSUPPORTED: return "not supported by the B200 kernel";
+    case SB_ERR_ALIGNMENT: return "pointer or leading-dimension alignment";
+    case SB_ERR_WORKSPACE: return "workspace missing or too small";
+    case SB_ERR_CUDA: return "CUDA runtime error";
+    case SB_ERR_DEVICE: return "device is not an sm_100 B200";
+    case SB_ERR_DEVICE_TIMEOUT: return "bounded device wait timed out";
+    default: return "unknown status";
+  }
+}
+
+const char* sb_last_error_message(void) { return t_last_error.c_str(); }
+
+int sb_device_status(int32_t* device_error, int32_t reset) {
+  cudaError_t e = cudaDeviceSynchronize();
+  if (e != cudaSuccess) return fail(SB_ERR_CUDA, std::string("cudaDeviceSynchronize: ") + cudaGetErrorString(e));
+  int v = 0;
+  e = cudaMemcpyFromSymbol(&v, g_device_error, sizeof(int));
+  if (e != cudaSuccess) return fail(SB_ERR_CUDA, std::string("cudaMemcpyFromSymbol: ") + cudaGetErrorString(e));
+  if (device_error) *device_error = v;
+  if (reset) {
+    const int zero = 0;
+    e = cudaMemcpyToSymbol(g_device_error, &zero, sizeof(int));
+    if (e != cudaSuccess) return fail(SB_ERR_CUDA, std::string("cudaMemcpyToSymbol: ") + cudaGetErrorString(e));
+  }
+  return v ? SB_ERR_DEVICE_TIMEOUT : SB_OK;
+}
+
+const char* sb_version(void) { return "strassen_b200 0.1.0 (sm_100a, tcgen05)"; }
+
+}  // extern "C"

@@ -1,0 +1,367 @@
+"""The ``strassen_matmul`` operator API, backed by the sm_100a kernel.
+
+Same entry points, argument names, argument meaning and error behaviour as the
+reference module ``strassen_pallas`` (strassen_pallas.py:127-140, 882-1221,
+1414-1421): validation raises ``ValueError``/``TypeError`` on the host with the
+reference's messages before anything is launched.  Arguments that only steer
+the TPU compiler (``dot_precision``, ``allow_input_fusion``,
+``vmem_limit_bytes``, ``interleave_products``, ``product_aware_*``) are
+accepted and validated but do not change the B200 arithmetic, which keeps the
+seven products in separate fp32 TMEM accumulators over the whole K range and
+recombines them once.  ``bm``/``bn``/``bk`` keep their reference meaning: they
+define the Strassen block whose quadrants are paired, so results follow the
+reference's pairing of operands.
+
+Tensors are ``torch.Tensor`` on a CUDA B200 device.  There is no CPU path:
+``interpret=True`` and CPU tensors raise.
+"""
+
+from __future__ import annotations
+
+import ctypes
+
+import torch
+
+from . import _native
+from ._native import SB_BF16, SB_F32, EPILOGUE_KINDS, SbEpilogue
+
+LANE = 128
+SUBLANE = 8
+# The reference's default deployment tile (strassen_pallas.py:20-25, "compact16").
+TUNED_BM, TUNED_BN, TUNED_BK = 1024, 1024, 512
+
+_EPILOGUES = ("swiglu", "geglu", "residual_add", "bias_add", "qk_norm_rope", "norm_residual_add")
+
+
+def check_tiling(bm: int, bn: int, bk: int) -> None:
+    """Validate tile alignment after the one-level split (strassen_pallas.py:127-140)."""
+    requirements = (("bm", bm, 2 * SUBLANE), ("bn", bn, 2 * LANE), ("bk", bk, 2 * LANE))
+    errors = [f"{name}={value} must be a multiple of {multiple}"
+              for name, value, multiple in requirements if value % multiple]
+    if errors:
+        raise ValueError("tile breaks TPU v5e alignment:\n  " + "\n  ".join(errors))
+
+
+def _dtype_name(dt) -> str:
+    return str(dt).replace("torch.", "")
+
+
+def _as_torch_dtype(dt):
+    if dt is None:
+        return None
+    if isinstance(dt, torch.dtype):
+        return dt
+    name = str(getattr(dt, "name", dt)).lower()
+    table = {"bfloat16": torch.bfloat16, "bf16": torch.bfloat16,
+             "float32": torch.float32, "f32": torch.float32, "fp32": torch.float32}
+    if name in table:
+        return table[name]
+    raise ValueError("output_dtype must be BF16 or FP32")
+
+
+def _ld(t: torch.Tensor) -> int:
+    return t.stride(0)
+
+
+def _rowmajor(t: torch.Tensor) -> torch.Tensor:
+    if t.dim() == 2 and t.stride(1) == 1 and t.stride(0) >= t.shape[1] and t.stride(0) % 8 == 0 \
+            and t.data_ptr() % 16 == 0:
+        return t
+    return t.contiguous()
+
+
+def _stream_handle(device: torch.device) -> ctypes.c_void_p:
+    return ctypes.c_void_p(torch.cuda.current_stream(device).cuda_stream)
+
+
+def strassen_matmul(
+    a,
+    b,
+    *,
+    bm=TUNED_BM,
+    bn=TUNED_BN,
+    bk=TUNED_BK,
+    dot_precision=None,
+    interleave_products=False,
+    block_permutation=0,
+    formula_variant="classical",
+    classical_panels=(),
+    panel_schedule=None,
+    epilogue=None,
+    residual=None,
+    bias=None,
+    rope_cos=None,
+    rope_sin=None,
+    rope_scale=None,
+    rope_head_dim=128,
+    rope_eps=1e-6,
+    norm_scale=None,
+    norm_eps=1e-6,
+    output_dtype=None,
+    allow_input_fusion=None,
+    product_aware_swiglu=False,
+    product_aware_residual=False,
+    interpret=False,
+    vmem_limit_bytes=None,
+    out=None,
+    workspace=None,
+):
+    """Compute ``a @ b`` with one tile-local classical Strassen level on B200.
+
+    Mirrors strassen_pallas.strassen_matmul (strassen_pallas.py:882-1221).
+    Extra keyword arguments: ``out`` (a preallocated output tensor) and
+    ``workspace`` (a caller-owned uint8 CUDA buffer of at least
+    :func:`workspace_bytes` bytes; allocated from torch's caching allocator
+    when omitted).
+    """
+    # --- the reference's validation, in its order (strassen_pallas.py:927-1047)
+    if a.ndim != 2 or b.ndim != 2:
+        raise ValueError("strassen_matmul expects two rank-2 matrices")
+    m, k = a.shape
+    k2, n = b.shape
+    if k != k2:
+        raise ValueError(f"inner dimensions disagree: {k} vs {k2}")
+    if a.dtype != b.dtype:
+        raise ValueError(f"input dtypes disagree: {_dtype_name(a.dtype)} vs {_dtype_name(b.dtype)}")
+    if a.dtype not in (torch.bfloat16, torch.float32):
+        raise ValueError("inputs must be BF16 or FP32")
+    if not isinstance(block_permutation, int) or not 0 <= block_permutation < 8:
+        raise ValueError("block_permutation must be an integer from 0 through 7")
+    if formula_variant not in ("classical", "dual", "powers"):
+        raise ValueError("formula_variant must be 'classical', 'dual', or 'powers'")
+    classical_panels = tuple(sorted({int(p) for p in classical_panels}))
+    out_dt = _as_torch_dtype(output_dtype)
+    if epilogue is not None:
+        if epilogue not in _EPILOGUES:
+            raise ValueError(
+                f"unknown epilogue {epilogue!r}; choose 'swiglu' or 'residual_add' or 'bias_add'")
+        if formula_variant == "powers":
+            raise ValueError("fused epilogues require a quadrant-basis formula")
+        if out_dt is not None and out_dt != torch.bfloat16:
+            raise ValueError("fused epilogues write a BF16 output tile")
+        if epilogue in ("swiglu", "geglu") and bn % 2:
+            raise ValueError(f"{epilogue} epilogue needs an even bn, got {bn}")
+        if epilogue == "residual_add" and residual is None:
+            raise ValueError("residual_add epilogue requires residual=")
+        if epilogue == "bias_add" and bias is None:
+            raise ValueError("bias_add epilogue requires bias=")
+    if residual is not None and epilogue not in ("residual_add", "norm_residual_add"):
+        raise ValueError("residual= is only used by the residual_add and norm_residual_add epilogues")
+    if bias is not None and epilogue != "bias_add":
+        raise ValueError("bias= is only used by the bias_add epilogue")
+    if epilogue == "norm_residual_add":
+        if residual is None or norm_scale is None:
+            raise ValueError("norm_residual_add requires residual= and norm_scale=")
+        if bn != n:
+            raise ValueError(
+                "norm_residual_add normalises over the whole output row, so "
+                f"the tile must span it: bn={bn} must equal n={n}")
+        if tuple(residual.shape) != (m, n):
+            raise ValueError(f"residual shape {tuple(residual.shape)} != output {(m, n)}")
+        if tuple(norm_scale.shape) != (n,):
+            raise ValueError(f"norm_scale shape {tuple(norm_scale.shape)} != output width {(n,)}")
+    if epilogue == "qk_norm_rope":
+        if rope_cos is None or rope_sin is None or rope_scale is None:
+            raise ValueError(
+                "qk_norm_rope epilogue requires rope_cos=, rope_sin= and "
+                "rope_scale= (use rope_layout_tables and rope_scale_layout)")
+        if bn % (2 * rope_head_dim):
+            raise ValueError(
+                f"qk_norm_rope needs bn a multiple of 2*head_dim={2 * rope_head_dim} so a "
+                f"tile half holds whole heads, got bn={bn}")
+        if tuple(rope_cos.shape) != (m, bn // 2) or tuple(rope_sin.shape) != (m, bn // 2):
+            raise ValueError(
+                f"rope tables must be {(m, bn // 2)}, got "
+                f"{tuple(rope_cos.shape)} and {tuple(rope_sin.shape)}")
+        if tuple(rope_scale.shape) != (bn,):
+            raise ValueError(f"rope_scale must be laid out to {(bn,)}, got {tuple(rope_scale.shape)}")
+    if rope_cos is not None and epilogue != "qk_norm_rope":
+        raise ValueError("rope_* are only used by the qk_norm_rope epilogue")
+    if product_aware_swiglu and epilogue not in ("swiglu", "geglu"):
+        raise ValueError("product_aware_swiglu is only valid with epilogue='swiglu' or 'geglu'")
+    if product_aware_residual and epilogue != "residual_add":
+        raise ValueError("product_aware_residual is only valid with epilogue='residual_add'")
+    if epilogue == "bias_add" and tuple(bias.shape) != (n,):
+        raise ValueError(f"bias shape {tuple(bias.shape)} != output width {(n,)}")
+    operand_count = 3 if epilogue in ("residual_add", "bias_add") else 2
+    if epilogue == "norm_residual_add":
+        operand_count = 4
+    if epilogue == "qk_norm_rope":
+        operand_count = 6
+    if allow_input_fusion is not None:
+        allow_input_fusion = tuple(allow_input_fusion)
+        if len(allow_input_fusion) != operand_count:
+            raise ValueError(
+                "allow_input_fusion must contain one boolean per operand: "
+                f"expected {operand_count}, got {len(allow_input_fusion)}")
+        if not all(isinstance(value, bool) for value in allow_input_fusion):
+            raise TypeError("allow_input_fusion entries must be bool")
+    if panel_schedule is not None and classical_panels:
+        raise ValueError("pass either classical_panels (static) or panel_schedule (prefetched), not both")
+    if classical_panels:
+        if formula_variant == "powers":
+            raise ValueError("classical_panels requires a quadrant-basis formula")
+        if classical_panels[0] < 0 or classical_panels[-1] >= k // bk:
+            raise ValueError(f"classical_panels {classical_panels} outside 0..{k // bk - 1}")
+    for name, dimension, block in (("M", m, bm), ("N", n, bn), ("K", k, bk)):
+        if dimension % block:
+            raise ValueError(f"{name}={dimension} is not divisible by {block}")
+    check_tiling(bm, bn, bk)
+    out_dt = a.dtype if out_dt is None else out_dt
+    if out_dt not in (torch.bfloat16, torch.float32):
+        raise ValueError("output_dtype must be BF16 or FP32")
+    if panel_schedule is not None and epilogue is not None:
+        raise ValueError("panel_schedule does not support fused epilogues")
+    if residual is not None and epilogue == "residual_add" and tuple(residual.shape) != (m, n):
+        raise ValueError(f"residual shape {tuple(residual.shape)} != output shape {(m, n)}")
+
+    # --- what the B200 build does not implement (yet): refuse loudly.
+    if interpret:
+        raise NotImplementedError(
+            "interpret=True: the B200 build has no CPU path; the CPU restatement lives in "
+            "oracle/ and is test infrastructure only")
+    if a.dtype != torch.bfloat16:
+        raise NotImplementedError("the B200 kernel computes bf16 inputs; FP32 inputs are not built")
+    if formula_variant != "classical" or block_permutation != 0:
+        raise NotImplementedError(
+            "formula_variant/block_permutation research options are not built for B200")
+    if classical_panels or panel_schedule is not None:
+        raise NotImplementedError("exact classical K panels are not built for B200")
+    if not (a.is_cuda and b.is_cuda):
+        raise ValueError("strassen_matmul runs on a CUDA device; got CPU tensors (no CPU fallback)")
+
+    device = a.device
+    a = _rowmajor(a)
+    b = _rowmajor(b.to(device))
+    gated = epilogue in ("swiglu", "geglu")
+    out_shape = (m, n // 2) if gated else (m, n)
+    if out is None:
+        out = torch.empty(out_shape, dtype=out_dt, device=device)
+    else:
+        if tuple(out.shape) != out_shape or out.dtype != out_dt or out.device != device:
+            raise ValueError(f"out must be a {out_shape} {_dtype_name(out_dt)} tensor on {device}")
+        if out.stride(1) != 1 or out.stride(0) % 8 or out.data_ptr() % 16:
+            raise ValueError("out must be row-major with a 16-byte aligned row stride")
+
+    ep = SbEpilogue()
+    ep.kind = EPILOGUE_KINDS[epilogue]
+    keep_alive = []
+    aux = [t for t in (bias, rope_cos, rope_sin, rope_scale, norm_scale) if t is not None]
+    aux_dt = torch.float32 if any(t.dtype == torch.float32 for t in aux) else torch.bfloat16
+    ep.aux_dtype = SB_F32 if aux_dt == torch.float32 else SB_BF16
+
+    def prep_aux(t):
+        t = t.to(device=device, dtype=aux_dt).contiguous()
+        keep_alive.append(t)
+        return t
+
+    if residual is not None:
+        r = residual.to(device)
+        if r.dtype not in (torch.bfloat16, torch.float32):
+            r = r.float()
+        r = _rowmajor(r)
+        keep_alive.append(r)
+        ep.residual = r.data_ptr()
+        ep.ld_residual = _ld(r)
+        ep.residual_dtype = SB_F32 if r.dtype == torch.float32 else SB_BF16
+    if bias is not None:
+        ep.bias = prep_aux(bias).data_ptr()
+    if rope_cos is not None:
+        cos_t = prep_aux(rope_cos)
+        ep.rope_cos = cos_t.data_ptr()
+        ep.rope_sin = prep_aux(rope_sin).data_ptr()
+        ep.ld_rope = cos_t.stride(0)
+        ep.rope_scale = prep_aux(rope_scale).data_ptr()
+    ep.rope_head_dim = int(rope_head_dim)
+    ep.rope_eps = float(rope_eps)
+    if norm_scale is not None:
+        ep.norm_scale = prep_aux(norm_scale).data_ptr()
+    ep.norm_eps = float(norm_eps)
+
+    lib = _native.load()
+    ws_bytes = int(lib.sb_workspace_bytes(m, n, k, ep.kind))
+    ws_ptr = None
+    if ws_bytes:
+        if workspace is None:
+            workspace = torch.empty(ws_bytes, dtype=torch.uint8, device=device)
+        if workspace.numel() * workspace.element_size() < ws_bytes:
+            raise ValueError(f"workspace must hold {ws_bytes} bytes")
+        ws_ptr = workspace.data_ptr()
+    with torch.cuda.device(device):
+        status = lib.sb_strassen_gemm(
+            _stream_handle(device), a.data_ptr(), b.data_ptr(), out.data_ptr(),
+            m, n, k, _ld(a), _ld(b), _ld(out), bm, bn, bk,
+            SB_F32 if out_dt == torch.float32 else SB_BF16, ctypes.byref(ep),
+            ws_ptr, ws_bytes)
+    _native.check(status)
+    return out
+
+
+def workspace_bytes(m: int, n: int, k: int, epilogue=None) -> int:
+    """Scratch bytes :func:`strassen_matmul` needs (non-zero for norm_residual_add)."""
+    return int(_native.load().sb_workspace_bytes(m, n, k, EPILOGUE_KINDS[epilogue]))
+
+
+def classical_matmul(a, b, *, bm=TUNED_BM, bn=TUNED_BN, bk=TUNED_BK, output_dtype=None, out=None):
+    """Matched-tile cubic control: the same sm_100a kernel skeleton with eight
+    classical sub-block products and no operand sums.
+
+    Mirrors the reference's blocked cubic Pallas control
+    (experiments/qwen3/benchmark_cubic_control.py:57-237, variant="blocked").
+    """
+    if a.ndim != 2 or b.ndim != 2:
+        raise ValueError("classical_matmul expects two rank-2 matrices")
+    m, k = a.shape
+    k2, n = b.shape
+    if k != k2:
+        raise ValueError(f"inner dimensions disagree: {k} vs {k2}")
+    if a.dtype != torch.bfloat16 or b.dtype != torch.bfloat16:
+        raise ValueError("inputs must be BF16")
+    for name, dimension, block in (("M", m, bm), ("N", n, bn), ("K", k, bk)):
+        if dimension % block:
+            raise ValueError(f"{name}={dimension} is not divisible by {block}")
+    check_tiling(bm, bn, bk)
+    out_dt = _as_torch_dtype(output_dtype) or torch.bfloat16
+    device = a.device
+    a, b = _rowmajor(a), _rowmajor(b)
+    if out is None:
+        out = torch.empty((m, n), dtype=out_dt, device=device)
+    lib = _native.load()
+    with torch.cuda.device(device):
+        status = lib.sb_classical_gemm(_stream_handle(device), a.data_ptr(), b.data_ptr(),
+                                       out.data_ptr(), m, n, k, _ld(a), _ld(b), _ld(out),
+                                       bm, bn, bk, SB_F32 if out_dt == torch.float32 else SB_BF16)
+    _native.check(status)
+    return out
+
+
+def rms_norm(x, scale, eps: float = 1e-6, out=None):
+    """bf16 RMSNorm with fp32 math on the sm_100a row kernel.
+
+    Mirrors experiments/qwen3/benchmark_qwen3_32b_layer.py:270-276:
+    ``bf16(x * rsqrt(mean(x^2, -1) + eps) * scale)``.  ``x`` is [..., n] bf16.
+    """
+    if x.dtype != torch.bfloat16:
+        raise ValueError("rms_norm expects a bf16 input")
+    n = x.shape[-1]
+    x2 = x.reshape(-1, n).contiguous()
+    w = scale.to(device=x.device)
+    if w.dtype not in (torch.bfloat16, torch.float32):
+        w = w.float()
+    w = w.contiguous()
+    y = torch.empty_like(x2) if out is None else out.reshape(-1, n)
+    lib = _native.load()
+    with torch.cuda.device(x.device):
+        status = lib.sb_rms_norm(_stream_handle(x.device), x2.data_ptr(), w.data_ptr(), y.data_ptr(),
+                                 x2.shape[0], n, SB_F32 if w.dtype == torch.float32 else SB_BF16,
+                                 float(eps))
+    _native.check(status)
+    return y.reshape(x.shape)
+
+
+def native_matmul(a, b):
+    """Classical bf16 GEMM with fp32 accumulation (cuBLAS): the comparison arm.
+
+    Mirrors strassen_pallas.native_matmul (strassen_pallas.py:1414-1421).
+    """
+    return torch.matmul(a, b).to(a.dtype)
