@@ -1,0 +1,344 @@
+#!/usr/bin/env python3
+"""Benchmark of the sm_100a tile-local Strassen GEMM (the north-star hot path).
+
+Workload: BASELINE.json metric "Strassen GEMM effective TFLOP/s (2MNK/t) vs
+cuBLAS" at its quoted point M = N = K = 8192 (config 3), bf16 inputs ~N(0,1)
+from numpy default_rng(20260902) / (20260903), fp32 accumulation, bf16 output,
+the reference's default tile (bm, bn, bk) = (1024, 1024, 512).  A "step" is one
+GEMM.  Inputs are 256 MiB (> 126 MiB L2), so no L2 flush is needed between
+steps.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
+
+N > 1 runs under torchrun, one rank per GPU; every rank computes its own
+independent GEMM of the same shape (weak scaling, no collective on the data
+path); times are CUDA-event times, max over ranks.  ``--impl reference`` times
+the CPU restatement of the reference's algorithm (``oracle/``) on the host
+cores -- the reference itself is JAX/Pallas-on-TPU and cannot run here.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import sys
+import threading
+import time
+from pathlib import Path
+
+import numpy as np
+
+REPO = Path(__file__).resolve().parent
+sys.path.insert(0, str(REPO))
+
+M = N = K = 8192
+TILE = (1024, 1024, 512)
+SEED_A, SEED_B = 20260902, 20260903
+METRIC = "strassen_gemm_effective_tflops"
+UNIT = "TFLOP/s"
+L2_BYTES = 126 * 1024 * 1024
+
+
+def parse():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=100)
+    p.add_argument("--warmup", type=int, default=5)
+    p.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    p.add_argument("--no-cpu-baseline", action="store_true",
+                   help="skip the CPU oracle timing (used for ncu captures)")
+    p.add_argument("--no-e2e", action="store_true", help="skip the host-buffer end-to-end loop")
+    return p.parse_args()
+
+
+def dist_env():
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return rank, world, local
+
+
+def host_inputs():
+    """Seeded bf16 inputs as uint16 bit patterns (the oracle's recipe)."""
+    from oracle import strassen_ref as ref
+    a = ref.bf16_bits(ref.normal_bf16((M, K), SEED_A))
+    b = ref.bf16_bits(ref.normal_bf16((K, N), SEED_B))
+    return a, b
+
+
+# ------------------------------------------------------------- clock sampler
+class ClockSampler:
+    """Samples SM clock and throttle reasons through NVML while running."""
+
+    REASONS = {
+        "gpu_idle": 0x1, "applications_clocks_setting": 0x2, "sw_power_cap": 0x4,
+        "hw_slowdown": 0x8, "sync_boost": 0x10, "sw_thermal_slowdown": 0x20,
+        "hw_thermal_slowdown": 0x40, "hw_power_brake_slowdown": 0x80,
+        "display_clock_setting": 0x100,
+    }
+
+    def __init__(self, index: int, period_s: float = 0.01):
+        self.index, self.period = index, period_s
+        self.samples, self.reasons = [], set()
+        self.max_mhz = None
+        self._stop = threading.Event()
+        self._thread = None
+        self.ok = False
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            self.nvml = pynvml
+            self.handle = pynvml.nvmlDeviceGetHandleByIndex(index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.handle, pynvml.NVML_CLOCK_SM)
+            self.ok = True
+        except Exception as exc:  # pragma: no cover - depends on the box
+            self.error = repr(exc)
+
+    def _run(self):
+        nv = self.nvml
+        while not self._stop.is_set():
+            try:
+                self.samples.append(nv.nvmlDeviceGetClockInfo(self.handle, nv.NVML_CLOCK_SM))
+                mask = nv.nvmlDeviceGetCurrentClocksEventReasons(self.handle)
+                for name, bit in self.REASONS.items():
+                    if mask & bit and name != "gpu_idle":
+                        self.reasons.add(name)
+            except Exception:
+                pass
+            time.sleep(self.period)
+
+    def __enter__(self):
+        if self.ok:
+            self._thread = threading.Thread(target=self._run, daemon=True)
+            self._thread.start()
+        return self
+
+    def __exit__(self, *exc):
+        self._stop.set()
+        if self._thread:
+            self._thread.join()
+
+    def summary(self):
+        if not self.ok or not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": sorted(self.reasons),
+                    "samples": len(self.samples)}
+        return {"sm_mhz": float(statistics.median(self.samples)), "sm_max_mhz": self.max_mhz,
+                "reasons": sorted(self.reasons), "samples": len(self.samples)}
+
+
+# ------------------------------------------------------------- CPU baseline
+def cpu_baseline(a_bits, b_bits, rows: int, cols: int | None = None, repeats: int = 1):
+    """Oracle (CPU restatement of the reference) on a bounded sample."""
+    from oracle import strassen_ref as ref
+    a = ref.from_bf16_bits(a_bits[:rows])
+    b = ref.from_bf16_bits(b_bits if cols is None else b_bits[:, :cols])
+    n = b.shape[1]
+    times = []
+    for _ in range(repeats):
+        t0 = time.perf_counter()
+        ref.strassen_matmul_ref(a, b, bm=TILE[0], bn=min(TILE[1], n), bk=TILE[2])
+        times.append(time.perf_counter() - t0)
+    t = min(times)
+    flops = 2.0 * rows * n * K
+    return flops / t / 1e12, t, rows, n
+
+
+def cpu_threads() -> int:
+    try:
+        from threadpoolctl import threadpool_info
+        info = [x for x in threadpool_info() if x.get("user_api") == "blas"]
+        if info:
+            return int(info[0]["num_threads"])
+    except Exception:
+        pass
+    return os.cpu_count() or 1
+
+
+# ------------------------------------------------------------- reference arm
+def run_reference(args):
+    rank, world, _ = dist_env()
+    if rank != 0:
+        return 0
+    a_bits, b_bits = host_inputs()
+    rows = cols = TILE[0]  # one (1024 x 1024) output tile of the 8192^3 GEMM per step
+    for _ in range(args.warmup):
+        cpu_baseline(a_bits, b_bits, rows, cols)
+    vals, ts = [], []
+    for _ in range(args.steps):
+        v, t, _, _ = cpu_baseline(a_bits, b_bits, rows, cols)
+        vals.append(v)
+        ts.append(t)
+    total_t = sum(ts)
+    value = args.steps * 2.0 * rows * cols * K / total_t / 1e12
+    threads = cpu_threads()
+    sample = (f"one {rows}x{cols} output tile (K={K}) of the {M}x{N}x{K} GEMM per step, "
+              f"tile {TILE}, numpy/BLAS oracle")
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT,
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": 1e3 * total_t / args.steps, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": f"strassen_gemm_{M}x{N}x{K}_bf16", "tile": list(TILE),
+                   "sample": sample},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port",
+                         "sample": sample},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# ------------------------------------------------------------------ our arm
+def run_ours(args):
+    import torch
+    import torch.distributed as dist
+
+    import strassen_tpu_b200 as sb
+    from strassen_tpu_b200 import _native
+
+    rank, world, local = dist_env()
+    if world > 1:
+        torch.cuda.set_device(local)
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+
+    a_bits, b_bits = host_inputs()
+    a_host = torch.from_numpy(a_bits.view(np.int16)).view(torch.bfloat16).pin_memory()
+    b_host = torch.from_numpy(b_bits.view(np.int16)).view(torch.bfloat16).pin_memory()
+    a = a_host.to(device)
+    b = b_host.to(device)
+    c = torch.empty(M, N, dtype=torch.bfloat16, device=device)
+    stream = torch.cuda.current_stream(device)
+    flops = 2.0 * M * N * K
+
+    def step():
+        sb.strassen_matmul(a, b, bm=TILE[0], bn=TILE[1], bk=TILE[2], out=c)
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[local])
+
+    def max_over_ranks(x: float) -> float:
+        if world == 1:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    def timed(fn, steps, warmup):
+        for _ in range(warmup):
+            fn()
+        barrier()
+        torch.cuda.synchronize(device)
+        start = torch.cuda.Event(enable_timing=True)
+        end = torch.cuda.Event(enable_timing=True)
+        start.record(stream)
+        for _ in range(steps):
+            fn()
+        end.record(stream)
+        torch.cuda.synchronize(device)
+        barrier()
+        return max_over_ranks(start.elapsed_time(end))
+
+    # --- the device-resident timed region (value), with clocks sampled during it
+    with ClockSampler(device.index) as clocks:
+        elapsed_ms = timed(step, args.steps, args.warmup)
+    ms = elapsed_ms / args.steps
+    value = world * flops * args.steps / (elapsed_ms * 1e-3) / 1e12
+    dev_err = _native.device_status(reset=True)
+    if dev_err:
+        raise RuntimeError(f"bounded in-kernel wait timed out (code {dev_err})")
+
+    # --- roofline of the dominant kernel: raw tensor FLOPs (7/8 of 2MNK) per launch
+    peaks = {}
+    peaks_path = REPO / "MEASURED_PEAKS.json"
+    if peaks_path.exists():
+        peaks = json.loads(peaks_path.read_text())
+    peak = peaks.get("bf16_tflops")
+    peak_src = "measured (MEASURED_PEAKS.json bf16_tflops, burst)"
+    if peak is None:
+        peak, peak_src = 1590.0, "fallback 1.59 PFLOP/s"
+    raw_flops = flops * 7.0 / 8.0
+    achieved = raw_flops / (ms * 1e-3) / 1e12
+    traffic = None
+    traffic_path = REPO / "profiles" / "strassen_gemm_8192_traffic.json"
+    if traffic_path.exists():
+        traffic = json.loads(traffic_path.read_text()).get("dram_bytes_per_launch")
+
+    # --- comparison arms on identical tensors (informational)
+    cublas_ms = timed(lambda: torch.matmul(a, b, out=c), max(10, args.steps // 2), 3) / max(10, args.steps // 2)
+    control_ms = timed(lambda: sb.classical_matmul(a, b, bm=TILE[0], bn=TILE[1], bk=TILE[2], out=c),
+                       max(10, args.steps // 2), 3) / max(10, args.steps // 2)
+
+    # --- end to end through the public API with host buffers
+    e2e = None
+    if not args.no_e2e:
+        c_host = torch.empty(M, N, dtype=torch.bfloat16).pin_memory()
+
+        def e2e_step():
+            ad = a_host.to(device, non_blocking=True)
+            bd = b_host.to(device, non_blocking=True)
+            out = sb.strassen_matmul(ad, bd, bm=TILE[0], bn=TILE[1], bk=TILE[2])
+            c_host.copy_(out, non_blocking=True)
+
+        e2e_steps = max(5, args.steps // 5)
+        e2e_ms = timed(e2e_step, e2e_steps, 2) / e2e_steps
+        e2e = {"value": world * flops / (e2e_ms * 1e-3) / 1e12, "unit": UNIT,
+               "h2d_bytes_per_step": 2 * M * K * 2, "d2h_bytes_per_step": M * N * 2,
+               "ms_per_step": e2e_ms}
+
+    # --- CPU baseline (rank 0 at N=1 only)
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        rows = 2 * TILE[0]
+        v, t, r, n = cpu_baseline(a_bits, b_bits, rows)
+        cpu = {"value": v, "unit": UNIT, "cores": cpu_threads(), "kind": "port",
+               "sample": f"first {r} rows (2 block rows) of the {M}x{N}x{K} GEMM, tile {TILE}, "
+                         f"{t:.1f} s, numpy/BLAS restatement of the reference"}
+
+    if world > 1:
+        barrier()
+        dist.destroy_process_group()
+    if rank != 0:
+        return 0
+    clock = clocks.summary()
+    line = {
+        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": f"strassen_gemm_{M}x{N}x{K}_bf16", "tile": list(TILE),
+                   "l2": "inputs 256 MiB > 126 MiB L2, no flush",
+                   "inputs": f"N(0,1) bf16, default_rng({SEED_A}) / ({SEED_B})",
+                   "parallelism": f"replicas x{world}" if world > 1 else "single GPU"},
+        "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": UNIT,
+                     "frac": achieved / peak, "traffic": traffic,
+                     "basis": "raw tensor FLOPs 7/8*2MNK per launch / CUDA-event launch time",
+                     "peak_source": peak_src, "effective_tflops": flops / (ms * 1e-3) / 1e12},
+        "cpu_baseline": cpu,
+        "e2e": e2e,
+        "clocks": clock,
+        "gpu_launches": args.steps,
+        "comparison": {
+            "cublas_tflops": flops / (cublas_ms * 1e-3) / 1e12,
+            "strassen_vs_cublas": (flops / (ms * 1e-3)) / (flops / (cublas_ms * 1e-3)),
+            "classical_control_tflops": flops / (control_ms * 1e-3) / 1e12,
+        },
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        return run_reference(args)
+    return run_ours(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

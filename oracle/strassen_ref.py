@@ -161,7 +161,8 @@ def _assemble_half(top, bottom, m, bm, hn, n_j):
 def silu(x):
     """jax.nn.silu in fp32: x * logistic(x)."""
     x = np.asarray(x, F32)
-    return (x * (F32(1) / (F32(1) + np.exp(-x)))).astype(F32)
+    with np.errstate(over="ignore"):
+        return (x * (F32(1) / (F32(1) + np.exp(-x)))).astype(F32)
 
 
 def gelu_tanh(x):
@@ -222,24 +223,33 @@ def strassen_matmul_ref(a, b, *, bm, bn, bk, interleave_products=False, epilogue
         scale_a, scale_b = scale[:hn], scale[hn:]
         cos = np.asarray(rope_cos, F32).reshape(n_i, 2, hm, hn)
         sin = np.asarray(rope_sin, F32).reshape(n_i, 2, hm, hn)
-        seg = rope_head_dim // 2
+        seg_width = rope_head_dim // 2
         inv = F32(1.0 / rope_head_dim)
         eps = F32(rope_eps)
+        # Segment sums through a 0/1 matrix padded to 128 lanes, per tile, as
+        # the reference does (strassen_pallas.py:1180-1197, 817-823).
+        cols = np.arange(hn)
+        segment = np.zeros((hn, 128), F32)
+        segment[cols, cols // seg_width] = 1.0
+        segment_t = np.ascontiguousarray(segment.T)
 
-        def rotate(first, second, half):
-            # first/second: [nI, nJ, hm, hn]; tables per block row I, same for all J
-            sums = (first * first).reshape(*first.shape[:3], hn // seg, seg).sum(-1, dtype=F32) \
-                + (second * second).reshape(*second.shape[:3], hn // seg, seg).sum(-1, dtype=F32)
-            recip = np.repeat(rsqrt(sums * inv + eps), seg, axis=-1)
+        def rotate(first, second, c, s):
+            sums = np.dot(first * first, segment).astype(F32) + np.dot(second * second, segment).astype(F32)
+            recip = np.dot(rsqrt(sums * inv + eps), segment_t).astype(F32)
             na = first * recip * scale_a
             nb = second * recip * scale_b
-            c = cos[:, half][:, None]
-            s = sin[:, half][:, None]
             return na * c - nb * s, nb * c + na * s
 
-        ta, tb = rotate(acc[0], acc[1], 0)
-        ba, bb = rotate(acc[2], acc[3], 1)
-        return bf16_round(_assemble([ta, tb, ba, bb], m, n, bm, bn))
+        quads = [np.empty_like(acc[0]) for _ in range(4)]
+        with np.errstate(divide="ignore", over="ignore", invalid="ignore"):
+            for i in range(n_i):
+                for j in range(n_j):
+                    for half in range(2):
+                        first, second = acc[2 * half][i, j], acc[2 * half + 1][i, j]
+                        oa, ob = rotate(first, second, cos[i, half], sin[i, half])
+                        quads[2 * half][i, j] = oa
+                        quads[2 * half + 1][i, j] = ob
+        return bf16_round(_assemble(quads, m, n, bm, bn))
     if epilogue == "norm_residual_add":  # strassen_pallas.py:836-866
         if bn != n:
             raise ValueError("norm_residual_add needs bn == n")

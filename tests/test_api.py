@@ -1,0 +1,114 @@
+"""Host-side contract of ``strassen_matmul`` (no GPU needed).
+
+Validation mirrors the reference's ValueError/TypeError conditions and messages
+(strassen_pallas.py:927-1057, check_tiling :127-140), raised before any launch.
+CPU tensors are used: every case here fails validation first.
+"""
+
+from __future__ import annotations
+
+import pytest
+import torch
+
+import strassen_tpu_b200 as sb
+
+BF = torch.bfloat16
+
+
+def mats(m=256, k=256, n=256, dtype=BF):
+    return torch.zeros(m, k, dtype=dtype), torch.zeros(k, n, dtype=dtype)
+
+
+def call(a=None, b=None, **kw):
+    if a is None:
+        a, b = mats()
+    kw.setdefault("bm", 256)
+    kw.setdefault("bn", 256)
+    kw.setdefault("bk", 256)
+    return sb.strassen_matmul(a, b, **kw)
+
+
+@pytest.mark.parametrize("kw, match", [
+    (dict(a=torch.zeros(2, 2, 2, dtype=BF), b=torch.zeros(2, 2, dtype=BF)), "two rank-2 matrices"),
+    (dict(a=torch.zeros(256, 512, dtype=BF), b=torch.zeros(256, 256, dtype=BF)), "inner dimensions disagree: 512 vs 256"),
+    (dict(a=torch.zeros(256, 256, dtype=BF), b=torch.zeros(256, 256, dtype=torch.float32)), "input dtypes disagree"),
+    (dict(a=torch.zeros(256, 256, dtype=torch.float16), b=torch.zeros(256, 256, dtype=torch.float16)), "BF16 or FP32"),
+    (dict(block_permutation=8), "block_permutation"),
+    (dict(formula_variant="winograd"), "formula_variant"),
+    (dict(epilogue="relu"), "unknown epilogue 'relu'"),
+    (dict(epilogue="swiglu", output_dtype=torch.float32), "fused epilogues write a BF16 output tile"),
+    (dict(epilogue="residual_add"), "residual_add epilogue requires residual="),
+    (dict(epilogue="bias_add"), "bias_add epilogue requires bias="),
+    (dict(residual=torch.zeros(256, 256, dtype=BF)), "residual= is only used"),
+    (dict(bias=torch.zeros(256, dtype=BF)), "bias= is only used"),
+    (dict(epilogue="norm_residual_add"), "norm_residual_add requires residual= and norm_scale="),
+    (dict(epilogue="qk_norm_rope"), "qk_norm_rope epilogue requires rope_cos="),
+    (dict(rope_cos=torch.zeros(256, 128, dtype=BF)), "rope_\\* are only used"),
+    (dict(product_aware_swiglu=True), "product_aware_swiglu is only valid"),
+    (dict(product_aware_residual=True), "product_aware_residual is only valid"),
+    (dict(allow_input_fusion=(True,)), "one boolean per operand: expected 2, got 1"),
+    (dict(classical_panels=(0,), panel_schedule=[0]), "either classical_panels"),
+    (dict(classical_panels=(5,)), "outside 0..0"),
+    (dict(bm=48), "M=256 is not divisible by 48"),
+    (dict(bn=128, a=torch.zeros(256, 256, dtype=BF), b=torch.zeros(256, 256, dtype=BF)), "bn=128 must be a multiple of 256"),
+    (dict(bm=8, a=torch.zeros(16, 256, dtype=BF), b=torch.zeros(256, 256, dtype=BF)), "bm=8 must be a multiple of 16"),
+    (dict(output_dtype="float16"), "output_dtype must be BF16 or FP32"),
+])
+def test_reference_value_errors(kw, match):
+    with pytest.raises(ValueError, match=match):
+        call(**kw)
+
+
+def test_allow_input_fusion_type_error():
+    with pytest.raises(TypeError, match="entries must be bool"):
+        call(allow_input_fusion=(1, 0))
+
+
+def test_norm_residual_requires_full_row_tile():
+    a, b = mats(256, 256, 512)
+    with pytest.raises(ValueError, match="bn=256 must equal n=512"):
+        call(a, b, epilogue="norm_residual_add", residual=torch.zeros(256, 512, dtype=BF),
+             norm_scale=torch.ones(512, dtype=BF))
+
+
+def test_qk_norm_rope_shape_contract():
+    a, b = mats(256, 256, 512)
+    with pytest.raises(ValueError, match="bn a multiple of 2\\*head_dim=768"):
+        call(a, b, bn=512, epilogue="qk_norm_rope", rope_head_dim=384, rope_cos=torch.zeros(256, 256),
+             rope_sin=torch.zeros(256, 256), rope_scale=torch.zeros(512))
+    with pytest.raises(ValueError, match="rope tables must be \\(256, 256\\)"):
+        call(a, b, bn=512, epilogue="qk_norm_rope", rope_cos=torch.zeros(256, 128),
+             rope_sin=torch.zeros(256, 128), rope_scale=torch.zeros(512))
+    with pytest.raises(ValueError, match="rope_scale must be laid out to \\(512,\\)"):
+        call(a, b, bn=512, epilogue="qk_norm_rope", rope_cos=torch.zeros(256, 256),
+             rope_sin=torch.zeros(256, 256), rope_scale=torch.zeros(128))
+
+
+def test_no_cpu_path():
+    # A valid call on CPU tensors must refuse, not silently compute on the host.
+    with pytest.raises(ValueError, match="no CPU fallback"):
+        call()
+    with pytest.raises(NotImplementedError, match="no CPU path"):
+        call(interpret=True)
+
+
+def test_unbuilt_reference_options_refuse_loudly():
+    with pytest.raises(NotImplementedError, match="FP32 inputs"):
+        call(*mats(dtype=torch.float32))
+    with pytest.raises(NotImplementedError):
+        call(formula_variant="dual")
+    with pytest.raises(NotImplementedError):
+        call(block_permutation=3)
+    with pytest.raises(NotImplementedError):
+        call(classical_panels=(0,))
+
+
+def test_check_tiling_message():
+    with pytest.raises(ValueError) as err:
+        sb.check_tiling(8, 128, 100)
+    msg = str(err.value)
+    assert msg.startswith("tile breaks TPU v5e alignment:")
+    assert "bm=8 must be a multiple of 16" in msg
+    assert "bn=128 must be a multiple of 256" in msg
+    assert "bk=100 must be a multiple of 256" in msg
+    sb.check_tiling(16, 256, 256)
