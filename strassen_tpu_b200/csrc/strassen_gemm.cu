@@ -50,38 +50,69 @@
 #include <cstring>
 #include <mutex>
 #include <string>
+#include <type_traits>
 
 namespace sb {
 
 // ------------------------------------------------------------------ shape
 constexpr int kBlockM = 128;  // product rows per CTA = TMEM lanes
 constexpr int kBlockN = 64;   // product columns per CTA = TMEM columns per product
-constexpr int kBlockK = 32;   // product depth per pipeline stage
-constexpr int kStages = 2;
-constexpr int kSlots = 7;     // operand tiles per side and stage
-constexpr int kASlotBytes = kBlockM * kBlockK * 2;              // 8192
-constexpr int kBSlotBytes = kBlockK * kBlockN * 2;              // 4096
-constexpr int kStageBytes = kSlots * (kASlotBytes + kBSlotBytes);  // 86016
-constexpr int kRawTxBytes = 4 * (kASlotBytes + kBSlotBytes);      // 49152
+#ifndef SB_BLOCK_K
+#define SB_BLOCK_K 16
+#endif
+#ifndef SB_STAGES
+#define SB_STAGES 5
+#endif
+#ifndef SB_C_BLOCK_K
+#define SB_C_BLOCK_K 64
+#endif
+#ifndef SB_C_STAGES
+#define SB_C_STAGES 2
+#endif
 constexpr int kFirstSumWarp = 4;
 constexpr int kSumWarps = 8;
+constexpr int kSumThreads = kSumWarps * 32;
 constexpr int kThreads = (kFirstSumWarp + kSumWarps) * 32;  // 384
 constexpr uint32_t kTmemCols = 512;
 constexpr int kBarrierBytes = 256;
-constexpr int kSmemBytes = kStages * kStageBytes + kBarrierBytes + 1024;  // + alignment slack
-
-static_assert(kBlockK == 32, "A-operand swizzle below assumes 64-byte K rows");
-static_assert(kStageBytes % 1024 == 0, "stages must keep 1024-byte alignment");
+constexpr int kRasterGroup = 16;  // product-row tiles per column sweep (L2 reuse)
 static_assert(7 * kBlockN <= (int)kTmemCols, "seven accumulators must fit in TMEM");
 
-// A: K-major, 64-byte rows -> 64B swizzle, 8-row core groups 512 bytes apart.
-constexpr uint32_t kALayout = kLayoutSwizzle64B;
-constexpr uint32_t kASbo = 8 * kBlockK * 2;  // 512
-constexpr uint32_t kALbo = 16;               // unused for swizzled K-major
-// B: N-major, 128-byte rows (64 columns) -> 128B swizzle, 8 k-rows per 1024 B.
-constexpr uint32_t kBLayout = kLayoutSwizzle128B;
-constexpr uint32_t kBSbo = 1024;
-constexpr uint32_t kBLbo = kBlockK * 128;    // next 64-column chunk (never used: N tile = 64)
+// Pipeline geometry.  A stage holds `kSlotsPerSide` A tiles (128 x BK, K-major)
+// and as many B tiles (BK x 64, N-major): the four raw quadrants first, then
+// (Strassen only) the operand sums.
+template <int kBK, int kNumStages, int kSlotsPerSide>
+struct PipeCfg {
+  static constexpr int BK = kBK;
+  static constexpr int STAGES = kNumStages;
+  static constexpr int SLOTS = kSlotsPerSide;
+  static constexpr int A_SLOT = kBlockM * kBK * 2;
+  static constexpr int B_SLOT = kBK * kBlockN * 2;
+  static constexpr int STAGE_BYTES = SLOTS * (A_SLOT + B_SLOT);
+  static constexpr int RAW_TX = 4 * (A_SLOT + B_SLOT);
+  static constexpr int SMEM = STAGES * STAGE_BYTES + kBarrierBytes + 1024;  // + alignment slack
+  // A: K-major, one BK-wide row per swizzle row (32/64/128 bytes); 8-row core
+  // groups 8*row bytes apart; LBO unused for swizzled K-major.
+  static constexpr uint32_t A_ROW = kBK * 2;
+  static constexpr uint32_t A_LAYOUT = A_ROW == 32 ? kLayoutSwizzle32B
+                                       : A_ROW == 64 ? kLayoutSwizzle64B : kLayoutSwizzle128B;
+  static constexpr uint32_t A_SBO = 8 * A_ROW;
+  static constexpr uint32_t A_LBO = 16;
+  // B: N-major 128-byte rows (64 columns), 128B swizzle, 8 k-rows per 1024 B; the
+  // LBO (next 64-column chunk) is never used because the N tile is 64.
+  static constexpr uint32_t B_LAYOUT = kLayoutSwizzle128B;
+  static constexpr uint32_t B_SBO = 1024;
+  static constexpr uint32_t B_LBO = kBK * 128;
+  static_assert(kBK == 16 || kBK == 32 || kBK == 64, "K chunk must be one swizzle row");
+  static_assert(STAGE_BYTES % 1024 == 0, "stages must keep 1024-byte alignment");
+  static_assert(SMEM <= 227 * 1024, "shared memory budget");
+  static_assert(kNumStages <= 8, "barrier area holds at most 8 stages");
+};
+using StrassenPipe = PipeCfg<SB_BLOCK_K, SB_STAGES, 7>;
+using ClassicalPipe = PipeCfg<SB_C_BLOCK_K, SB_C_STAGES, 4>;
+template <bool kStrassen>
+using PipeFor = typename std::conditional<kStrassen, StrassenPipe, ClassicalPipe>::type;
+
 constexpr uint32_t kIdesc = umma_idesc_bf16_f32(kBlockM, kBlockN, false, true);
 
 // Operand slots inside a stage.  Raw tiles land in slots 0..3
@@ -206,6 +237,13 @@ template <bool kStrassen, int kEpi, bool kOutF32>
 __global__ void __launch_bounds__(kThreads, 1)
     strassen_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a,
                          const __grid_constant__ CUtensorMap tmap_b, const GemmParams p) {
+  using P = PipeFor<kStrassen>;
+  constexpr int kStages = P::STAGES;
+  constexpr int kStageBytes = P::STAGE_BYTES;
+  constexpr int kASlotBytes = P::A_SLOT;
+  constexpr int kBSlotBytes = P::B_SLOT;
+  constexpr int kSlots = P::SLOTS;
+  constexpr int kBlockK = P::BK;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_addr = smem_addr(smem_raw);
   uint8_t* smem = smem_raw + ((1024u - (raw_addr & 1023u)) & 1023u);
@@ -225,7 +263,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   // Grouped rasterisation: walk 8 product-row tiles per column sweep for L2 reuse.
   const int tile = blockIdx.x;
-  const int group_rows = 8;
+  const int group_rows = kRasterGroup;
   const int per_group = group_rows * p.tiles_n;
   const int group = tile / per_group;
   const int first_m = group * group_rows;
@@ -273,7 +311,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t ph = (c / kStages) & 1u;
         if (!mbar_wait(empty_bar + 8 * s, ph ^ 1u, abort_flag, p.err, kErrWaitEmpty)) break;
         const uint32_t fb = full_bar + 8 * s;
-        mbar_arrive_expect_tx(fb, kRawTxBytes);
+        mbar_arrive_expect_tx(fb, P::RAW_TX);
         const int kap = c * kBlockK;
         const int panel = kap / p.half_bk;
         const int kin = kap - panel * p.half_bk;
@@ -319,18 +357,18 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
             for (int i = 0; i < 7; ++i) {
               const uint64_t ad =
-                  umma_smem_desc(a_stage + kASlot[i] * kASlotBytes + kk * 32, kALbo, kASbo, kALayout);
+                  umma_smem_desc(a_stage + kASlot[i] * kASlotBytes + kk * 32, P::A_LBO, P::A_SBO, P::A_LAYOUT);
               const uint64_t bd = umma_smem_desc(b_stage + kBSlot[i] * kBSlotBytes + kk * 2048,
-                                                 kBLbo, kBSbo, kBLayout);
+                                                 P::B_LBO, P::B_SBO, P::B_LAYOUT);
               umma_bf16_ss(tmem_base + i * kBlockN, ad, bd, kIdesc, (c | kk) != 0 ? 1u : 0u);
             }
           } else {
 #pragma unroll
             for (int i = 0; i < 8; ++i) {
-              const uint64_t ad = umma_smem_desc(a_stage + kCAslot[i] * kASlotBytes + kk * 32, kALbo,
-                                                 kASbo, kALayout);
+              const uint64_t ad = umma_smem_desc(a_stage + kCAslot[i] * kASlotBytes + kk * 32, P::A_LBO,
+                                                 P::A_SBO, P::A_LAYOUT);
               const uint64_t bd = umma_smem_desc(b_stage + kCBslot[i] * kBSlotBytes + kk * 2048,
-                                                 kBLbo, kBSbo, kBLayout);
+                                                 P::B_LBO, P::B_SBO, P::B_LAYOUT);
               const bool first = (c == 0) && (kk == 0) && ((i & 1) == 0);
               umma_bf16_ss(tmem_base + (i >> 1) * kBlockN, ad, bd, kIdesc, first ? 0u : 1u);
             }
@@ -356,8 +394,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t a_stage = smem_base + s * kStageBytes;
         const uint32_t b_stage = a_stage + kSlots * kASlotBytes;
 #pragma unroll
-        for (int r = 0; r < kASlotBytes / 16 / (kSumWarps * 32); ++r) {
-          const uint32_t off = (sum_tid + r * kSumWarps * 32) * 16;
+        for (int idx = sum_tid; idx < kASlotBytes / 16; idx += kSumThreads) {
+          const uint32_t off = idx * 16;
           const uint4 a0 = lds128(a_stage + 0 * kASlotBytes + off);
           const uint4 a1 = lds128(a_stage + 1 * kASlotBytes + off);
           const uint4 a2 = lds128(a_stage + 2 * kASlotBytes + off);
@@ -369,8 +407,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           sts128(a_stage + 2 * kASlotBytes + off, sub4(a2, a0));
         }
 #pragma unroll
-        for (int r = 0; r < kBSlotBytes / 16 / (kSumWarps * 32); ++r) {
-          const uint32_t off = (sum_tid + r * kSumWarps * 32) * 16;
+        for (int idx = sum_tid; idx < kBSlotBytes / 16; idx += kSumThreads) {
+          const uint32_t off = idx * 16;
           const uint4 b0 = lds128(b_stage + 0 * kBSlotBytes + off);
           const uint4 b1 = lds128(b_stage + 1 * kBSlotBytes + off);
           const uint4 b2 = lds128(b_stage + 2 * kBSlotBytes + off);
@@ -694,12 +732,13 @@ int launch_typed(cudaStream_t stream, const CUtensorMap& ta, const CUtensorMap& 
   static std::once_flag once;
   static cudaError_t attr_err = cudaSuccess;
   std::call_once(once, [&]() {
-    attr_err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+    attr_err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    PipeFor<kStrassen>::SMEM);
   });
   if (attr_err != cudaSuccess)
     return fail(SB_ERR_CUDA, std::string("cudaFuncSetAttribute: ") + cudaGetErrorString(attr_err));
   const unsigned grid = (unsigned)(p.tiles_m * p.tiles_n);
-  kernel<<<grid, kThreads, kSmemBytes, stream>>>(ta, tb, p);
+  kernel<<<grid, kThreads, PipeFor<kStrassen>::SMEM, stream>>>(ta, tb, p);
   const cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return fail(SB_ERR_CUDA, std::string("kernel launch: ") + cudaGetErrorString(e));
   return SB_OK;
@@ -781,28 +820,31 @@ int validate_core(const void* a, const void* b, const void* c, int64_t m, int64_
 }
 
 int make_maps(const void* a, const void* b, int64_t m, int64_t n, int64_t k, int64_t lda,
-              int64_t ldb, int32_t bm, CUtensorMap* ta, CUtensorMap* tb) {
+              int64_t ldb, int32_t bm, int bk_chunk, CUtensorMap* ta, CUtensorMap* tb) {
+  const int a_row_bytes = bk_chunk * 2;
   EncodeTiledFn enc = encode_fn();
   if (!enc) return fail(SB_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
   const int half_bm = bm / 2;
   const uint32_t rows = half_bm >= kBlockM ? kBlockM : half_bm;
   const uint32_t blocks = half_bm >= kBlockM ? 1 : kBlockM / half_bm;
   {
-    // A viewed as [M/bm][bm][K]; a box is BLOCK_K columns of `rows` rows in each
+    // A viewed as [M/bm][bm][K]; a box is kBlockK columns of `rows` rows in each
     // of `blocks` consecutive Strassen blocks = one 128-row product tile.
     cuuint64_t dims[3] = {(cuuint64_t)k, (cuuint64_t)bm, (cuuint64_t)(m / bm)};
     cuuint64_t strides[2] = {(cuuint64_t)lda * 2, (cuuint64_t)lda * 2 * bm};
-    cuuint32_t box[3] = {(cuuint32_t)kBlockK, rows, blocks};
+    cuuint32_t box[3] = {(cuuint32_t)bk_chunk, rows, blocks};
     cuuint32_t estr[3] = {1, 1, 1};
     CUresult r = enc(ta, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(a), dims, strides, box,
-                     estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B,
+                     estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                     a_row_bytes == 32 ? CU_TENSOR_MAP_SWIZZLE_32B
+                     : a_row_bytes == 64 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B,
                      CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) return fail(SB_ERR_CUDA, "cuTensorMapEncodeTiled(A) failed: " + std::to_string((int)r));
   }
   {
     cuuint64_t dims[2] = {(cuuint64_t)n, (cuuint64_t)k};
     cuuint64_t strides[1] = {(cuuint64_t)ldb * 2};
-    cuuint32_t box[2] = {(cuuint32_t)kBlockN, (cuuint32_t)kBlockK};
+    cuuint32_t box[2] = {(cuuint32_t)kBlockN, (cuuint32_t)bk_chunk};
     cuuint32_t estr[2] = {1, 1};
     CUresult r = enc(tb, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(b), dims, strides, box,
                      estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
@@ -813,7 +855,7 @@ int make_maps(const void* a, const void* b, int64_t m, int64_t n, int64_t k, int
 }
 
 GemmParams base_params(int64_t m, int64_t n, int64_t k, int32_t bm, int32_t bn, int32_t bk, void* c,
-                       int64_t ldc) {
+                       int64_t ldc, int bk_chunk) {
   GemmParams p;
   std::memset(&p, 0, sizeof(p));
   p.M = (int32_t)m;
@@ -827,7 +869,7 @@ GemmParams base_params(int64_t m, int64_t n, int64_t k, int32_t bm, int32_t bn, 
   p.half_bk = bk / 2;
   p.Mp = (int32_t)(m / 2);
   p.Np = (int32_t)(n / 2);
-  p.num_chunks = (int32_t)(k / 2 / kBlockK);
+  p.num_chunks = (int32_t)(k / 2 / bk_chunk);
   p.tiles_m = (p.Mp + kBlockM - 1) / kBlockM;
   p.tiles_n = p.Np / kBlockN;
   p.C = c;
@@ -902,12 +944,12 @@ int sb_strassen_gemm(sb_stream_t stream_, const void* a, const void* b, void* c,
   if (st != SB_OK) return st;
 
   CUtensorMap ta, tb;
-  st = make_maps(a, b, m, n, k, lda, ldb, bm, &ta, &tb);
+  st = make_maps(a, b, m, n, k, lda, ldb, bm, StrassenPipe::BK, &ta, &tb);
   if (st != SB_OK) return st;
 
   if (epi == SB_EPI_NORM_RESIDUAL_ADD) {
     // Pass 1: fp32 pre-norm rows into the caller's workspace; pass 2: row norm.
-    GemmParams p = base_params(m, n, k, bm, bn, bk, workspace, n);
+    GemmParams p = base_params(m, n, k, bm, bn, bk, workspace, n, StrassenPipe::BK);
     st = dispatch(true, SB_EPI_NONE, true, stream, ta, tb, p);
     if (st != SB_OK) return st;
     norm_residual_rows_kernel<<<(unsigned)m, 256, 0, stream>>>(
@@ -919,7 +961,7 @@ int sb_strassen_gemm(sb_stream_t stream_, const void* a, const void* b, void* c,
     return SB_OK;
   }
 
-  GemmParams p = base_params(m, n, k, bm, bn, bk, c, ldc);
+  GemmParams p = base_params(m, n, k, bm, bn, bk, c, ldc, StrassenPipe::BK);
   if (ep) {
     p.residual = ep->residual;
     p.ldr = ep->ld_residual;
@@ -949,9 +991,9 @@ int sb_classical_gemm(sb_stream_t stream_, const void* a, const void* b, void* c
   st = check_device();
   if (st != SB_OK) return st;
   CUtensorMap ta, tb;
-  st = make_maps(a, b, m, n, k, lda, ldb, bm, &ta, &tb);
+  st = make_maps(a, b, m, n, k, lda, ldb, bm, ClassicalPipe::BK, &ta, &tb);
   if (st != SB_OK) return st;
-  GemmParams p = base_params(m, n, k, bm, bn, bk, c, ldc);
+  GemmParams p = base_params(m, n, k, bm, bn, bk, c, ldc, ClassicalPipe::BK);
   return dispatch(false, SB_EPI_NONE, out_dtype == SB_F32, stream, ta, tb, p);
 }
 
@@ -974,7 +1016,7 @@ int sb_rms_norm(sb_stream_t stream_, const void* x, const void* w, void* y, int6
 void sb_query_tile(int32_t* block_m, int32_t* block_n, int32_t* block_k) {
   if (block_m) *block_m = kBlockM;
   if (block_n) *block_n = kBlockN;
-  if (block_k) *block_k = kBlockK;
+  if (block_k) *block_k = StrassenPipe::BK;
 }
 
 const char* sb_status_string(int32_t status) {
