@@ -124,6 +124,27 @@ SB_API int sb_classical_gemm(sb_stream_t stream,
                       int32_t bm, int32_t bn, int32_t bk, int32_t out_dtype);
 
 /*
+ * sb_strassen_gemm_norm_residual_noalloc -- the norm_residual_add epilogue of
+ * sb_strassen_gemm, with its fp32 scratch in a device array built into the
+ * library instead of a caller workspace.  No counterpart in the reference.
+ *
+ * For callers that cannot provide or allocate scratch memory: a custom-call
+ * handler in a framework that owns device memory (cudaMalloc would compete with
+ * its allocator and synchronise the device), or a service with a fixed memory
+ * budget.  It allocates nothing.  Limit: M*N <= 8,388,608 (32 MiB of fp32),
+ * else SB_ERR_WORKSPACE.  Every GPU that loads the library holds the 32 MiB
+ * until exit; all calls share it, so calls that overlap on the GPU race.  The
+ * first call on a device looks up the array's address (make it before any
+ * stream capture).  `ep->kind` must be SB_EPI_NORM_RESIDUAL_ADD and bn == n.
+ */
+SB_API int sb_strassen_gemm_norm_residual_noalloc(sb_stream_t stream,
+                                                  const void* a, const void* b, void* c,
+                                                  int64_t m, int64_t n, int64_t k,
+                                                  int64_t lda, int64_t ldb, int64_t ldc,
+                                                  int32_t bm, int32_t bn, int32_t bk,
+                                                  const sb_epilogue* ep);
+
+/*
  * sb_rms_norm -- y = bf16(x * rsqrt(mean(x^2) + eps) * w), fp32 math.
  * Replaces the reference's rms_norm
  * (experiments/qwen3/benchmark_qwen3_32b_layer.py:270-276).  x, y: [rows, n]

@@ -47,6 +47,9 @@ SIGNATURES = {
                                   _c_i64, _c_i64, _c_i64, _c_int, _c_int, _c_int, _c_int,
                                   ctypes.POINTER(SbEpilogue), _c_ptr, _c_size]),
     "sb_workspace_bytes": (_c_size, [_c_i64, _c_i64, _c_i64, _c_int]),
+    "sb_strassen_gemm_norm_residual_noalloc": (
+        _c_int, [_c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_i64, _c_i64, _c_i64, _c_i64, _c_i64, _c_i64,
+                 _c_int, _c_int, _c_int, ctypes.POINTER(SbEpilogue)]),
     "sb_classical_gemm": (_c_int, [_c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_i64, _c_i64, _c_i64,
                                    _c_i64, _c_i64, _c_i64, _c_int, _c_int, _c_int, _c_int]),
     "sb_rms_norm": (_c_int, [_c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_i64, _c_i64, _c_int,

@@ -981,6 +981,100 @@ int sb_strassen_gemm(sb_stream_t stream_, const void* a, const void* b, void* c,
   return dispatch(true, epi, out_dtype == SB_F32, stream, ta, tb, p);
 }
 
+}  // extern "C"
+
+// ---------------------------------------------------------------------------
+// No-allocation variant of the norm_residual_add path.
+//
+// Some callers cannot hand this library a scratch buffer or let it call
+// cudaMalloc: a custom-call handler inside a framework that owns the device
+// memory (XLA reserves most of it up front and cudaMalloc would both compete
+// with its allocator and synchronise the device), or a serving process that
+// runs with a fixed, pre-planned memory budget.  For them the fp32 pre-norm
+// rows live in this file-scope device array instead of a caller workspace.
+//
+// Limits and sharing rules:
+//   * capacity kNoAllocScratchFloats fp32 values (32 MiB): M * N must not
+//     exceed it, otherwise the call returns SB_ERR_WORKSPACE before launching;
+//   * every GPU that loads the library holds this array until the process
+//     exits;
+//   * all calls share the one array and it keeps the previous call's
+//     contents; nothing needs clearing, because the GEMM pass overwrites all
+//     M * N values before the row pass reads them;
+//   * calls whose kernels overlap on the GPU (different streams, or several
+//     host threads) race on the array -- serialise them;
+//   * the first call on a device resolves the array's device address with
+//     cudaGetSymbolAddress (once per device, with that device current); make
+//     that first call before any stream capture.
+// ---------------------------------------------------------------------------
+namespace sb {
+namespace {
+constexpr size_t kNoAllocScratchFloats = size_t(32) << 20 >> 2;  // 32 MiB of fp32
+static __device__ __align__(256) float g_noalloc_scratch[kNoAllocScratchFloats];
+
+int noalloc_scratch_address(float** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return fail(SB_ERR_CUDA, std::string("cudaGetDevice: ") + cudaGetErrorString(e));
+  if (dev < 0 || dev >= 64) return fail(SB_ERR_DEVICE, "device ordinal out of range");
+  static float* addr[64];
+  static cudaError_t status[64];
+  static std::once_flag once[64];
+  std::call_once(once[dev], [&]() {
+    void* p = nullptr;
+    status[dev] = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    addr[dev] = static_cast<float*>(p);
+  });
+  if (status[dev] != cudaSuccess || addr[dev] == nullptr)
+    return fail(SB_ERR_CUDA, std::string("cudaGetSymbolAddress(no-alloc scratch): ") +
+                                 cudaGetErrorString(status[dev]));
+  *out = addr[dev];
+  return SB_OK;
+}
+}  // namespace
+}  // namespace sb
+
+extern "C" int sb_strassen_gemm_norm_residual_noalloc(sb_stream_t stream_, const void* a, const void* b,
+                                                      void* c, int64_t m, int64_t n, int64_t k,
+                                                      int64_t lda, int64_t ldb, int64_t ldc, int32_t bm,
+                                                      int32_t bn, int32_t bk, const sb_epilogue* ep) {
+  cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_);
+  if (!ep || ep->kind != SB_EPI_NORM_RESIDUAL_ADD)
+    return fail(SB_ERR_EPILOGUE, "the no-allocation entry point runs the norm_residual_add epilogue only");
+  int st = validate_core(a, b, c, m, n, k, lda, ldb, ldc, bm, bn, bk, SB_BF16);
+  if (st != SB_OK) return st;
+  if (!ep->residual || !aligned16(ep->residual) || ep->ld_residual % 8 || ep->ld_residual < n)
+    return fail(SB_ERR_EPILOGUE, "residual must be a 16-byte aligned [M, N] array with ld % 8 == 0");
+  if (!ep->norm_scale) return fail(SB_ERR_EPILOGUE, "norm_residual_add requires residual= and norm_scale=");
+  if (bn != n)
+    return fail(SB_ERR_EPILOGUE, "norm_residual_add normalises over the whole output row, so the tile must "
+                                 "span it: bn=" + std::to_string(bn) + " must equal n=" + std::to_string(n));
+  if (ldc < n) return fail(SB_ERR_ALIGNMENT, "ldc must be >= N");
+  if ((uint64_t)m * (uint64_t)n > kNoAllocScratchFloats)
+    return fail(SB_ERR_WORKSPACE, "M*N=" + std::to_string((uint64_t)m * (uint64_t)n) +
+                                      " exceeds the no-allocation scratch capacity of " +
+                                      std::to_string(kNoAllocScratchFloats) + " fp32 values (32 MiB)");
+  st = check_device();
+  if (st != SB_OK) return st;
+  float* scratch = nullptr;
+  st = noalloc_scratch_address(&scratch);
+  if (st != SB_OK) return st;
+  CUtensorMap ta, tb;
+  st = make_maps(a, b, m, n, k, lda, ldb, bm, StrassenPipe::BK, &ta, &tb);
+  if (st != SB_OK) return st;
+  GemmParams p = base_params(m, n, k, bm, bn, bk, scratch, n, StrassenPipe::BK);
+  st = dispatch(true, SB_EPI_NONE, true, stream, ta, tb, p);
+  if (st != SB_OK) return st;
+  norm_residual_rows_kernel<<<(unsigned)m, 256, 0, stream>>>(
+      scratch, n, ep->norm_scale, ep->aux_dtype == SB_F32, ep->residual, ep->ld_residual,
+      ep->residual_dtype == SB_F32, ep->norm_eps, reinterpret_cast<__nv_bfloat16*>(c), ldc);
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return fail(SB_ERR_CUDA, std::string("norm rows launch: ") + cudaGetErrorString(e));
+  return SB_OK;
+}
+
+extern "C" {
+
 int sb_classical_gemm(sb_stream_t stream_, const void* a, const void* b, void* c, int64_t m,
                       int64_t n, int64_t k, int64_t lda, int64_t ldb, int64_t ldc, int32_t bm,
                       int32_t bn, int32_t bk, int32_t out_dtype) {
