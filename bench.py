@@ -50,6 +50,12 @@ def parse():
     p.add_argument("--no-cpu-baseline", action="store_true",
                    help="skip the CPU oracle timing (used for ncu captures)")
     p.add_argument("--no-e2e", action="store_true", help="skip the host-buffer end-to-end loop")
+    p.add_argument("--workload", default="gemm", choices=["gemm", "qwen3-8b", "qwen3-32b"],
+                   help="gemm: the 8192^3 Strassen GEMM (default, the driver's line); "
+                        "qwen3-*: tensor-parallel decoder prefill tokens/s (BASELINE configs 4/5)")
+    p.add_argument("--backend", default="strassen", choices=["strassen", "native"],
+                   help="decoder GEMM sites: sm_100a Strassen kernels or the cuBLAS classical arm")
+    p.add_argument("--layers", type=int, default=None, help="decoder layers (default: the model's)")
     return p.parse_args()
 
 
@@ -333,10 +339,101 @@ def run_ours(args):
     return 0
 
 
+# --------------------------------------------------------------- decoder arm
+def run_decoder(args):
+    """Qwen3 prefill at TP = world size: tokens/s (strong scaling), max over ranks."""
+    import torch
+    import torch.distributed as dist
+
+    from strassen_tpu_b200 import qwen3
+
+    rank, world, local = dist_env()
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=device)
+    cfg, (batch, seq) = ({"qwen3-8b": (qwen3.QWEN3_8B, (8, 2048)),
+                          "qwen3-32b": (qwen3.QWEN3_32B, (16, 4096))}[args.workload])
+    tp = qwen3.TensorParallel()
+    model = qwen3.Qwen3Prefill(cfg, tp, device, backend=args.backend, layers=args.layers)
+    g = torch.Generator().manual_seed(20260911)
+    tokens_host = torch.randint(0, cfg.vocab, (batch, seq), generator=g).pin_memory()
+    tokens = tokens_host.to(device)
+    rope = model.rope(batch, seq)
+    stream = torch.cuda.current_stream(device)
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[local])
+
+    def max_over_ranks(x):
+        if world == 1:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    def timed(fn, steps, warmup):
+        for _ in range(warmup):
+            fn()
+        barrier()
+        torch.cuda.synchronize(device)
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record(stream)
+        for _ in range(steps):
+            fn()
+        e.record(stream)
+        torch.cuda.synchronize(device)
+        barrier()
+        return max_over_ranks(s.elapsed_time(e))
+
+    with ClockSampler(device.index) as clocks:
+        ms = timed(lambda: model.forward(tokens, rope), args.steps, args.warmup) / args.steps
+    logits_host = torch.empty(batch, cfg.vocab, dtype=torch.bfloat16).pin_memory()
+
+    def e2e_step():
+        t = tokens_host.to(device, non_blocking=True)
+        logits_host.copy_(model.forward(t, rope), non_blocking=True)
+
+    e2e_ms = timed(e2e_step, max(2, args.steps // 2), 1) / max(2, args.steps // 2)
+    n_layers = len(model.blocks)
+    flops = qwen3.prefill_flops(cfg, batch, seq, n_layers)
+    strassen_sites = sorted(k for k, v in model.blocks[0].sites.items() if v.strassen)
+    launches = 0
+    if args.backend == "strassen":
+        launches = n_layers * (2 + len(strassen_sites))  # two RMSNorm rows + one GEMM per site
+    if world > 1:
+        barrier()
+        dist.destroy_process_group()
+    if rank != 0:
+        return 0
+    tok = batch * seq
+    line = {
+        "metric": f"{args.workload.replace('-', '_')}_prefill_tokens_per_s", "value": tok / (ms * 1e-3),
+        "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": ms, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+        "dtype": "bf16", "data": "synthetic (uniform token ids, random N(0,0.02) weights)",
+        "config": {"workload": args.workload, "model": args.workload, "global_batch": batch,
+                   "seq_len": seq, "layers": n_layers, "parallelism": f"tp{world}",
+                   "backend": args.backend, "strassen_sites": strassen_sites,
+                   "lm_head": "last position per sequence"},
+        "achieved_tflops": flops / (ms * 1e-3) / 1e12,
+        "e2e": {"value": tok / (e2e_ms * 1e-3), "unit": "tokens/s",
+                "h2d_bytes_per_step": tok * 8, "d2h_bytes_per_step": batch * cfg.vocab * 2},
+        "clocks": clocks.summary(),
+        "gpu_launches": launches * args.steps,
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
 def main():
     args = parse()
     if args.impl == "reference":
         return run_reference(args)
+    if args.workload != "gemm":
+        return run_decoder(args)
     return run_ours(args)
 
 

@@ -1,0 +1,320 @@
+"""Qwen3 dense decoder prefill -- the caller of the Strassen operator, tensor-parallel.
+
+Mirrors the reference's Qwen3 block composition
+(experiments/qwen3/benchmark_qwen3_32b_layer.py:344-398,
+benchmark_qwen3_32b_full_layer_product_inference.py:138-176): RMSNorm -> q/k
+projections with the fused per-head RMSNorm + RoPE epilogue -> v -> causal
+attention -> o projection + residual -> RMSNorm -> gate/up projection with the
+fused SwiGLU epilogue -> down projection + residual.  Attention itself is not on
+the hot path (torch SDPA, as the reference uses XLA's dot_product_attention).
+
+Tensor parallelism over ``torch.distributed`` (NCCL on B200, gloo for CPU tests):
+q/k/v/gate/up are split by output columns (whole heads / whole SwiGLU channel
+pairs per rank), o/down by input rows; the o and down partial outputs are summed
+with one all-reduce each.  Rank 0 fuses the residual into its o/down GEMM
+epilogue, so the all-reduce adds it exactly once.
+
+Backends: ``"strassen"`` runs every eligible site on the sm_100a kernels
+(strassen_matmul with the reference's fused epilogues, rms_norm row kernel);
+``"native"`` is the reference's XLA-classical arm (torch.matmul = cuBLAS on GPU,
+unfused torch math) and is also what the CPU multi-process tests run.  A site
+whose per-rank width cannot satisfy the reference's tile rules (e.g. k at TP=8:
+one 128-wide kv head, below bn = 2*head_dim) uses the native arm for that site,
+the same per-site choice the reference's harness makes.
+
+Weights are random (N(0, 0.02); norm weights 1 + N(0, 0.02)) from per-tensor
+seeds: every rank generates the same full tensor and keeps its shard.
+"""
+
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass, field
+
+import torch
+import torch.nn.functional as F
+
+from . import layouts
+from . import strassen as sp
+
+
+@dataclass(frozen=True)
+class Qwen3Config:
+    hidden: int
+    layers: int
+    heads: int
+    kv_heads: int
+    head_dim: int
+    intermediate: int
+    vocab: int = 151936
+    rope_theta: float = 1e6
+    rms_eps: float = 1e-6
+
+
+# BASELINE.json configs 4 and 5, plus a small shape for tests.
+QWEN3_8B = Qwen3Config(hidden=4096, layers=36, heads=32, kv_heads=8, head_dim=128, intermediate=12288)
+QWEN3_32B = Qwen3Config(hidden=5120, layers=64, heads=64, kv_heads=8, head_dim=128, intermediate=25600)
+QWEN3_TINY = Qwen3Config(hidden=512, layers=2, heads=8, kv_heads=4, head_dim=64, intermediate=1024,
+                         vocab=1000)
+
+
+@dataclass(frozen=True)
+class StrassenTiles:
+    """The reference's per-site (bm, bn, bk) choices; bn is capped per site so it
+    divides the rank-local width."""
+
+    bm: int = 1024
+    bk: int = 512
+    qk_bn: int = 1024
+    up_bn: int = 1024
+    bn: int = 1024
+
+
+class TensorParallel:
+    """Rank, world size and the one collective the decoder needs."""
+
+    def __init__(self, group=None):
+        import torch.distributed as dist
+        self.dist = dist if dist.is_available() and dist.is_initialized() else None
+        self.group = group
+        self.rank = self.dist.get_rank(group) if self.dist else 0
+        self.world = self.dist.get_world_size(group) if self.dist else 1
+
+    def all_reduce(self, x: torch.Tensor) -> torch.Tensor:
+        if self.world > 1:
+            self.dist.all_reduce(x, group=self.group)
+        return x
+
+
+def _pick_bn(width: int, preferred: int, minimum: int) -> int | None:
+    """Largest bn <= preferred that is a multiple of `minimum` and of 256 and divides width."""
+    bn = preferred
+    while bn >= max(minimum, 256):
+        if width % bn == 0 and bn % 256 == 0 and bn % minimum == 0:
+            return bn
+        bn //= 2
+    return None
+
+
+def _randn(shape, seed, device, scale=0.02, offset=0.0):
+    g = torch.Generator(device=device)
+    g.manual_seed(seed)
+    w = torch.randn(shape, generator=g, device=device, dtype=torch.float32)
+    return (w * scale + offset).to(torch.bfloat16)
+
+
+def rms_norm_torch(x, scale, eps):
+    """benchmark_qwen3_32b_layer.py:270-276 in torch (fp32 math, bf16 out)."""
+    x32 = x.float()
+    return (x32 * torch.rsqrt((x32 * x32).mean(-1, keepdim=True) + eps) * scale.float()).to(torch.bfloat16)
+
+
+def apply_rope_torch(x, cos, sin):
+    """benchmark_qwen3_32b_layer.py:278-284: rotate-half RoPE in fp32. x [T, H, D], cos/sin [T, D]."""
+    x32 = x.float()
+    first, second = x32.chunk(2, dim=-1)
+    rotated = torch.cat((-second, first), dim=-1)
+    return (x32 * cos[:, None, :].float() + rotated * sin[:, None, :].float()).to(torch.bfloat16)
+
+
+def rope_tables(positions: torch.Tensor, cfg: Qwen3Config):
+    """bf16 cos/sin [len(positions), head_dim] (benchmark_qwen3_32b_layer.py:258-267)."""
+    hd = cfg.head_dim
+    inv = 1.0 / (cfg.rope_theta ** (torch.arange(0, hd, 2, dtype=torch.float32,
+                                                  device=positions.device) / hd))
+    ang = positions.float()[:, None] * inv[None, :]
+    ang = torch.cat((ang, ang), dim=-1)
+    return torch.cos(ang).to(torch.bfloat16), torch.sin(ang).to(torch.bfloat16)
+
+
+@dataclass
+class _Site:
+    weight: torch.Tensor          # [K, N_rank] as the site's GEMM consumes it
+    strassen: bool
+    bn: int | None = None
+
+
+@dataclass
+class Qwen3Layer:
+    cfg: Qwen3Config
+    tp: TensorParallel
+    backend: str
+    tiles: StrassenTiles
+    ln1: torch.Tensor = None
+    ln2: torch.Tensor = None
+    q_norm: torch.Tensor = None
+    k_norm: torch.Tensor = None
+    sites: dict = field(default_factory=dict)
+
+    @property
+    def heads_rank(self):
+        return self.cfg.heads // self.tp.world
+
+    @property
+    def kv_rank(self):
+        return self.cfg.kv_heads // self.tp.world
+
+    @property
+    def inter_rank(self):
+        return self.cfg.intermediate // self.tp.world
+
+
+def build_layer(cfg: Qwen3Config, index: int, tp: TensorParallel, device, backend="strassen",
+                tiles: StrassenTiles = StrassenTiles(), seed: int = 20260910) -> Qwen3Layer:
+    """Random-init layer `index`, sharded for this rank and laid out for the fused epilogues."""
+    if cfg.heads % tp.world or cfg.kv_heads % tp.world or cfg.intermediate % tp.world:
+        raise ValueError(f"tensor parallel size {tp.world} does not divide heads/kv heads/intermediate")
+    hd, r, w = cfg.head_dim, tp.rank, tp.world
+    base = seed + 1000 * index
+    layer = Qwen3Layer(cfg=cfg, tp=tp, backend=backend, tiles=tiles)
+    layer.ln1 = _randn((cfg.hidden,), base + 1, device, offset=1.0)
+    layer.ln2 = _randn((cfg.hidden,), base + 2, device, offset=1.0)
+    layer.q_norm = _randn((hd,), base + 3, device, offset=1.0)
+    layer.k_norm = _randn((hd,), base + 4, device, offset=1.0)
+    hq, hkv, ir = cfg.heads // w, cfg.kv_heads // w, cfg.intermediate // w
+    use = backend == "strassen"
+
+    def cols(full, lo, hi):
+        return full[:, lo:hi].contiguous()
+
+    wq = cols(_randn((cfg.hidden, cfg.heads * hd), base + 10, device), r * hq * hd, (r + 1) * hq * hd)
+    wk = cols(_randn((cfg.hidden, cfg.kv_heads * hd), base + 11, device), r * hkv * hd, (r + 1) * hkv * hd)
+    wv = cols(_randn((cfg.hidden, cfg.kv_heads * hd), base + 12, device), r * hkv * hd, (r + 1) * hkv * hd)
+    wo = _randn((cfg.heads * hd, cfg.hidden), base + 13, device)[r * hq * hd:(r + 1) * hq * hd].contiguous()
+    wg = cols(_randn((cfg.hidden, cfg.intermediate), base + 14, device), r * ir, (r + 1) * ir)
+    wu = cols(_randn((cfg.hidden, cfg.intermediate), base + 15, device), r * ir, (r + 1) * ir)
+    wd = _randn((cfg.intermediate, cfg.hidden), base + 16, device)[r * ir:(r + 1) * ir].contiguous()
+
+    for name, wt in (("q", wq), ("k", wk)):
+        bn = _pick_bn(wt.shape[1], tiles.qk_bn, 2 * hd) if use else None
+        if bn is not None:
+            layer.sites[name] = _Site(layouts.rope_weight_layout(wt, bn, head_dim=hd), True, bn)
+        else:
+            layer.sites[name] = _Site(wt, False)
+    bn = _pick_bn(wv.shape[1], tiles.bn, 256) if use else None
+    layer.sites["v"] = _Site(wv, bn is not None, bn)
+    bn = _pick_bn(cfg.hidden, tiles.bn, 256) if use and wo.shape[0] % tiles.bk == 0 else None
+    layer.sites["o"] = _Site(wo, bn is not None, bn)
+    gate_up = torch.cat([wg, wu], dim=1)
+    bn = _pick_bn(2 * ir, tiles.up_bn, 256) if use else None
+    if bn is not None and ir % (bn // 2) == 0:
+        layer.sites["up"] = _Site(layouts.swiglu_weight_layout(gate_up, bn), True, bn)
+    else:
+        layer.sites["up"] = _Site(gate_up, False)
+    bn = _pick_bn(cfg.hidden, tiles.bn, 256) if use and ir % tiles.bk == 0 else None
+    layer.sites["down"] = _Site(wd, bn is not None, bn)
+    return layer
+
+
+def _qk(layer: Qwen3Layer, name: str, h, heads, norm_w, cos, sin, cos_laid, sin_laid):
+    cfg = layer.cfg
+    site = layer.sites[name]
+    t = h.shape[0]
+    if site.strassen:
+        bn = site.bn
+        scale = layouts.rope_scale_layout(norm_w, bn, head_dim=cfg.head_dim)
+        c, s = cos_laid[bn], sin_laid[bn]
+        flat = sp.strassen_matmul(h, site.weight, bm=layer.tiles.bm, bn=bn, bk=layer.tiles.bk,
+                                  epilogue="qk_norm_rope", rope_cos=c, rope_sin=s, rope_scale=scale,
+                                  rope_head_dim=cfg.head_dim, rope_eps=cfg.rms_eps)
+        return layouts.rope_layout_to_heads(flat, heads, bn, head_dim=cfg.head_dim)
+    x = sp.native_matmul(h, site.weight).view(t, heads, cfg.head_dim)
+    x = rms_norm_torch(x, norm_w, cfg.rms_eps)
+    return apply_rope_torch(x, cos, sin)
+
+
+def _plain(layer: Qwen3Layer, name: str, h, residual=None):
+    site = layer.sites[name]
+    if site.strassen:
+        kw = {}
+        if residual is not None:
+            kw = dict(epilogue="residual_add", residual=residual)
+        return sp.strassen_matmul(h, site.weight, bm=layer.tiles.bm, bn=site.bn, bk=layer.tiles.bk, **kw)
+    out = sp.native_matmul(h, site.weight)
+    if residual is not None:
+        out = (out.float() + residual.float()).to(torch.bfloat16)
+    return out
+
+
+def layer_forward(layer: Qwen3Layer, x: torch.Tensor, batch: int, seq: int, rope) -> torch.Tensor:
+    """One decoder block on x [batch*seq, hidden] (bf16); returns the new hidden state."""
+    cfg, tp = layer.cfg, layer.tp
+    cos, sin, cos_laid, sin_laid = rope
+    norm = sp.rms_norm if layer.backend == "strassen" else (lambda a, b, eps: rms_norm_torch(a, b, eps))
+    h = norm(x, layer.ln1, cfg.rms_eps)
+    hq, hkv, hd = layer.heads_rank, layer.kv_rank, cfg.head_dim
+    q = _qk(layer, "q", h, hq, layer.q_norm, cos, sin, cos_laid, sin_laid)
+    k = _qk(layer, "k", h, hkv, layer.k_norm, cos, sin, cos_laid, sin_laid)
+    v = _plain(layer, "v", h).view(-1, hkv, hd)
+    q4 = q.view(batch, seq, hq, hd).transpose(1, 2)
+    k4 = k.view(batch, seq, hkv, hd).transpose(1, 2)
+    v4 = v.view(batch, seq, hkv, hd).transpose(1, 2)
+    if hkv != hq:
+        rep = hq // hkv
+        k4 = k4.repeat_interleave(rep, dim=1)
+        v4 = v4.repeat_interleave(rep, dim=1)
+    attn = F.scaled_dot_product_attention(q4, k4, v4, is_causal=True)
+    attn = attn.transpose(1, 2).reshape(batch * seq, hq * hd)
+    x1 = tp.all_reduce(_plain(layer, "o", attn, residual=x if tp.rank == 0 else None))
+    h2 = norm(x1, layer.ln2, cfg.rms_eps)
+    up = layer.sites["up"]
+    if up.strassen:
+        g = sp.strassen_matmul(h2, up.weight, bm=layer.tiles.bm, bn=up.bn, bk=layer.tiles.bk,
+                               epilogue="swiglu", product_aware_swiglu=True, interleave_products=True)
+    else:
+        gu = sp.native_matmul(h2, up.weight).float()
+        gate, upv = gu.chunk(2, dim=-1)
+        g = (F.silu(gate) * upv).to(torch.bfloat16)
+    return tp.all_reduce(_plain(layer, "down", g, residual=x1 if tp.rank == 0 else None))
+
+
+class Qwen3Prefill:
+    """Embedding -> N decoder blocks -> final norm -> last-position logits.
+
+    The LM head scores only the last position of each sequence (prefill serving
+    semantics); the vocabulary projection is replicated on every rank.
+    """
+
+    def __init__(self, cfg: Qwen3Config, tp: TensorParallel, device, backend="strassen",
+                 tiles: StrassenTiles = StrassenTiles(), layers: int | None = None, seed=20260910):
+        self.cfg, self.tp, self.device, self.backend = cfg, tp, device, backend
+        self.embed = _randn((cfg.vocab, cfg.hidden), seed, device)
+        self.final_norm = _randn((cfg.hidden,), seed + 7, device, offset=1.0)
+        self.lm_head = _randn((cfg.hidden, cfg.vocab), seed + 8, device)
+        n = cfg.layers if layers is None else layers
+        self.blocks = [build_layer(cfg, i, tp, device, backend, tiles, seed) for i in range(n)]
+
+    def rope(self, batch: int, seq: int):
+        pos = torch.arange(seq, device=self.device).repeat(batch)
+        cos, sin = rope_tables(pos, self.cfg)
+        cos_laid, sin_laid = {}, {}
+        for blk in self.blocks[:1]:
+            for site in ("q", "k"):
+                s = blk.sites[site]
+                if s.strassen and s.bn not in cos_laid:
+                    c, si = layouts.rope_layout_tables(cos, sin, s.bn // 2, head_dim=self.cfg.head_dim)
+                    cos_laid[s.bn], sin_laid[s.bn] = c.contiguous(), si.contiguous()
+        return cos, sin, cos_laid, sin_laid
+
+    def forward(self, tokens: torch.Tensor, rope=None) -> torch.Tensor:
+        """tokens [batch, seq] int64 -> logits [batch, vocab] of the last positions."""
+        batch, seq = tokens.shape
+        rope = rope if rope is not None else self.rope(batch, seq)
+        x = self.embed[tokens.reshape(-1)]
+        for blk in self.blocks:
+            x = layer_forward(blk, x, batch, seq, rope)
+        last = x.view(batch, seq, -1)[:, -1]
+        last = rms_norm_torch(last, self.final_norm, self.cfg.rms_eps)
+        return sp.native_matmul(last, self.lm_head)
+
+
+def prefill_flops(cfg: Qwen3Config, batch: int, seq: int, layers: int | None = None) -> float:
+    """GEMM + causal-attention FLOPs of one prefill (LM head on last positions only)."""
+    n = cfg.layers if layers is None else layers
+    t = batch * seq
+    hd = cfg.head_dim
+    gemm = 2 * t * cfg.hidden * (cfg.heads * hd + 2 * cfg.kv_heads * hd) \
+        + 2 * t * cfg.heads * hd * cfg.hidden + 2 * t * cfg.hidden * 2 * cfg.intermediate \
+        + 2 * t * cfg.intermediate * cfg.hidden
+    attn = 2 * 2 * batch * cfg.heads * hd * seq * seq / 2
+    return n * (gemm + attn) + 2 * batch * cfg.hidden * cfg.vocab

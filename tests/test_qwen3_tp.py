@@ -1,0 +1,126 @@
+"""Tensor-parallel Qwen3 decoder: sharding math and failure handling on CPU ranks.
+
+world_size-2 gloo process groups on 127.0.0.1 run the decoder with the native
+(classical) arm, so the column/row splits, the per-rank layouts and the
+residual-once all-reduce are checked without a GPU.  The failure test makes a
+rank die before its collective and checks that the survivor gets an error
+within the process-group timeout instead of hanging.
+"""
+
+from __future__ import annotations
+
+import os
+import socket
+import time
+from datetime import timedelta
+
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from strassen_tpu_b200 import qwen3
+
+CFG = qwen3.QWEN3_TINY
+BATCH, SEQ = 2, 32
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _tokens():
+    g = torch.Generator().manual_seed(5)
+    return torch.randint(0, CFG.vocab, (BATCH, SEQ), generator=g)
+
+
+def _tp_worker(rank, world, port, out_path):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=60))
+    try:
+        tp = qwen3.TensorParallel()
+        model = qwen3.Qwen3Prefill(CFG, tp, "cpu", backend="native")
+        logits = model.forward(_tokens())
+        if rank == 0:
+            torch.save(logits, out_path)
+    finally:
+        dist.destroy_process_group()
+
+
+def test_tp2_matches_tp1_on_cpu_ranks(tmp_path):
+    out = tmp_path / "tp2.pt"
+    mp.spawn(_tp_worker, args=(2, _free_port(), str(out)), nprocs=2, join=True)
+    tp2 = torch.load(out).float()
+    single = qwen3.Qwen3Prefill(CFG, qwen3.TensorParallel(), "cpu", backend="native")
+    tp1 = single.forward(_tokens()).float()
+    rel = (tp2 - tp1).norm() / tp1.norm()
+    assert rel < 3e-2, rel.item()
+
+
+def test_shards_partition_the_full_weights():
+    class FakeTP:
+        def __init__(self, rank, world):
+            self.rank, self.world = rank, world
+
+        def all_reduce(self, x):
+            return x
+
+    full = qwen3.build_layer(CFG, 0, FakeTP(0, 1), "cpu", backend="native")
+    parts = [qwen3.build_layer(CFG, 0, FakeTP(r, 2), "cpu", backend="native") for r in range(2)]
+    for name in ("q", "k", "v"):
+        joined = torch.cat([p.sites[name].weight for p in parts], dim=1)
+        assert torch.equal(joined, full.sites[name].weight), name
+    for name in ("o", "down"):
+        joined = torch.cat([p.sites[name].weight for p in parts], dim=0)
+        assert torch.equal(joined, full.sites[name].weight), name
+    # gate/up: each rank holds [gate_r | up_r]; together they are the full gate and up.
+    ir = CFG.intermediate
+    gate = torch.cat([p.sites["up"].weight[:, : ir // 2] for p in parts], dim=1)
+    up = torch.cat([p.sites["up"].weight[:, ir // 2:] for p in parts], dim=1)
+    assert torch.equal(gate, full.sites["up"].weight[:, :ir])
+    assert torch.equal(up, full.sites["up"].weight[:, ir:])
+
+
+def test_tp_size_must_divide_heads():
+    class FakeTP:
+        rank, world = 0, 3
+
+    with pytest.raises(ValueError, match="does not divide"):
+        qwen3.build_layer(CFG, 0, FakeTP(), "cpu", backend="native")
+
+
+def _dying_worker(rank, world, port, result_path):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=5))
+    if rank == 1:
+        os._exit(3)  # dies between steps, with nothing in flight
+    t0 = time.monotonic()
+    x = torch.ones(8)
+    try:
+        dist.all_reduce(x)
+        outcome = "completed"
+    except Exception as exc:  # the survivor must learn of the failure, not hang
+        outcome = f"error:{type(exc).__name__}"
+    with open(result_path, "w") as f:
+        f.write(f"{outcome} {time.monotonic() - t0:.1f}")
+    os._exit(0)
+
+
+def test_dead_rank_surfaces_as_an_error_not_a_hang(tmp_path):
+    result = tmp_path / "r0.txt"
+    ctx = mp.get_context("spawn")
+    port = _free_port()
+    procs = [ctx.Process(target=_dying_worker, args=(r, 2, port, str(result))) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=60)
+    alive = [p for p in procs if p.is_alive()]
+    for p in alive:
+        p.kill()
+    assert not alive, "a rank hung"
+    outcome, seconds = result.read_text().split()
+    assert outcome.startswith("error:"), outcome
+    assert float(seconds) < 30
