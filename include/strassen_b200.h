@@ -86,6 +86,22 @@ typedef struct sb_epilogue {
   float norm_eps;             /* default 1e-6                                      */
 } sb_epilogue;
 
+/* ---- research options (strassen_pallas.py:205-226, 381-517, 575-586) ------ */
+typedef enum sb_formula {
+  SB_FORMULA_CLASSICAL = 0,  /* Strassen's P1..P7, strassen_pallas.py:324-379   */
+  SB_FORMULA_DUAL = 1,       /* the dual rank-7 formula Q1..Q7, :466-517         */
+  SB_FORMULA_POWERS = 2      /* power-of-two formula R1..R7, :381-464 (not built) */
+} sb_formula;
+
+typedef struct sb_options {
+  int32_t formula_variant;        /* sb_formula                                     */
+  int32_t block_permutation;      /* bit 0 swaps M halves, bit 1 K halves, bit 2 N   */
+  /* Exact classical K panels: device int32 array [K/bk], nonzero = run that panel
+   * as eight exact sub-block products instead of Strassen (the reference's
+   * classical_panels / panel_schedule).  NULL = none. */
+  const int32_t* panel_schedule;
+} sb_options;
+
 /*
  * sb_strassen_gemm -- C = epilogue(A·B) with one tile-local Strassen level.
  *
@@ -105,6 +121,20 @@ SB_API int sb_strassen_gemm(sb_stream_t stream,
                      int32_t bm, int32_t bn, int32_t bk,
                      int32_t out_dtype, const sb_epilogue* ep,
                      void* workspace, size_t workspace_bytes);
+
+/*
+ * sb_strassen_gemm_ex -- sb_strassen_gemm with the reference's research options
+ * (formula_variant, block_permutation, classical_panels / panel_schedule of
+ * strassen_matmul, strassen_pallas.py:882-911).  opt == NULL is sb_strassen_gemm.
+ */
+SB_API int sb_strassen_gemm_ex(sb_stream_t stream,
+                               const void* a, const void* b, void* c,
+                               int64_t m, int64_t n, int64_t k,
+                               int64_t lda, int64_t ldb, int64_t ldc,
+                               int32_t bm, int32_t bn, int32_t bk,
+                               int32_t out_dtype, const sb_epilogue* ep,
+                               const sb_options* opt,
+                               void* workspace, size_t workspace_bytes);
 
 /* Scratch bytes sb_strassen_gemm needs for this problem (0 for most).
  * Replaces the reference's VMEM scratch_shapes sizing (strassen_pallas.py:1074-1078). */

@@ -76,6 +76,21 @@ INTERLEAVED_ORDER = (4, 6, 5, 2, 7, 3, 1)             # strassen_pallas.py:556-5
 PRODUCT_AWARE_SWIGLU_FINAL = (4, 5, 7, 3, 1, 6, 2)    # strassen_pallas.py:621-635
 PRODUCT_AWARE_RESIDUAL_FINAL = (4, 6, 5, 2, 7, 3, 1)  # strassen_pallas.py:671-682
 
+# The dual rank-7 formula Q1..Q7 (strassen_pallas.py:466-517), same layout as PRODUCTS.
+DUAL_PRODUCTS = {
+    1: (((0, 1), (3, 1)), ((0, 1), (3, 1)), ((0, 1), (3, 1))),
+    2: (((0, 1),), ((1, 1), (3, 1)), ((1, 1), (3, -1))),
+    3: (((2, 1), (3, -1)), ((0, 1),), ((2, 1), (3, 1))),
+    4: (((1, 1), (0, -1)), ((3, 1),), ((0, 1), (1, 1))),
+    5: (((3, 1),), ((0, 1), (2, 1)), ((0, -1), (2, 1))),
+    6: (((0, 1), (2, 1)), ((1, 1), (0, -1)), ((3, 1),)),
+    7: (((1, 1), (3, 1)), ((2, 1), (3, -1)), ((0, 1),)),
+}
+DUAL_PLAIN_ORDER = (1, 2, 3, 4, 5, 6, 7)              # strassen_pallas.py:549-556
+DUAL_INTERLEAVED_ORDER = (5, 6, 4, 3, 7, 2, 1)        # strassen_pallas.py:540-548
+# Exact eight-product panel (strassen_pallas.py:575-586): (output quadrant, A quadrant, B quadrant).
+EXACT_PANEL = ((0, 0, 0), (1, 0, 1), (2, 2, 0), (3, 2, 1), (0, 1, 2), (1, 1, 3), (2, 3, 2), (3, 3, 3))
+
 
 def _operand(quads, terms):
     """bf16 operand for a product: one quadrant, or a sum rounded once to bf16."""
@@ -102,39 +117,62 @@ def _split_b(b, bk, bn):
     return [np.ascontiguousarray(blocks[:, :, q // 2, q % 2]) for q in range(4)]
 
 
+def _permuted(index_row, index_col, swap_rows, swap_cols):
+    """strassen_pallas.py:210-211: quadrant index after swapping block halves."""
+    return 2 * (index_row ^ swap_rows) + (index_col ^ swap_cols)
+
+
 def strassen_accumulators(a, b, bm, bn, bk, *, interleave_products=False,
-                          final_order=None):
+                          final_order=None, formula_variant="classical", block_permutation=0,
+                          exact_panels=()):
     """fp32 quadrant accumulators acc[q][I, J, r, c] after all K panels.
 
     a, b: float32 arrays of bf16 values.  Reproduces the reference's per-panel
     accumulation (strassen_pallas.py:234-266, 519-573): at every panel P the
     products run in order and each updates its one or two quadrant
     accumulators.  ``final_order`` overrides the order on the last panel (the
-    product-aware schedules).
+    product-aware schedules).  ``formula_variant`` "classical" or "dual";
+    ``block_permutation`` swaps M/K/N block halves before the formula and maps
+    the quadrants back (strassen_pallas.py:205-226); panels in ``exact_panels``
+    run the exact eight-product update instead (strassen_pallas.py:575-586).
     """
     a = np.asarray(a, F32)
     b = np.asarray(b, F32)
     aq = _split_a(a, bm, bk)   # each [nI, nP, hm, hk]
     bq = _split_b(b, bk, bn)   # each [nP, nJ, hk, hn]
+    swap_m, swap_k, swap_n = (block_permutation & 1), (block_permutation >> 1) & 1, (block_permutation >> 2) & 1
+    aq = [aq[_permuted(r, c, swap_m, swap_k)] for r in range(2) for c in range(2)]
+    bq = [bq[_permuted(r, c, swap_k, swap_n)] for r in range(2) for c in range(2)]
+    out_index = [_permuted(r, c, swap_m, swap_n) for r in range(2) for c in range(2)]
     n_i, n_p = aq[0].shape[:2]
     n_j = bq[0].shape[1]
     hm, hn = bm // 2, bn // 2
-    order = INTERLEAVED_ORDER if interleave_products else PLAIN_ORDER
+    if formula_variant == "classical":
+        table, order = PRODUCTS, (INTERLEAVED_ORDER if interleave_products else PLAIN_ORDER)
+    elif formula_variant == "dual":
+        table, order = DUAL_PRODUCTS, (DUAL_INTERLEAVED_ORDER if interleave_products else DUAL_PLAIN_ORDER)
+    else:
+        raise NotImplementedError(formula_variant)
+    exact = set(int(x) for x in exact_panels)
     acc = [np.zeros((n_i, n_j, hm, hn), F32) for _ in range(4)]
     for p in range(n_p):
         ap = [x[:, p] for x in aq]         # [nI, hm, hk]
         bp = [x[p] for x in bq]            # [nJ, hk, hn]
+        if p in exact:
+            for q, ia, ib in EXACT_PANEL:
+                acc[out_index[q]] += np.matmul(ap[ia][:, None], bp[ib][None]).astype(F32)
+            continue
         this_order = final_order if (final_order is not None and p == n_p - 1) else order
         for idx in this_order:
-            a_terms, b_terms, updates = PRODUCTS[idx]
+            a_terms, b_terms, updates = table[idx]
             sa = _operand(ap, a_terms)
             sb = _operand(bp, b_terms)
             prod = np.matmul(sa[:, None], sb[None]).astype(F32)  # [nI, nJ, hm, hn]
             for q, sign in updates:
                 if sign > 0:
-                    acc[q] += prod
+                    acc[out_index[q]] += prod
                 else:
-                    acc[q] -= prod
+                    acc[out_index[q]] -= prod
     return acc
 
 
@@ -182,7 +220,8 @@ def strassen_matmul_ref(a, b, *, bm, bn, bk, interleave_products=False, epilogue
                         residual=None, bias=None, rope_cos=None, rope_sin=None, rope_scale=None,
                         rope_head_dim=128, rope_eps=1e-6, norm_scale=None, norm_eps=1e-6,
                         output_dtype="bfloat16", product_aware_swiglu=False,
-                        product_aware_residual=False):
+                        product_aware_residual=False, formula_variant="classical",
+                        block_permutation=0, classical_panels=(), panel_schedule=None):
     """Restatement of strassen_pallas.strassen_matmul for bf16 inputs.
 
     Returns a float32 array; for a bf16 output its values are bf16-rounded.
@@ -200,8 +239,12 @@ def strassen_matmul_ref(a, b, *, bm, bn, bk, interleave_products=False, epilogue
         final = PRODUCT_AWARE_SWIGLU_FINAL
     elif product_aware_residual:
         final = PRODUCT_AWARE_RESIDUAL_FINAL
+    exact = tuple(classical_panels)
+    if panel_schedule is not None:
+        exact = tuple(i for i, v in enumerate(np.asarray(panel_schedule).reshape(-1)) if v != 0)
     acc = strassen_accumulators(a, b, bm, bn, bk, interleave_products=interleave_products,
-                                final_order=final)
+                                final_order=final, formula_variant=formula_variant,
+                                block_permutation=block_permutation, exact_panels=exact)
     hm, hn = bm // 2, bn // 2
     n_i, n_j = m // bm, n // bn
     if epilogue is None:

@@ -42,10 +42,24 @@ class SbEpilogue(ctypes.Structure):
     ]
 
 
+class SbOptions(ctypes.Structure):
+    """Mirror of ``struct sb_options``."""
+
+    _fields_ = [
+        ("formula_variant", ctypes.c_int32),
+        ("block_permutation", ctypes.c_int32),
+        ("panel_schedule", ctypes.c_void_p),
+    ]
+
+
 SIGNATURES = {
     "sb_strassen_gemm": (_c_int, [_c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_i64, _c_i64, _c_i64,
                                   _c_i64, _c_i64, _c_i64, _c_int, _c_int, _c_int, _c_int,
                                   ctypes.POINTER(SbEpilogue), _c_ptr, _c_size]),
+    "sb_strassen_gemm_ex": (_c_int, [_c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_i64, _c_i64, _c_i64,
+                                     _c_i64, _c_i64, _c_i64, _c_int, _c_int, _c_int, _c_int,
+                                     ctypes.POINTER(SbEpilogue), ctypes.POINTER(SbOptions),
+                                     _c_ptr, _c_size]),
     "sb_workspace_bytes": (_c_size, [_c_i64, _c_i64, _c_i64, _c_int]),
     "sb_strassen_gemm_norm_residual_noalloc": (
         _c_int, [_c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_i64, _c_i64, _c_i64, _c_i64, _c_i64, _c_i64,
@@ -66,6 +80,7 @@ SB_OK = 0
 SB_ERR_UNSUPPORTED = 8
 SB_ERR_DEVICE_TIMEOUT = 13
 SB_BF16, SB_F32 = 0, 1
+FORMULAS = {"classical": 0, "dual": 1, "powers": 2}
 EPILOGUE_KINDS = {
     None: 0,
     "swiglu": 1,

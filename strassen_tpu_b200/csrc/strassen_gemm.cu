@@ -114,6 +114,7 @@ template <bool kStrassen>
 using PipeFor = typename std::conditional<kStrassen, StrassenPipe, ClassicalPipe>::type;
 
 constexpr uint32_t kIdesc = umma_idesc_bf16_f32(kBlockM, kBlockN, false, true);
+constexpr uint32_t kIdescNegA = kIdesc | (1u << 13);  // D (+)= -A * B
 
 // Operand slots inside a stage.  Raw tiles land in slots 0..3
 // (a0=A[top,left] a1=A[top,right] a2=A[bottom,left] a3=A[bottom,right];
@@ -126,6 +127,25 @@ constexpr uint32_t kIdesc = umma_idesc_bf16_f32(kBlockM, kBlockN, false, true);
 //   P5=(a0+a1)b3       P6=(a2-a0)(b0+b1)           P7=(a1-a3)(b2+b3)
 __constant__ int kASlot[7] = {4, 5, 0, 3, 1, 2, 6};
 __constant__ int kBSlot[7] = {4, 0, 1, 2, 3, 5, 6};
+// Dual formula (strassen_pallas.py:466-517), same in-place slot scheme:
+//   Q1=(a0+a3)(b0+b3)  Q2=a0(b1+b3)  Q3=(a2-a3)b0  Q4=(a1-a0)b3
+//   Q5=a3(b0+b2)       Q6=(a0+a2)(b1-b0)           Q7=(a1+a3)(b2-b3)
+//   A: 1 <- a1-a0  2 <- a2-a3  4 <- a0+a3  5 <- a0+a2  6 <- a1+a3
+//   B: 1 <- b1+b3  2 <- b0+b2  4 <- b0+b3  5 <- b1-b0  6 <- b2-b3
+__constant__ int kDualASlot[7] = {4, 0, 2, 1, 3, 5, 6};
+__constant__ int kDualBSlot[7] = {4, 1, 0, 3, 2, 5, 6};
+// Exact classical panel (strassen_pallas.py:575-586) expressed in the seven
+// accumulators, so the unchanged recombination yields C0 += a0b0+a1b2,
+// C1 += a0b1+a1b3, C2 += a2b0+a3b2, C3 += a2b1+a3b3:
+//   classical: acc6 += E0, acc2 += E1, acc1 += E2, acc5 += E3 - E1 + E2
+//   dual:      acc6 += E0, acc1 += E1, acc2 += E2, acc5 += E3 + E1 - E2
+// Entries: accumulator, A raw slot, B raw slot, negate (for the two formulas).
+__constant__ int kExactAcc[2][12] = {{6, 6, 2, 2, 1, 1, 5, 5, 5, 5, 5, 5},
+                                     {6, 6, 1, 1, 2, 2, 5, 5, 5, 5, 5, 5}};
+__constant__ int kExactA[12] = {0, 1, 0, 1, 2, 3, 2, 3, 0, 1, 2, 3};
+__constant__ int kExactB[12] = {0, 2, 1, 3, 0, 2, 1, 3, 1, 3, 0, 2};
+__constant__ int kExactNeg[2][12] = {{0, 0, 0, 0, 0, 0, 0, 0, 1, 1, 0, 0},
+                                     {0, 0, 0, 0, 0, 0, 0, 0, 0, 0, 1, 1}};
 // Classical control: C0+=a0b0, C0+=a1b2, C1+=a0b1, C1+=a1b3, C2+=a2b0, C2+=a3b2,
 // C3+=a2b1, C3+=a3b3 (strassen_pallas.py:575-586 order).
 __constant__ int kCAslot[8] = {0, 1, 0, 1, 2, 3, 2, 3};
@@ -153,7 +173,28 @@ struct GemmParams {
   float inv_head_dim;
   float eps;
   int* err;
+  // Research options (strassen_pallas.py:205-226, 466-517, 575-586).
+  int32_t formula;                 // 0 classical, 1 dual
+  int32_t swap_m, swap_k, swap_n;  // block_permutation bits
+  const int32_t* panel_schedule;   // device [num_panels], nonzero = exact panel; may be null
+  int32_t num_panels;
 };
+
+// Whether K chunk c lies in an exact classical panel.
+__device__ __forceinline__ bool exact_chunk(const GemmParams& p, int c, int chunk_k) {
+  if (p.panel_schedule == nullptr) return false;
+  const int panel = (c * chunk_k) / p.half_bk;
+  return __ldg(p.panel_schedule + panel) != 0;
+}
+
+// True when every K panel is exact: then accumulators 0, 3 and 4 are never
+// written (the exact schedule below only uses 1, 2, 5 and 6).
+__device__ __forceinline__ bool all_panels_exact(const GemmParams& p) {
+  if (p.panel_schedule == nullptr) return false;
+  for (int i = 0; i < p.num_panels; ++i)
+    if (__ldg(p.panel_schedule + i) == 0) return false;
+  return true;
+}
 
 __device__ int g_device_error = 0;
 
@@ -213,19 +254,56 @@ struct Quad8 {
   float c[4][8];
 };
 
-template <bool kStrassen>
-__device__ __forceinline__ void read_quadrants(uint32_t tmem_row, int col, Quad8& out) {
+template <bool kStrassen, bool kOpts>
+__device__ __forceinline__ void read_quadrants(uint32_t tmem_row, int col, Quad8& out,
+                                               const GemmParams& p, bool all_exact) {
   if constexpr (kStrassen) {
     float m[7][8];
 #pragma unroll
     for (int i = 0; i < 7; ++i) tmem_load_8(tmem_row + i * kBlockN + col, m[i]);
+    if (kOpts && all_exact) {
 #pragma unroll
-    for (int e = 0; e < 8; ++e) {
-      // strassen_pallas.py:324-379 quadrant updates, summed once.
-      out.c[0][e] = ((m[0][e] + m[3][e]) - m[4][e]) + m[6][e];
-      out.c[1][e] = m[2][e] + m[4][e];
-      out.c[2][e] = m[1][e] + m[3][e];
-      out.c[3][e] = ((m[0][e] - m[1][e]) + m[2][e]) + m[5][e];
+      for (int e = 0; e < 8; ++e) m[0][e] = m[3][e] = m[4][e] = 0.f;
+    }
+    if (!kOpts || p.formula == 0) {
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        // strassen_pallas.py:324-379 quadrant updates, summed once.
+        out.c[0][e] = ((m[0][e] + m[3][e]) - m[4][e]) + m[6][e];
+        out.c[1][e] = m[2][e] + m[4][e];
+        out.c[2][e] = m[1][e] + m[3][e];
+        out.c[3][e] = ((m[0][e] - m[1][e]) + m[2][e]) + m[5][e];
+      }
+    } else {
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        // Dual formula, strassen_pallas.py:466-517.
+        out.c[0][e] = ((m[0][e] + m[3][e]) - m[4][e]) + m[6][e];
+        out.c[1][e] = m[1][e] + m[3][e];
+        out.c[2][e] = m[2][e] + m[4][e];
+        out.c[3][e] = ((m[0][e] - m[1][e]) + m[2][e]) + m[5][e];
+      }
+    }
+    // block_permutation: the quadrant computed at (r, c) belongs at (r^swap_m, c^swap_n).
+    if (kOpts && p.swap_m) {
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        float t0 = out.c[0][e], t1 = out.c[1][e];
+        out.c[0][e] = out.c[2][e];
+        out.c[1][e] = out.c[3][e];
+        out.c[2][e] = t0;
+        out.c[3][e] = t1;
+      }
+    }
+    if (kOpts && p.swap_n) {
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        float t0 = out.c[0][e], t2 = out.c[2][e];
+        out.c[0][e] = out.c[1][e];
+        out.c[2][e] = out.c[3][e];
+        out.c[1][e] = t0;
+        out.c[3][e] = t2;
+      }
     }
   } else {
 #pragma unroll
@@ -233,7 +311,9 @@ __device__ __forceinline__ void read_quadrants(uint32_t tmem_row, int col, Quad8
   }
 }
 
-template <bool kStrassen, int kEpi, bool kOutF32>
+// kOpts compiles in the research options (dual formula, block permutation,
+// exact panels); the default launch uses the lean classical instantiation.
+template <bool kStrassen, int kEpi, bool kOutF32, bool kOpts>
 __global__ void __launch_bounds__(kThreads, 1)
     strassen_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a,
                          const __grid_constant__ CUtensorMap tmap_b, const GemmParams p) {
@@ -316,18 +396,24 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int panel = kap / p.half_bk;
         const int kin = kap - panel * p.half_bk;
         const uint32_t stage = smem_base + s * kStageBytes;
+        // Slot (2*qr + qk) of A holds the block's quadrant (qr^swap_m, qk^swap_k);
+        // slot (2*qk + qc) of B holds (qk^swap_k, qc^swap_n): the reference's
+        // block_permutation (strassen_pallas.py:205-226).
 #pragma unroll
+        const int swap_m = kOpts ? p.swap_m : 0;
+        const int swap_k = kOpts ? p.swap_k : 0;
+        const int swap_n = kOpts ? p.swap_n : 0;
         for (int qk = 0; qk < 2; ++qk) {
-          const int kcol = panel * p.bk + qk * p.half_bk + kin;
+          const int kcol = panel * p.bk + (qk ^ swap_k) * p.half_bk + kin;
 #pragma unroll
           for (int qr = 0; qr < 2; ++qr) {
             tma_load_3d(stage + (2 * qr + qk) * kASlotBytes, &tmap_a, fb, kcol,
-                        qr * p.half_bm + a_row_base, a_block);
+                        (qr ^ swap_m) * p.half_bm + a_row_base, a_block);
           }
 #pragma unroll
           for (int qc = 0; qc < 2; ++qc) {
             tma_load_2d(stage + kSlots * kASlotBytes + (2 * qk + qc) * kBSlotBytes, &tmap_b, fb,
-                        b_col0 + qc * p.half_bn, kcol);
+                        b_col0 + (qc ^ swap_n) * p.half_bn, kcol);
           }
         }
         last_issued[s] = c;
@@ -341,6 +427,14 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
+      uint32_t written = 0;  // accumulators that already hold a product (accumulate flag)
+      // Operand slot byte offsets of the seven products, resolved once.
+      uint32_t a_off[7], b_off[7];
+#pragma unroll
+      for (int i = 0; i < 7; ++i) {
+        a_off[i] = ((kOpts && p.formula != 0) ? kDualASlot[i] : kASlot[i]) * kASlotBytes;
+        b_off[i] = ((kOpts && p.formula != 0) ? kDualBSlot[i] : kBSlot[i]) * kBSlotBytes;
+      }
       for (int c = 0; c < p.num_chunks; ++c) {
         const int s = c % kStages;
         const uint32_t ph = (c / kStages) & 1u;
@@ -351,16 +445,33 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_after();
         const uint32_t a_stage = smem_base + s * kStageBytes;
         const uint32_t b_stage = a_stage + kSlots * kASlotBytes;
+        const bool exact = kStrassen && kOpts && exact_chunk(p, c, kBlockK);
 #pragma unroll
         for (int kk = 0; kk < kBlockK / 16; ++kk) {
           if constexpr (kStrassen) {
+            if (!exact) {
 #pragma unroll
-            for (int i = 0; i < 7; ++i) {
-              const uint64_t ad =
-                  umma_smem_desc(a_stage + kASlot[i] * kASlotBytes + kk * 32, P::A_LBO, P::A_SBO, P::A_LAYOUT);
-              const uint64_t bd = umma_smem_desc(b_stage + kBSlot[i] * kBSlotBytes + kk * 2048,
-                                                 P::B_LBO, P::B_SBO, P::B_LAYOUT);
-              umma_bf16_ss(tmem_base + i * kBlockN, ad, bd, kIdesc, (c | kk) != 0 ? 1u : 0u);
+              for (int i = 0; i < 7; ++i) {
+                const uint64_t ad = umma_smem_desc(a_stage + a_off[i] + kk * 32, P::A_LBO,
+                                                   P::A_SBO, P::A_LAYOUT);
+                const uint64_t bd = umma_smem_desc(b_stage + b_off[i] + kk * 2048,
+                                                   P::B_LBO, P::B_SBO, P::B_LAYOUT);
+                umma_bf16_ss(tmem_base + i * kBlockN, ad, bd, kIdesc, (written >> i) & 1u);
+              }
+              written = 0x7Fu;
+            } else {
+              // Exact classical panel on the raw quadrants (no operand sums).
+#pragma unroll
+              for (int e = 0; e < 12; ++e) {
+                const int acc = kExactAcc[p.formula][e];
+                const uint64_t ad = umma_smem_desc(a_stage + kExactA[e] * kASlotBytes + kk * 32,
+                                                   P::A_LBO, P::A_SBO, P::A_LAYOUT);
+                const uint64_t bd = umma_smem_desc(b_stage + kExactB[e] * kBSlotBytes + kk * 2048,
+                                                   P::B_LBO, P::B_SBO, P::B_LAYOUT);
+                umma_bf16_ss(tmem_base + acc * kBlockN, ad, bd,
+                             kExactNeg[p.formula][e] ? kIdescNegA : kIdesc, (written >> acc) & 1u);
+                written |= 1u << acc;
+              }
             }
           } else {
 #pragma unroll
@@ -393,31 +504,63 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         const uint32_t a_stage = smem_base + s * kStageBytes;
         const uint32_t b_stage = a_stage + kSlots * kASlotBytes;
+        if (kOpts && exact_chunk(p, c, kBlockK)) {
+          // Exact panels multiply the raw quadrants: leave them untouched.
+        } else if (!kOpts || p.formula == 0) {
 #pragma unroll
-        for (int idx = sum_tid; idx < kASlotBytes / 16; idx += kSumThreads) {
-          const uint32_t off = idx * 16;
-          const uint4 a0 = lds128(a_stage + 0 * kASlotBytes + off);
-          const uint4 a1 = lds128(a_stage + 1 * kASlotBytes + off);
-          const uint4 a2 = lds128(a_stage + 2 * kASlotBytes + off);
-          const uint4 a3 = lds128(a_stage + 3 * kASlotBytes + off);
-          sts128(a_stage + 4 * kASlotBytes + off, add4(a0, a3));
-          sts128(a_stage + 5 * kASlotBytes + off, add4(a2, a3));
-          sts128(a_stage + 6 * kASlotBytes + off, sub4(a1, a3));
-          sts128(a_stage + 1 * kASlotBytes + off, add4(a0, a1));
-          sts128(a_stage + 2 * kASlotBytes + off, sub4(a2, a0));
-        }
+          for (int idx = sum_tid; idx < kASlotBytes / 16; idx += kSumThreads) {
+            const uint32_t off = idx * 16;
+            const uint4 a0 = lds128(a_stage + 0 * kASlotBytes + off);
+            const uint4 a1 = lds128(a_stage + 1 * kASlotBytes + off);
+            const uint4 a2 = lds128(a_stage + 2 * kASlotBytes + off);
+            const uint4 a3 = lds128(a_stage + 3 * kASlotBytes + off);
+            sts128(a_stage + 4 * kASlotBytes + off, add4(a0, a3));
+            sts128(a_stage + 5 * kASlotBytes + off, add4(a2, a3));
+            sts128(a_stage + 6 * kASlotBytes + off, sub4(a1, a3));
+            sts128(a_stage + 1 * kASlotBytes + off, add4(a0, a1));
+            sts128(a_stage + 2 * kASlotBytes + off, sub4(a2, a0));
+          }
 #pragma unroll
-        for (int idx = sum_tid; idx < kBSlotBytes / 16; idx += kSumThreads) {
-          const uint32_t off = idx * 16;
-          const uint4 b0 = lds128(b_stage + 0 * kBSlotBytes + off);
-          const uint4 b1 = lds128(b_stage + 1 * kBSlotBytes + off);
-          const uint4 b2 = lds128(b_stage + 2 * kBSlotBytes + off);
-          const uint4 b3 = lds128(b_stage + 3 * kBSlotBytes + off);
-          sts128(b_stage + 4 * kBSlotBytes + off, add4(b0, b3));
-          sts128(b_stage + 5 * kBSlotBytes + off, add4(b0, b1));
-          sts128(b_stage + 6 * kBSlotBytes + off, add4(b2, b3));
-          sts128(b_stage + 1 * kBSlotBytes + off, sub4(b1, b3));
-          sts128(b_stage + 2 * kBSlotBytes + off, sub4(b2, b0));
+          for (int idx = sum_tid; idx < kBSlotBytes / 16; idx += kSumThreads) {
+            const uint32_t off = idx * 16;
+            const uint4 b0 = lds128(b_stage + 0 * kBSlotBytes + off);
+            const uint4 b1 = lds128(b_stage + 1 * kBSlotBytes + off);
+            const uint4 b2 = lds128(b_stage + 2 * kBSlotBytes + off);
+            const uint4 b3 = lds128(b_stage + 3 * kBSlotBytes + off);
+            sts128(b_stage + 4 * kBSlotBytes + off, add4(b0, b3));
+            sts128(b_stage + 5 * kBSlotBytes + off, add4(b0, b1));
+            sts128(b_stage + 6 * kBSlotBytes + off, add4(b2, b3));
+            sts128(b_stage + 1 * kBSlotBytes + off, sub4(b1, b3));
+            sts128(b_stage + 2 * kBSlotBytes + off, sub4(b2, b0));
+          }
+        } else {
+          // Dual formula operand sums (strassen_pallas.py:466-517).
+#pragma unroll
+          for (int idx = sum_tid; idx < kASlotBytes / 16; idx += kSumThreads) {
+            const uint32_t off = idx * 16;
+            const uint4 a0 = lds128(a_stage + 0 * kASlotBytes + off);
+            const uint4 a1 = lds128(a_stage + 1 * kASlotBytes + off);
+            const uint4 a2 = lds128(a_stage + 2 * kASlotBytes + off);
+            const uint4 a3 = lds128(a_stage + 3 * kASlotBytes + off);
+            sts128(a_stage + 4 * kASlotBytes + off, add4(a0, a3));
+            sts128(a_stage + 5 * kASlotBytes + off, add4(a0, a2));
+            sts128(a_stage + 6 * kASlotBytes + off, add4(a1, a3));
+            sts128(a_stage + 1 * kASlotBytes + off, sub4(a1, a0));
+            sts128(a_stage + 2 * kASlotBytes + off, sub4(a2, a3));
+          }
+#pragma unroll
+          for (int idx = sum_tid; idx < kBSlotBytes / 16; idx += kSumThreads) {
+            const uint32_t off = idx * 16;
+            const uint4 b0 = lds128(b_stage + 0 * kBSlotBytes + off);
+            const uint4 b1 = lds128(b_stage + 1 * kBSlotBytes + off);
+            const uint4 b2 = lds128(b_stage + 2 * kBSlotBytes + off);
+            const uint4 b3 = lds128(b_stage + 3 * kBSlotBytes + off);
+            sts128(b_stage + 4 * kBSlotBytes + off, add4(b0, b3));
+            sts128(b_stage + 5 * kBSlotBytes + off, sub4(b1, b0));
+            sts128(b_stage + 6 * kBSlotBytes + off, sub4(b2, b3));
+            sts128(b_stage + 1 * kBSlotBytes + off, add4(b1, b3));
+            sts128(b_stage + 2 * kBSlotBytes + off, add4(b0, b2));
+          }
         }
         // Make the generic-proxy writes visible to the tensor core, then signal.
         fence_proxy_async_smem();
@@ -442,6 +585,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int cp_base = u0 - j_block * p.half_bn;  // column inside the half block
       const int64_t col_left0 = (int64_t)j_block * p.bn + cp_base;
       const uint32_t tmem_row = tmem_base + ((uint32_t)(32 * q) << 16);
+      const bool all_exact = kStrassen && kOpts && all_panels_exact(p);
 
       if constexpr (kEpi == SB_EPI_QK_NORM_ROPE) {
         // Per-head sum of squares over both halves of every head
@@ -460,7 +604,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int j = 0; j < 4; ++j) {
           const int col = 32 * h + 8 * j;
           Quad8 v;
-          read_quadrants<kStrassen>(tmem_row, col, v);
+          read_quadrants<kStrassen, kOpts>(tmem_row, col, v, p, all_exact);
           const int slot = col / p.half_head;
           float st = 0.f, sbm = 0.f;
 #pragma unroll
@@ -480,7 +624,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int j = 0; j < 4; ++j) {
           const int col = 32 * h + 8 * j;
           Quad8 v;
-          read_quadrants<kStrassen>(tmem_row, col, v);
+          read_quadrants<kStrassen, kOpts>(tmem_row, col, v, p, all_exact);
           const int slot = col / p.half_head;
           const int cp = cp_base + col;
 #pragma unroll
@@ -512,7 +656,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int j = 0; j < 4; ++j) {
           const int col = 32 * h + 8 * j;
           Quad8 v;
-          read_quadrants<kStrassen>(tmem_row, col, v);
+          read_quadrants<kStrassen, kOpts>(tmem_row, col, v, p, all_exact);
           if (!row_ok) continue;
           const int64_t cl = col_left0 + col;
           const int64_t cr = cl + p.half_bn;
@@ -725,10 +869,10 @@ EncodeTiledFn encode_fn() {
 bool is_pow2(int64_t v) { return v > 0 && (v & (v - 1)) == 0; }
 bool aligned16(const void* ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15u) == 0; }
 
-template <bool kStrassen, int kEpi, bool kOutF32>
+template <bool kStrassen, int kEpi, bool kOutF32, bool kOpts>
 int launch_typed(cudaStream_t stream, const CUtensorMap& ta, const CUtensorMap& tb,
                  const GemmParams& p) {
-  auto kernel = strassen_gemm_kernel<kStrassen, kEpi, kOutF32>;
+  auto kernel = strassen_gemm_kernel<kStrassen, kEpi, kOutF32, kOpts>;
   static std::once_flag once;
   static cudaError_t attr_err = cudaSuccess;
   std::call_once(once, [&]() {
@@ -744,23 +888,33 @@ int launch_typed(cudaStream_t stream, const CUtensorMap& ta, const CUtensorMap& 
   return SB_OK;
 }
 
+template <bool kOpts>
+int dispatch_strassen(int epi, bool out_f32, cudaStream_t stream, const CUtensorMap& ta,
+                      const CUtensorMap& tb, const GemmParams& p) {
+  switch (epi) {
+    case SB_EPI_NONE:
+      return out_f32 ? launch_typed<true, SB_EPI_NONE, true, kOpts>(stream, ta, tb, p)
+                     : launch_typed<true, SB_EPI_NONE, false, kOpts>(stream, ta, tb, p);
+    case SB_EPI_SWIGLU: return launch_typed<true, SB_EPI_SWIGLU, false, kOpts>(stream, ta, tb, p);
+    case SB_EPI_GEGLU: return launch_typed<true, SB_EPI_GEGLU, false, kOpts>(stream, ta, tb, p);
+    case SB_EPI_RESIDUAL_ADD:
+      return launch_typed<true, SB_EPI_RESIDUAL_ADD, false, kOpts>(stream, ta, tb, p);
+    case SB_EPI_BIAS_ADD: return launch_typed<true, SB_EPI_BIAS_ADD, false, kOpts>(stream, ta, tb, p);
+    case SB_EPI_QK_NORM_ROPE:
+      return launch_typed<true, SB_EPI_QK_NORM_ROPE, false, kOpts>(stream, ta, tb, p);
+    default: return fail(SB_ERR_EPILOGUE, "unknown epilogue kind");
+  }
+}
+
 int dispatch(bool strassen, int epi, bool out_f32, cudaStream_t stream, const CUtensorMap& ta,
              const CUtensorMap& tb, const GemmParams& p) {
   if (!strassen) {
-    return out_f32 ? launch_typed<false, SB_EPI_NONE, true>(stream, ta, tb, p)
-                   : launch_typed<false, SB_EPI_NONE, false>(stream, ta, tb, p);
+    return out_f32 ? launch_typed<false, SB_EPI_NONE, true, false>(stream, ta, tb, p)
+                   : launch_typed<false, SB_EPI_NONE, false, false>(stream, ta, tb, p);
   }
-  switch (epi) {
-    case SB_EPI_NONE:
-      return out_f32 ? launch_typed<true, SB_EPI_NONE, true>(stream, ta, tb, p)
-                     : launch_typed<true, SB_EPI_NONE, false>(stream, ta, tb, p);
-    case SB_EPI_SWIGLU: return launch_typed<true, SB_EPI_SWIGLU, false>(stream, ta, tb, p);
-    case SB_EPI_GEGLU: return launch_typed<true, SB_EPI_GEGLU, false>(stream, ta, tb, p);
-    case SB_EPI_RESIDUAL_ADD: return launch_typed<true, SB_EPI_RESIDUAL_ADD, false>(stream, ta, tb, p);
-    case SB_EPI_BIAS_ADD: return launch_typed<true, SB_EPI_BIAS_ADD, false>(stream, ta, tb, p);
-    case SB_EPI_QK_NORM_ROPE: return launch_typed<true, SB_EPI_QK_NORM_ROPE, false>(stream, ta, tb, p);
-    default: return fail(SB_ERR_EPILOGUE, "unknown epilogue kind");
-  }
+  const bool opts = p.formula != 0 || p.swap_m || p.swap_k || p.swap_n || p.panel_schedule;
+  return opts ? dispatch_strassen<true>(epi, out_f32, stream, ta, tb, p)
+              : dispatch_strassen<false>(epi, out_f32, stream, ta, tb, p);
 }
 
 int check_device() {
@@ -883,6 +1037,15 @@ GemmParams base_params(int64_t m, int64_t n, int64_t k, int32_t bm, int32_t bn, 
   return p;
 }
 
+void apply_options(GemmParams& p, int formula, int perm, const int32_t* schedule) {
+  p.formula = formula == SB_FORMULA_DUAL ? 1 : 0;
+  p.swap_m = perm & 1;
+  p.swap_k = (perm >> 1) & 1;
+  p.swap_n = (perm >> 2) & 1;
+  p.panel_schedule = schedule;
+  p.num_panels = p.K / p.bk;
+}
+
 }  // namespace
 }  // namespace sb
 
@@ -900,12 +1063,30 @@ int sb_strassen_gemm(sb_stream_t stream_, const void* a, const void* b, void* c,
                      int64_t n, int64_t k, int64_t lda, int64_t ldb, int64_t ldc, int32_t bm,
                      int32_t bn, int32_t bk, int32_t out_dtype, const sb_epilogue* ep,
                      void* workspace, size_t workspace_bytes) {
+  return sb_strassen_gemm_ex(stream_, a, b, c, m, n, k, lda, ldb, ldc, bm, bn, bk, out_dtype, ep,
+                             nullptr, workspace, workspace_bytes);
+}
+
+int sb_strassen_gemm_ex(sb_stream_t stream_, const void* a, const void* b, void* c, int64_t m,
+                        int64_t n, int64_t k, int64_t lda, int64_t ldb, int64_t ldc, int32_t bm,
+                        int32_t bn, int32_t bk, int32_t out_dtype, const sb_epilogue* ep,
+                        const sb_options* opt, void* workspace, size_t workspace_bytes) {
   cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_);
   const int epi = ep ? ep->kind : SB_EPI_NONE;
   int st = validate_core(a, b, c, m, n, k, lda, ldb, ldc, bm, bn, bk, out_dtype);
   if (st != SB_OK) return st;
   if (epi < SB_EPI_NONE || epi > SB_EPI_NORM_RESIDUAL_ADD)
     return fail(SB_ERR_EPILOGUE, "unknown epilogue kind " + std::to_string(epi));
+  const int formula = opt ? opt->formula_variant : SB_FORMULA_CLASSICAL;
+  const int perm = opt ? opt->block_permutation : 0;
+  const int32_t* schedule = opt ? opt->panel_schedule : nullptr;
+  if (formula == SB_FORMULA_POWERS)
+    return fail(SB_ERR_UNSUPPORTED, "formula_variant='powers' is not built for B200");
+  if (formula != SB_FORMULA_CLASSICAL && formula != SB_FORMULA_DUAL)
+    return fail(SB_ERR_RANK, "formula_variant must be 'classical', 'dual', or 'powers'");
+  if (perm < 0 || perm > 7) return fail(SB_ERR_RANK, "block_permutation must be an integer from 0 through 7");
+  if (schedule && (reinterpret_cast<uintptr_t>(schedule) & 3u))
+    return fail(SB_ERR_ALIGNMENT, "panel_schedule must be a 4-byte aligned int32 device array");
   if (epi != SB_EPI_NONE && out_dtype != SB_BF16)
     return fail(SB_ERR_OUTPUT_DTYPE, "fused epilogues write a BF16 output tile");
   if ((epi == SB_EPI_SWIGLU || epi == SB_EPI_GEGLU) && (bn % 2))
@@ -950,6 +1131,7 @@ int sb_strassen_gemm(sb_stream_t stream_, const void* a, const void* b, void* c,
   if (epi == SB_EPI_NORM_RESIDUAL_ADD) {
     // Pass 1: fp32 pre-norm rows into the caller's workspace; pass 2: row norm.
     GemmParams p = base_params(m, n, k, bm, bn, bk, workspace, n, StrassenPipe::BK);
+    apply_options(p, formula, perm, schedule);
     st = dispatch(true, SB_EPI_NONE, true, stream, ta, tb, p);
     if (st != SB_OK) return st;
     norm_residual_rows_kernel<<<(unsigned)m, 256, 0, stream>>>(
@@ -962,6 +1144,7 @@ int sb_strassen_gemm(sb_stream_t stream_, const void* a, const void* b, void* c,
   }
 
   GemmParams p = base_params(m, n, k, bm, bn, bk, c, ldc, StrassenPipe::BK);
+  apply_options(p, formula, perm, schedule);
   if (ep) {
     p.residual = ep->residual;
     p.ldr = ep->ld_residual;

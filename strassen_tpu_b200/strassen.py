@@ -8,7 +8,10 @@ the TPU compiler (``dot_precision``, ``allow_input_fusion``,
 ``vmem_limit_bytes``, ``interleave_products``, ``product_aware_*``) are
 accepted and validated but do not change the B200 arithmetic, which keeps the
 seven products in separate fp32 TMEM accumulators over the whole K range and
-recombines them once.  ``bm``/``bn``/``bk`` keep their reference meaning: they
+recombines them once.  The research options ``formula_variant="dual"``,
+``block_permutation`` and exact classical panels (``classical_panels`` /
+``panel_schedule``) run on the same kernel; ``formula_variant="powers"`` is not
+built.  ``bm``/``bn``/``bk`` keep their reference meaning: they
 define the Strassen block whose quadrants are paired, so results follow the
 reference's pairing of operands.
 
@@ -23,7 +26,7 @@ import ctypes
 import torch
 
 from . import _native
-from ._native import SB_BF16, SB_F32, EPILOGUE_KINDS, SbEpilogue
+from ._native import SB_BF16, SB_F32, EPILOGUE_KINDS, FORMULAS, SbEpilogue, SbOptions
 
 LANE = 128
 SUBLANE = 8
@@ -215,6 +218,29 @@ def strassen_matmul(
     if residual is not None and epilogue == "residual_add" and tuple(residual.shape) != (m, n):
         raise ValueError(f"residual shape {tuple(residual.shape)} != output shape {(m, n)}")
 
+    nk = k // bk
+    if panel_schedule is not None:
+        schedule_shape = tuple(torch.as_tensor(panel_schedule).shape)
+        if schedule_shape != (nk,):
+            raise ValueError(f"panel_schedule must have shape ({nk},), got {schedule_shape}")
+    # Checks the reference makes while tracing its kernel (strassen_pallas.py:282-312).
+    if product_aware_swiglu and (
+            out_dt == torch.float32 or formula_variant != "classical" or block_permutation != 0
+            or (nk - 1) in classical_panels or panel_schedule is not None
+            or epilogue not in ("swiglu", "geglu")):
+        raise ValueError(
+            "product-aware SwiGLU requires unpermuted classical Strassen "
+            "with quadrant accumulators; exact panels are allowed except on "
+            "the final K panel, whose product order the schedule owns")
+    if product_aware_residual and (
+            out_dt == torch.float32 or formula_variant != "classical" or block_permutation != 0
+            or (nk - 1) in classical_panels or panel_schedule is not None
+            or epilogue != "residual_add"):
+        raise ValueError(
+            "product-aware residual requires unpermuted classical Strassen "
+            "with quadrant accumulators and the residual_add epilogue; exact "
+            "panels are allowed except on the final K panel")
+
     # --- what the B200 build does not implement (yet): refuse loudly.
     if interpret:
         raise NotImplementedError(
@@ -222,11 +248,8 @@ def strassen_matmul(
             "oracle/ and is test infrastructure only")
     if a.dtype != torch.bfloat16:
         raise NotImplementedError("the B200 kernel computes bf16 inputs; FP32 inputs are not built")
-    if formula_variant != "classical" or block_permutation != 0:
-        raise NotImplementedError(
-            "formula_variant/block_permutation research options are not built for B200")
-    if classical_panels or panel_schedule is not None:
-        raise NotImplementedError("exact classical K panels are not built for B200")
+    if formula_variant == "powers":
+        raise NotImplementedError("formula_variant='powers' is not built for B200")
     if not (a.is_cuda and b.is_cuda):
         raise ValueError("strassen_matmul runs on a CUDA device; got CPU tensors (no CPU fallback)")
 
@@ -278,6 +301,19 @@ def strassen_matmul(
         ep.norm_scale = prep_aux(norm_scale).data_ptr()
     ep.norm_eps = float(norm_eps)
 
+    opts = SbOptions()
+    opts.formula_variant = FORMULAS[formula_variant]
+    opts.block_permutation = int(block_permutation)
+    if classical_panels or panel_schedule is not None:
+        if panel_schedule is not None:
+            sched = torch.as_tensor(panel_schedule).to(device=device, dtype=torch.int32).contiguous()
+        else:
+            sched = torch.zeros(nk, dtype=torch.int32)
+            sched[list(classical_panels)] = 1
+            sched = sched.to(device)
+        keep_alive.append(sched)
+        opts.panel_schedule = sched.data_ptr()
+
     lib = _native.load()
     ws_bytes = int(lib.sb_workspace_bytes(m, n, k, ep.kind))
     ws_ptr = None
@@ -288,10 +324,10 @@ def strassen_matmul(
             raise ValueError(f"workspace must hold {ws_bytes} bytes")
         ws_ptr = workspace.data_ptr()
     with torch.cuda.device(device):
-        status = lib.sb_strassen_gemm(
+        status = lib.sb_strassen_gemm_ex(
             _stream_handle(device), a.data_ptr(), b.data_ptr(), out.data_ptr(),
             m, n, k, _ld(a), _ld(b), _ld(out), bm, bn, bk,
-            SB_F32 if out_dt == torch.float32 else SB_BF16, ctypes.byref(ep),
+            SB_F32 if out_dt == torch.float32 else SB_BF16, ctypes.byref(ep), ctypes.byref(opts),
             ws_ptr, ws_bytes)
     _native.check(status)
     return out

@@ -138,6 +138,15 @@ class _CompilerParams:
         self.kwargs = kwargs
 
 
+class _PrefetchScalarGridSpec:
+    def __init__(self, num_scalar_prefetch, grid, in_specs, out_specs, scratch_shapes=()):
+        self.num_scalar_prefetch = num_scalar_prefetch
+        self.grid = grid
+        self.in_specs = in_specs
+        self.out_specs = out_specs
+        self.scratch_shapes = scratch_shapes
+
+
 _GRID_STATE = {"ids": ()}
 
 
@@ -156,21 +165,28 @@ def _when(cond):
 def _pallas_call(kernel, *, grid=None, grid_spec=None, in_specs=None, out_specs=None,
                  out_shape=None, scratch_shapes=(), compiler_params=None, interpret=False,
                  **_unused):
+    n_prefetch = 0
     if grid_spec is not None:
-        raise NotImplementedError("prefetched grid specs are not needed for the golden cases")
+        # Scalar-prefetch grid: the first operands are passed whole to the kernel
+        # and appended to every index map's arguments.
+        n_prefetch = grid_spec.num_scalar_prefetch
+        grid, in_specs = grid_spec.grid, grid_spec.in_specs
+        out_specs, scratch_shapes = grid_spec.out_specs, grid_spec.scratch_shapes
 
     def run(*operands):
         out = np.zeros(out_shape.shape, out_shape.dtype)
         scratch = [np.zeros(s.shape, s.dtype) for s in scratch_shapes]
+        prefetch = [np.asarray(x) for x in operands[:n_prefetch]]
+        tensors = operands[n_prefetch:]
 
         def block(array, spec, ids):
-            idx = spec.index_map(*ids)
+            idx = spec.index_map(*ids, *prefetch)
             return array[tuple(slice(i * s, (i + 1) * s) for i, s in zip(idx, spec.block_shape))]
 
         for ids in np.ndindex(*grid):
             _GRID_STATE["ids"] = ids
-            in_refs = [block(np.asarray(x), spec, ids) for x, spec in zip(operands, in_specs)]
-            kernel(*in_refs, block(out, out_specs, ids), *scratch)
+            in_refs = [block(np.asarray(x), spec, ids) for x, spec in zip(tensors, in_specs)]
+            kernel(*prefetch, *in_refs, block(out, out_specs, ids), *scratch)
         return out
 
     return run
@@ -184,6 +200,7 @@ def install_stand_in():
         setattr(jnp, name, ml_dtypes.bfloat16)
     jnp.float32 = np.float32
     jnp.int32 = np.int32
+    jnp.asarray = _asarray
     jnp.dtype = np.dtype
     jnp.asarray = _asarray
     jnp.zeros = _zeros
@@ -218,6 +235,7 @@ def install_stand_in():
     tpu = types.ModuleType("jax.experimental.pallas.tpu")
     tpu.VMEM = _VMEM
     tpu.CompilerParams = _CompilerParams
+    tpu.PrefetchScalarGridSpec = _PrefetchScalarGridSpec
     pallas.tpu = tpu
     experimental.pallas = pallas
     jax.experimental = experimental
@@ -275,6 +293,27 @@ def cases():
          rope_head_dim=64)
     gemm("norm_residual_256x512x512", 256, 512, 512, (256, 512, 256), seed=47,
          epilogue="norm_residual_add")
+    # Research options: dual formula, block permutation, exact panels.
+    gemm("dual_512", 512, 512, 512, (256, 256, 256), seed=51, formula_variant="dual")
+    gemm("dual_interleaved_512", 512, 512, 512, (256, 256, 256), seed=52, formula_variant="dual",
+         interleave_products=True)
+    gemm("blockperm5_512", 512, 512, 512, (256, 256, 256), seed=53, block_permutation=5)
+    gemm("blockperm7_dual_f32", 256, 512, 512, (256, 256, 256), seed=54, block_permutation=7,
+         formula_variant="dual", output_dtype="float32")
+    gemm("exact_panels_0_2", 512, 1024, 512, (256, 256, 256), seed=55, classical_panels=(0, 2))
+    gemm("panel_schedule_1001", 512, 1024, 512, (256, 256, 256), seed=56,
+         panel_schedule=[1, 0, 0, 1])
+    gemm("panel_schedule_all", 256, 512, 256, (256, 256, 256), seed=57, panel_schedule=[1, 1])
+    gemm("int_exact_dual_perm3", 64, 1024, 512, (32, 256, 256), kind="int", seed=58,
+         classical_panels=(1,), formula_variant="dual", block_permutation=3,
+         output_dtype="float32")
+    gemm("swiglu_blockperm6", 512, 512, 1024, (256, 512, 256), seed=59, epilogue="swiglu",
+         block_permutation=6)
+    gemm("swiglu_product_aware_exact0", 512, 1024, 1024, (256, 512, 256), seed=60,
+         epilogue="swiglu", product_aware_swiglu=True, interleave_products=True,
+         classical_panels=(0,))
+    gemm("residual_dual_exact1", 256, 1024, 512, (256, 256, 512), seed=61,
+         epilogue="residual_add", formula_variant="dual", classical_panels=(1,))
     return out
 
 

@@ -95,12 +95,30 @@ def test_no_cpu_path():
 def test_unbuilt_reference_options_refuse_loudly():
     with pytest.raises(NotImplementedError, match="FP32 inputs"):
         call(*mats(dtype=torch.float32))
-    with pytest.raises(NotImplementedError):
-        call(formula_variant="dual")
-    with pytest.raises(NotImplementedError):
-        call(block_permutation=3)
-    with pytest.raises(NotImplementedError):
-        call(classical_panels=(0,))
+    with pytest.raises(NotImplementedError, match="powers"):
+        call(formula_variant="powers")
+
+
+def test_research_options_reach_the_device_check():
+    # dual / block_permutation / exact panels are built: on CPU tensors they
+    # fail only at the device check, after validation.
+    for kw in (dict(formula_variant="dual"), dict(block_permutation=3), dict(classical_panels=(0,)),
+               dict(panel_schedule=[1])):
+        with pytest.raises(ValueError, match="no CPU fallback"):
+            call(**kw)
+
+
+def test_product_aware_schedule_contract():
+    a, b = mats(256, 512, 512)
+    with pytest.raises(ValueError, match="product-aware SwiGLU requires unpermuted classical"):
+        call(a, b, bn=512, epilogue="swiglu", product_aware_swiglu=True, classical_panels=(1,))
+    with pytest.raises(ValueError, match="product-aware SwiGLU requires unpermuted classical"):
+        call(a, b, bn=512, epilogue="swiglu", product_aware_swiglu=True, block_permutation=1)
+    with pytest.raises(ValueError, match="product-aware residual requires"):
+        call(a, b, epilogue="residual_add", residual=torch.zeros(256, 512, dtype=BF),
+             product_aware_residual=True, formula_variant="dual")
+    with pytest.raises(ValueError, match="panel_schedule must have shape \\(2,\\)"):
+        call(a, b, panel_schedule=[1, 0, 1])
 
 
 def test_check_tiling_message():

@@ -46,14 +46,14 @@ def bf16_ulp(x):
 def assert_parity(got, want, exact=None, rounding_step=False):
     """got/want: float arrays; exact: fp64 yardstick for the 2x-error rule.
 
-    rounding_step=True (bf16 outputs of large GEMMs): an element may also differ
-    by exactly one bf16 rounding step of the reference value.  Both sides round
+    rounding_step=True (bf16 outputs): an element may also differ by exactly one
+    bf16 rounding step of the reference value, on at most 0.1% of elements.  Both sides round
     fp32 sums to bf16; when the fp32 summation order differs (it always does
     between a tensor-core kernel and a CPU oracle) an fp32 value near a rounding
     boundary lands on the neighbouring bf16 value.  At 8192^3 one such step at
-    |C| ~ 300 is 2.0 > 2e-2 * rms(C) = 1.8, so the fixed bar alone would reject
-    any correct implementation; the fp32-output comparison in the same test
-    keeps the strict bar on the unrounded values.
+    |C| ~ 300 is 2.0 > 2e-2 * rms(C) = 1.8, and heavy-tailed SwiGLU outputs
+    reach |y| ~ 4 rms at 512 wide, so the fixed bar alone would reject any
+    correct implementation; fp32-output comparisons keep the strict bar.
     """
     got = np.asarray(got, np.float64)
     want = np.asarray(want, np.float64)
@@ -62,8 +62,11 @@ def assert_parity(got, want, exact=None, rounding_step=False):
     rms = np.sqrt(np.mean(want ** 2))
     diff = np.abs(got - want)
     if rounding_step:
+        over = diff > MAX_ABS_REL_RMS * rms
         bad = diff > np.maximum(MAX_ABS_REL_RMS * rms, bf16_ulp(want) * (1 + 1e-9))
         assert not bad.any(), (diff.max(), rms, int(bad.sum()))
+        # single-step flips must stay rare
+        assert over.sum() <= max(1, 1e-3 * over.size), (int(over.sum()), over.size)
     else:
         assert diff.max() <= MAX_ABS_REL_RMS * rms, (diff.max(), rms)
     if exact is not None:
@@ -92,14 +95,13 @@ def fp64_yardstick(p, a, b, extra, rows):
                             rope_head_dim=kw.get("rope_head_dim", 128), **sub)
 
 
-GOLDEN_CASES = [
-    "config1_1024_plain", "interleaved_512x512x512", "int_16x256x256", "int_32x768x512",
-    "int_512x1024x512_f32", "normal_16x256x256_seed23", "normal_256x512x768_f32",
-    "normal_512x512x512_tile512", "normal_1024x512x256_bm64", "sentinel_256x512x256",
-    "swiglu_512x512x1024", "swiglu_product_aware", "geglu_256x512x512",
-    "residual_512x768x512", "residual_product_aware", "bias_256x512x512",
-    "qk_norm_rope_256x512x1024", "qk_norm_rope_hd64", "norm_residual_256x512x512",
-]
+def _golden_case_names():
+    import json
+    from conftest import GOLDEN
+    return sorted(json.loads((GOLDEN / "golden_cases.json").read_text())["cases"])
+
+
+GOLDEN_CASES = _golden_case_names()
 
 
 @pytest.mark.parametrize("case", GOLDEN_CASES)
@@ -116,7 +118,8 @@ def test_golden_case(golden, case):
         np.testing.assert_array_equal(got, want)
         return
     rows = slice(None, None, stride)
-    assert_parity(got, want, fp64_yardstick(p, a, b, extra, rows))
+    assert_parity(got, want, fp64_yardstick(p, a, b, extra, rows),
+                  rounding_step=p["output"] == "bf16_bits")
 
 
 def test_device_error_word_is_clear():
