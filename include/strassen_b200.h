@@ -175,6 +175,20 @@ SB_API int sb_strassen_gemm_norm_residual_noalloc(sb_stream_t stream,
                                                   const sb_epilogue* ep);
 
 /*
+ * sb_strassen_gemm_lhs_transposed -- C = A^T·B with A stored (K, M) row-major
+ * (leading dimension ldat >= M), without materialising the transpose.
+ * Replaces strassen_pallas.strassen_matmul_lhs_transposed
+ * (strassen_pallas.py:1224-1312): classical formula, no epilogue, bf16 or fp32
+ * output.  B200 restriction: bm must be a multiple of 128.
+ */
+SB_API int sb_strassen_gemm_lhs_transposed(sb_stream_t stream,
+                                           const void* at, const void* b, void* c,
+                                           int64_t m, int64_t n, int64_t k,
+                                           int64_t ldat, int64_t ldb, int64_t ldc,
+                                           int32_t bm, int32_t bn, int32_t bk,
+                                           int32_t out_dtype);
+
+/*
  * sb_rms_norm -- y = bf16(x * rsqrt(mean(x^2) + eps) * w), fp32 math.
  * Replaces the reference's rms_norm
  * (experiments/qwen3/benchmark_qwen3_32b_layer.py:270-276).  x, y: [rows, n]

@@ -309,6 +309,18 @@ def strassen_matmul_ref(a, b, *, bm, bn, bk, interleave_products=False, epilogue
     raise ValueError(f"unknown epilogue {epilogue!r}")
 
 
+def strassen_lhs_transposed_ref(at, b, *, bm, bn, bk, interleave_products=False,
+                                output_dtype="bfloat16"):
+    """Restatement of strassen_matmul_lhs_transposed (strassen_pallas.py:1224-1312).
+
+    ``at`` is stored (K, M); the reference transposes each (bk, bm) tile in VMEM
+    before the ordinary kernel, which equals the tile-local Strassen product of
+    at.T and b.
+    """
+    return strassen_matmul_ref(np.asarray(at).T, b, bm=bm, bn=bn, bk=bk,
+                               interleave_products=interleave_products, output_dtype=output_dtype)
+
+
 # ------------------------------------------------------------- classical arms
 
 

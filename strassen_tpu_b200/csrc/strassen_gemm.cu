@@ -115,6 +115,7 @@ using PipeFor = typename std::conditional<kStrassen, StrassenPipe, ClassicalPipe
 
 constexpr uint32_t kIdesc = umma_idesc_bf16_f32(kBlockM, kBlockN, false, true);
 constexpr uint32_t kIdescNegA = kIdesc | (1u << 13);  // D (+)= -A * B
+constexpr uint32_t kIdescAT = umma_idesc_bf16_f32(kBlockM, kBlockN, true, true);  // A MN-major
 
 // Operand slots inside a stage.  Raw tiles land in slots 0..3
 // (a0=A[top,left] a1=A[top,right] a2=A[bottom,left] a3=A[bottom,right];
@@ -313,7 +314,9 @@ __device__ __forceinline__ void read_quadrants(uint32_t tmem_row, int col, Quad8
 
 // kOpts compiles in the research options (dual formula, block permutation,
 // exact panels); the default launch uses the lean classical instantiation.
-template <bool kStrassen, int kEpi, bool kOutF32, bool kOpts>
+// kATrans: A is stored transposed, (K, M) row-major (strassen_matmul_lhs_transposed);
+// its tiles arrive M-major and feed the MMA as an MN-major operand.
+template <bool kStrassen, int kEpi, bool kOutF32, bool kOpts, bool kATrans = false>
 __global__ void __launch_bounds__(kThreads, 1)
     strassen_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a,
                          const __grid_constant__ CUtensorMap tmap_b, const GemmParams p) {
@@ -407,8 +410,20 @@ __global__ void __launch_bounds__(kThreads, 1)
           const int kcol = panel * p.bk + (qk ^ swap_k) * p.half_bk + kin;
 #pragma unroll
           for (int qr = 0; qr < 2; ++qr) {
-            tma_load_3d(stage + (2 * qr + qk) * kASlotBytes, &tmap_a, fb, kcol,
-                        (qr ^ swap_m) * p.half_bm + a_row_base, a_block);
+            if constexpr (kATrans) {
+              // Two 64-row halves of the 128-row product tile, each a (16 k x 64 m)
+              // box of A^T; half h lands 2 KB after half 0 (the MN-major LBO).
+#pragma unroll
+              for (int h = 0; h < 2; ++h) {
+                const int t = t0 + 64 * h;
+                const int blk = t / p.half_bm;
+                const int m_coord = blk * p.bm + (qr ^ swap_m) * p.half_bm + (t - blk * p.half_bm);
+                tma_load_2d(stage + (2 * qr + qk) * kASlotBytes + h * 2048, &tmap_a, fb, m_coord, kcol);
+              }
+            } else {
+              tma_load_3d(stage + (2 * qr + qk) * kASlotBytes, &tmap_a, fb, kcol,
+                          (qr ^ swap_m) * p.half_bm + a_row_base, a_block);
+            }
           }
 #pragma unroll
           for (int qc = 0; qc < 2; ++qc) {
@@ -452,11 +467,13 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (!exact) {
 #pragma unroll
               for (int i = 0; i < 7; ++i) {
-                const uint64_t ad = umma_smem_desc(a_stage + a_off[i] + kk * 32, P::A_LBO,
-                                                   P::A_SBO, P::A_LAYOUT);
+                const uint64_t ad = kATrans
+                    ? umma_smem_desc(a_stage + a_off[i] + kk * 2048, 2048, 1024, kLayoutSwizzle128B)
+                    : umma_smem_desc(a_stage + a_off[i] + kk * 32, P::A_LBO, P::A_SBO, P::A_LAYOUT);
                 const uint64_t bd = umma_smem_desc(b_stage + b_off[i] + kk * 2048,
                                                    P::B_LBO, P::B_SBO, P::B_LAYOUT);
-                umma_bf16_ss(tmem_base + i * kBlockN, ad, bd, kIdesc, (written >> i) & 1u);
+                umma_bf16_ss(tmem_base + i * kBlockN, ad, bd, kATrans ? kIdescAT : kIdesc,
+                             (written >> i) & 1u);
               }
               written = 0x7Fu;
             } else {
@@ -869,10 +886,10 @@ EncodeTiledFn encode_fn() {
 bool is_pow2(int64_t v) { return v > 0 && (v & (v - 1)) == 0; }
 bool aligned16(const void* ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15u) == 0; }
 
-template <bool kStrassen, int kEpi, bool kOutF32, bool kOpts>
+template <bool kStrassen, int kEpi, bool kOutF32, bool kOpts, bool kATrans = false>
 int launch_typed(cudaStream_t stream, const CUtensorMap& ta, const CUtensorMap& tb,
                  const GemmParams& p) {
-  auto kernel = strassen_gemm_kernel<kStrassen, kEpi, kOutF32, kOpts>;
+  auto kernel = strassen_gemm_kernel<kStrassen, kEpi, kOutF32, kOpts, kATrans>;
   static std::once_flag once;
   static cudaError_t attr_err = cudaSuccess;
   std::call_once(once, [&]() {
@@ -1272,6 +1289,44 @@ int sb_classical_gemm(sb_stream_t stream_, const void* a, const void* b, void* c
   if (st != SB_OK) return st;
   GemmParams p = base_params(m, n, k, bm, bn, bk, c, ldc, ClassicalPipe::BK);
   return dispatch(false, SB_EPI_NONE, out_dtype == SB_F32, stream, ta, tb, p);
+}
+
+int sb_strassen_gemm_lhs_transposed(sb_stream_t stream_, const void* at, const void* b, void* c,
+                                    int64_t m, int64_t n, int64_t k, int64_t ldat, int64_t ldb,
+                                    int64_t ldc, int32_t bm, int32_t bn, int32_t bk,
+                                    int32_t out_dtype) {
+  cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_);
+  // validate_core checks lda >= k for a row-major A; A^T needs ldat >= m instead.
+  int st = validate_core(at, b, c, m, n, k, k, ldb, ldc, bm, bn, bk, out_dtype);
+  if (st != SB_OK) return st;
+  if (ldat < m || ldat % 8)
+    return fail(SB_ERR_ALIGNMENT, "A^T leading dimension must cover M and be a multiple of 8");
+  if ((bm / 2) % 64)
+    return fail(SB_ERR_UNSUPPORTED, "strassen_matmul_lhs_transposed on B200 needs bm a multiple of 128, got " +
+                                        std::to_string(bm));
+  if (ldc < n) return fail(SB_ERR_ALIGNMENT, "ldc must be >= N");
+  st = check_device();
+  if (st != SB_OK) return st;
+  EncodeTiledFn enc = encode_fn();
+  if (!enc) return fail(SB_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
+  CUtensorMap ta, tb, unused;
+  {
+    cuuint64_t dims[2] = {(cuuint64_t)m, (cuuint64_t)k};
+    cuuint64_t strides[1] = {(cuuint64_t)ldat * 2};
+    cuuint32_t box[2] = {64, (cuuint32_t)StrassenPipe::BK};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = enc(&ta, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(at), dims, strides, box,
+                     estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                     CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS)
+      return fail(SB_ERR_CUDA, "cuTensorMapEncodeTiled(A^T) failed: " + std::to_string((int)r));
+  }
+  // B map exactly as for the ordinary GEMM (the A map it builds alongside is discarded).
+  st = make_maps(b, b, m, n, k, ldb, ldb, bm, StrassenPipe::BK, &unused, &tb);
+  if (st != SB_OK) return st;
+  GemmParams p = base_params(m, n, k, bm, bn, bk, c, ldc, StrassenPipe::BK);
+  return out_dtype == SB_F32 ? launch_typed<true, SB_EPI_NONE, true, false, true>(stream, ta, tb, p)
+                             : launch_typed<true, SB_EPI_NONE, false, false, true>(stream, ta, tb, p);
 }
 
 int sb_rms_norm(sb_stream_t stream_, const void* x, const void* w, void* y, int64_t rows, int64_t n,

@@ -333,6 +333,70 @@ def strassen_matmul(
     return out
 
 
+def strassen_matmul_lhs_transposed(
+    a,
+    b,
+    *,
+    bm=TUNED_BM,
+    bn=TUNED_BN,
+    bk=TUNED_BK,
+    dot_precision=None,
+    interleave_products=False,
+    output_dtype=None,
+    allow_input_fusion=None,
+    interpret=False,
+    vmem_limit_bytes=None,
+    out=None,
+):
+    """Compute ``a.T @ b`` without materialising the transpose; ``a`` is (K, M).
+
+    Mirrors strassen_pallas.strassen_matmul_lhs_transposed
+    (strassen_pallas.py:1224-1312): the kernel loads M-major tiles of ``a`` with
+    TMA and feeds them to the tensor cores as an MN-major operand.  B200
+    restriction: ``bm`` must be a multiple of 128.
+    """
+    if a.ndim != 2 or b.ndim != 2:
+        raise ValueError("strassen_matmul_lhs_transposed expects rank-2 inputs")
+    k, m = a.shape
+    k2, n = b.shape
+    if k != k2:
+        raise ValueError(f"contracting dimensions disagree: {k} vs {k2}")
+    if a.dtype != b.dtype:
+        raise ValueError(f"input dtypes disagree: {_dtype_name(a.dtype)} vs {_dtype_name(b.dtype)}")
+    if a.dtype not in (torch.bfloat16, torch.float32):
+        raise ValueError("inputs must be BF16 or FP32")
+    for name, dimension, block in (("M", m, bm), ("N", n, bn), ("K", k, bk)):
+        if dimension % block:
+            raise ValueError(f"{name}={dimension} is not divisible by {block}")
+    check_tiling(bm, bn, bk)
+    if allow_input_fusion is not None:
+        allow_input_fusion = tuple(allow_input_fusion)
+        if len(allow_input_fusion) != 2:
+            raise ValueError("allow_input_fusion must contain two booleans")
+    out_dt = _as_torch_dtype(output_dtype) or a.dtype
+    if out_dt not in (torch.bfloat16, torch.float32):
+        raise ValueError("output_dtype must be BF16 or FP32")
+    if interpret:
+        raise NotImplementedError("interpret=True: the B200 build has no CPU path")
+    if a.dtype != torch.bfloat16:
+        raise NotImplementedError("the B200 kernel computes bf16 inputs; FP32 inputs are not built")
+    if bm % 128:
+        raise NotImplementedError(f"strassen_matmul_lhs_transposed on B200 needs bm a multiple of 128, got {bm}")
+    if not (a.is_cuda and b.is_cuda):
+        raise ValueError("strassen_matmul_lhs_transposed runs on a CUDA device; got CPU tensors (no CPU fallback)")
+    device = a.device
+    a, b = _rowmajor(a), _rowmajor(b)
+    if out is None:
+        out = torch.empty((m, n), dtype=out_dt, device=device)
+    lib = _native.load()
+    with torch.cuda.device(device):
+        status = lib.sb_strassen_gemm_lhs_transposed(
+            _stream_handle(device), a.data_ptr(), b.data_ptr(), out.data_ptr(), m, n, k,
+            _ld(a), _ld(b), _ld(out), bm, bn, bk, SB_F32 if out_dt == torch.float32 else SB_BF16)
+    _native.check(status)
+    return out
+
+
 def workspace_bytes(m: int, n: int, k: int, epilogue=None) -> int:
     """Scratch bytes :func:`strassen_matmul` needs (non-zero for norm_residual_add)."""
     return int(_native.load().sb_workspace_bytes(m, n, k, EPILOGUE_KINDS[epilogue]))

@@ -21,11 +21,19 @@ def pytest_configure(config):
 
 
 @pytest.fixture(scope="session")
+def golden_lhs_t():
+    """(manifest, arrays) of the reference's strassen_matmul_lhs_transposed outputs."""
+    manifest = json.loads((GOLDEN / "golden_cases.json").read_text())["lhs_transposed_cases"]
+    arrays = np.load(GOLDEN / "golden_outputs.npz")
+    return manifest, {k.split("/", 1)[1]: arrays[k] for k in arrays.files if k.startswith("lhs_t/")}
+
+
+@pytest.fixture(scope="session")
 def golden():
     """(manifest, arrays): reference outputs keyed by case name."""
     manifest = json.loads((GOLDEN / "golden_cases.json").read_text())["cases"]
     arrays = np.load(GOLDEN / "golden_outputs.npz")
-    return manifest, {k: arrays[k] for k in arrays.files}
+    return manifest, {k: arrays[k] for k in arrays.files if "/" not in k}
 
 
 def golden_output(p, arr):

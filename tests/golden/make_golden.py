@@ -341,7 +341,7 @@ def main():
     parser.add_argument("--out", default=str(HERE))
     args = parser.parse_args()
     sp = import_reference(Path(args.reference))
-    manifest, arrays = {}, {}
+    manifest, arrays, lhs_manifest = {}, {}, {}
     for name, p in cases():
         out = run_reference(sp, p)
         # Large outputs are stored row-subsampled (every ROW_STRIDE-th row).
@@ -358,6 +358,28 @@ def main():
         p["shape"] = full_shape
         manifest[name] = p
         print(f"{name}: out {out.shape} {out.dtype}", flush=True)
+    # strassen_matmul_lhs_transposed (strassen_pallas.py:1224-1312): a is stored (K, M).
+    lt_cases = {
+        "lhs_t_512x768x512": dict(m=512, k=768, n=512, tile=(256, 256, 256), seed=71, kw={}),
+        "lhs_t_interleaved_f32": dict(m=256, k=512, n=512, tile=(256, 256, 256), seed=72,
+                                      kw=dict(interleave_products=True), out="float32"),
+        "lhs_t_bm128_1024": dict(m=1024, k=1024, n=512, tile=(128, 256, 512), seed=73, kw={}),
+    }
+    for name, c in lt_cases.items():
+        at = ref.normal_bf16((c["k"], c["m"]), c["seed"])
+        bt = ref.normal_bf16((c["k"], c["n"]), c["seed"] + 1)
+        out = np.asarray(sp.strassen_matmul_lhs_transposed(
+            np.asarray(at).astype(BF16), np.asarray(bt).astype(BF16), bm=c["tile"][0],
+            bn=c["tile"][1], bk=c["tile"][2], interpret=True,
+            output_dtype=np.float32 if c.get("out") == "float32" else None, **c["kw"]))
+        full_shape = list(out.shape)
+        stride = 4 if out.shape[0] * out.shape[1] > 70_000 else 1
+        arrays["lhs_t/" + name] = (out.view(np.uint16) if out.dtype == BF16 else out.astype(np.float32))[::stride]
+        lhs_manifest[name] = dict(m=c["m"], k=c["k"], n=c["n"], bm=c["tile"][0], bn=c["tile"][1],
+                                  bk=c["tile"][2], seed=c["seed"], kwargs=c["kw"], shape=full_shape,
+                                  row_stride=stride,
+                                  output="float32" if out.dtype != BF16 else "bf16_bits")
+        print(f"lhs_t/{name}: out {out.shape} {out.dtype}", flush=True)
     # Layout helpers (strassen_pallas.py:1315-1411) on index-valued inputs, so the
     # stored result is the column permutation itself.
     layouts = {}
@@ -377,7 +399,7 @@ def main():
     (out_dir / "golden_cases.json").write_text(json.dumps(
         {"generator": "tests/golden/make_golden.py",
          "reference": "sarsid/strassen-tpu strassen_pallas.py (kernel + wrapper, CPU stand-in)",
-         "cases": manifest}, indent=1, sort_keys=True))
+         "cases": manifest, "lhs_transposed_cases": lhs_manifest}, indent=1, sort_keys=True))
     np.savez_compressed(out_dir / "golden_outputs.npz", **arrays)
 
 

@@ -239,3 +239,30 @@ def test_full_size_8192_block_row_and_global_error():
     maxnorm = (err.abs().max() / fp32.abs().max()).item()
     assert rmse <= 4.0 * nat_rmse, (rmse, nat_rmse)
     assert maxnorm <= 0.01, maxnorm
+
+
+def test_lhs_transposed_golden(golden_lhs_t):
+    """strassen_matmul_lhs_transposed against the reference's own outputs."""
+    import strassen_tpu_b200 as sb
+    manifest, arrays = golden_lhs_t
+    for name, c in manifest.items():
+        at = ref.normal_bf16((c["k"], c["m"]), c["seed"])
+        b = ref.normal_bf16((c["k"], c["n"]), c["seed"] + 1)
+        f32 = c["output"] == "float32"
+        got = host(sb.strassen_matmul_lhs_transposed(
+            dev_bf16(at), dev_bf16(b), bm=c["bm"], bn=c["bn"], bk=c["bk"],
+            output_dtype=torch.float32 if f32 else None, **c["kwargs"]))[::c["row_stride"]]
+        want = golden_output(c, arrays[name])
+        exact = ref.classical_f64(at.T[::c["row_stride"]], b)
+        assert_parity(got, want, exact, rounding_step=not f32)
+
+
+def test_lhs_transposed_exact_integers():
+    import strassen_tpu_b200 as sb
+    k, m, n = 1024, 512, 768
+    at = ref.integers_bf16((k, m), -2, 2, 81)
+    b = ref.integers_bf16((k, n), -2, 2, 82)
+    for tile in ((128, 256, 256), (256, 256, 512), (512, 256, 256)):
+        got = host(sb.strassen_matmul_lhs_transposed(dev_bf16(at), dev_bf16(b), bm=tile[0], bn=tile[1],
+                                                     bk=tile[2], output_dtype=torch.float32))
+        np.testing.assert_array_equal(got, at.T @ b, err_msg=str(tile))

@@ -142,3 +142,16 @@ def test_strassen_error_is_within_twice_native(golden):
     nat = ref.error_stats(native, exact)
     assert s["l2_relative"] < 0.01
     assert s["rmse"] <= 4.0 * nat["rmse"]
+
+
+def test_lhs_transposed_oracle_matches_reference(golden_lhs_t):
+    manifest, arrays = golden_lhs_t
+    assert len(manifest) >= 3
+    for name, c in manifest.items():
+        at = ref.normal_bf16((c["k"], c["m"]), c["seed"])
+        b = ref.normal_bf16((c["k"], c["n"]), c["seed"] + 1)
+        got = ref.strassen_lhs_transposed_ref(at, b, bm=c["bm"], bn=c["bn"], bk=c["bk"],
+                                              output_dtype=c["output"] if c["output"] == "float32"
+                                              else "bfloat16", **c["kwargs"])
+        want = golden_output(c, arrays[name])
+        np.testing.assert_array_equal(got[::c["row_stride"]], want, err_msg=name)
