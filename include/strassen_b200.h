@@ -90,7 +90,8 @@ typedef struct sb_epilogue {
 typedef enum sb_formula {
   SB_FORMULA_CLASSICAL = 0,  /* Strassen's P1..P7, strassen_pallas.py:324-379   */
   SB_FORMULA_DUAL = 1,       /* the dual rank-7 formula Q1..Q7, :466-517         */
-  SB_FORMULA_POWERS = 2      /* power-of-two formula R1..R7, :381-464 (not built) */
+  SB_FORMULA_POWERS = 2      /* power-of-two formula R1..R7, :381-464; no epilogue,
+                                no exact panels                                   */
 } sb_formula;
 
 typedef struct sb_options {

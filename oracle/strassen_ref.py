@@ -122,6 +122,59 @@ def _permuted(index_row, index_col, swap_rows, swap_cols):
     return 2 * (index_row ^ swap_rows) + (index_col ^ swap_cols)
 
 
+# The power-of-two formula R1..R7 (strassen_pallas.py:381-464).  Every bf16
+# operation rounds, in the reference's order; x*0.5 and x*0.25 are exact.
+def _h(x):
+    return bf16_round(x * F32(0.5))
+
+
+def _q(x):
+    return bf16_round(x * F32(0.25))
+
+
+def _sub(x, y):
+    return bf16_round(x - y)
+
+
+def _add(x, y):
+    return bf16_round(x + y)
+
+
+POWERS_A = {
+    1: lambda a: _sub(a[2], a[1]),
+    2: lambda a: _add(_sub(a[0], _h(a[2])), _sub(_h(a[1]), _q(a[3]))),
+    3: lambda a: _sub(a[2], _h(a[3])),
+    4: lambda a: _sub(a[1], _h(a[3])),
+    5: lambda a: _add(a[2], _h(a[3])),
+    6: lambda a: _add(_sub(a[0], _h(a[1])), _sub(_h(a[2]), _q(a[3]))),
+    7: lambda a: _add(a[1], _h(a[3])),
+}
+POWERS_B = {
+    1: lambda b: _sub(b[0], b[3]),
+    2: lambda b: _add(b[0], _h(b[1])),
+    3: lambda b: _sub(_h(b[1]), b[3]),
+    4: lambda b: _add(_sub(_h(b[0]), b[2]), _sub(_q(b[1]), _h(b[3]))),
+    5: lambda b: _add(_h(b[1]), b[3]),
+    6: lambda b: _sub(b[0], _h(b[1])),
+    7: lambda b: _sub(_add(_h(b[0]), b[2]), _add(_q(b[1]), _h(b[3]))),
+}
+# Basis updates z0..z3 (not permuted; strassen_pallas.py:398-464).
+POWERS_UPDATES = {1: ((3, 1),), 2: ((2, 1),), 3: ((0, 1), (3, -1)), 4: ((2, -1), (3, 1)),
+                  5: ((0, 1),), 6: ((1, 1),), 7: ((1, 1), (3, 1))}
+POWERS_PLAIN_ORDER = (1, 2, 3, 4, 5, 6, 7)            # strassen_pallas.py:530-537
+POWERS_INTERLEAVED_ORDER = (3, 2, 6, 5, 4, 7, 1)      # strassen_pallas.py:520-528
+
+
+def powers_decode(z):
+    """Output quadrants from the sparse basis z0..z3 (strassen_pallas.py:744-761)."""
+    z0, z1, z2, z3 = z
+    c3 = z0
+    c2 = z3 + z0 * F32(0.5)
+    c0 = (z1 + z2) * F32(0.5) + z0 * F32(0.25)
+    c1 = ((z2 - z1) + z3) + z0 * F32(0.5)
+    return [c0.astype(F32), c1.astype(F32), c2.astype(F32), c3.astype(F32)]
+
+
 def strassen_accumulators(a, b, bm, bn, bk, *, interleave_products=False,
                           final_order=None, formula_variant="classical", block_permutation=0,
                           exact_panels=()):
@@ -147,6 +200,26 @@ def strassen_accumulators(a, b, bm, bn, bk, *, interleave_products=False,
     n_i, n_p = aq[0].shape[:2]
     n_j = bq[0].shape[1]
     hm, hn = bm // 2, bn // 2
+    if formula_variant == "powers":
+        if exact_panels:
+            raise NotImplementedError("exact panels need a quadrant-basis formula")
+        order = POWERS_INTERLEAVED_ORDER if interleave_products else POWERS_PLAIN_ORDER
+        z = [np.zeros((n_i, n_j, hm, hn), F32) for _ in range(4)]
+        for p in range(n_p):
+            ap = [x[:, p] for x in aq]
+            bp = [x[p] for x in bq]
+            for idx in order:
+                prod = np.matmul(POWERS_A[idx](ap)[:, None], POWERS_B[idx](bp)[None]).astype(F32)
+                for q, sign in POWERS_UPDATES[idx]:
+                    if sign > 0:
+                        z[q] += prod
+                    else:
+                        z[q] -= prod
+        decoded = powers_decode(z)
+        acc = [None] * 4
+        for q in range(4):
+            acc[out_index[q]] = decoded[q]
+        return acc
     if formula_variant == "classical":
         table, order = PRODUCTS, (INTERLEAVED_ORDER if interleave_products else PLAIN_ORDER)
     elif formula_variant == "dual":

@@ -240,6 +240,20 @@ __device__ __forceinline__ uint32_t bf16x2_sub(uint32_t a, uint32_t b) {
   asm("sub.rn.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
   return d;
 }
+// x * 0.5 and x * 0.25 on bf16x2 (exact: the power-of-two formula's scalings).
+__device__ __forceinline__ uint32_t bf16x2_mul(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+__device__ __forceinline__ uint4 half4(uint4 a) {
+  const uint32_t h = 0x3F003F00u;  // (0.5, 0.5)
+  return make_uint4(bf16x2_mul(a.x, h), bf16x2_mul(a.y, h), bf16x2_mul(a.z, h), bf16x2_mul(a.w, h));
+}
+__device__ __forceinline__ uint4 quarter4(uint4 a) {
+  const uint32_t q = 0x3E803E80u;  // (0.25, 0.25)
+  return make_uint4(bf16x2_mul(a.x, q), bf16x2_mul(a.y, q), bf16x2_mul(a.z, q), bf16x2_mul(a.w, q));
+}
 __device__ __forceinline__ uint4 add4(uint4 a, uint4 b) {
   return make_uint4(bf16x2_add(a.x, b.x), bf16x2_add(a.y, b.y), bf16x2_add(a.z, b.z),
                     bf16x2_add(a.w, b.w));

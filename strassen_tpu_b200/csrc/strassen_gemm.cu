@@ -275,6 +275,20 @@ __device__ __forceinline__ void read_quadrants(uint32_t tmem_row, int col, Quad8
         out.c[2][e] = m[1][e] + m[3][e];
         out.c[3][e] = ((m[0][e] - m[1][e]) + m[2][e]) + m[5][e];
       }
+    } else if (p.formula == 2) {
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        // Power-of-two formula: basis updates (strassen_pallas.py:398-464) then
+        // the decode of strassen_pallas.py:744-761.
+        const float z0 = m[2][e] + m[4][e];
+        const float z1 = m[5][e] + m[6][e];
+        const float z2 = m[1][e] - m[3][e];
+        const float z3 = ((m[0][e] - m[2][e]) + m[3][e]) + m[6][e];
+        out.c[3][e] = z0;
+        out.c[2][e] = z3 + z0 * 0.5f;
+        out.c[0][e] = (z1 + z2) * 0.5f + z0 * 0.25f;
+        out.c[1][e] = ((z2 - z1) + z3) + z0 * 0.5f;
+      }
     } else {
 #pragma unroll
       for (int e = 0; e < 8; ++e) {
@@ -447,8 +461,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t a_off[7], b_off[7];
 #pragma unroll
       for (int i = 0; i < 7; ++i) {
-        a_off[i] = ((kOpts && p.formula != 0) ? kDualASlot[i] : kASlot[i]) * kASlotBytes;
-        b_off[i] = ((kOpts && p.formula != 0) ? kDualBSlot[i] : kBSlot[i]) * kBSlotBytes;
+        const int fa = !kOpts || p.formula == 0 ? kASlot[i] : p.formula == 1 ? kDualASlot[i] : i;
+        const int fb = !kOpts || p.formula == 0 ? kBSlot[i] : p.formula == 1 ? kDualBSlot[i] : i;
+        a_off[i] = fa * kASlotBytes;
+        b_off[i] = fb * kBSlotBytes;
       }
       for (int c = 0; c < p.num_chunks; ++c) {
         const int s = c % kStages;
@@ -549,6 +565,42 @@ __global__ void __launch_bounds__(kThreads, 1)
             sts128(b_stage + 6 * kBSlotBytes + off, add4(b2, b3));
             sts128(b_stage + 1 * kBSlotBytes + off, sub4(b1, b3));
             sts128(b_stage + 2 * kBSlotBytes + off, sub4(b2, b0));
+          }
+        } else if (p.formula == 2) {
+          // Power-of-two formula (strassen_pallas.py:398-464): all seven operands
+          // per side are computed (each bf16 op rounds, in the reference's
+          // order) and written over slots 0..6, operand i-1 for product Ri.
+#pragma unroll
+          for (int idx = sum_tid; idx < kASlotBytes / 16; idx += kSumThreads) {
+            const uint32_t off = idx * 16;
+            const uint4 a0 = lds128(a_stage + 0 * kASlotBytes + off);
+            const uint4 a1 = lds128(a_stage + 1 * kASlotBytes + off);
+            const uint4 a2 = lds128(a_stage + 2 * kASlotBytes + off);
+            const uint4 a3 = lds128(a_stage + 3 * kASlotBytes + off);
+            const uint4 h1 = half4(a1), h2 = half4(a2), h3 = half4(a3), q3 = quarter4(a3);
+            sts128(a_stage + 0 * kASlotBytes + off, sub4(a2, a1));
+            sts128(a_stage + 1 * kASlotBytes + off, add4(sub4(a0, h2), sub4(h1, q3)));
+            sts128(a_stage + 2 * kASlotBytes + off, sub4(a2, h3));
+            sts128(a_stage + 3 * kASlotBytes + off, sub4(a1, h3));
+            sts128(a_stage + 4 * kASlotBytes + off, add4(a2, h3));
+            sts128(a_stage + 5 * kASlotBytes + off, add4(sub4(a0, h1), sub4(h2, q3)));
+            sts128(a_stage + 6 * kASlotBytes + off, add4(a1, h3));
+          }
+#pragma unroll
+          for (int idx = sum_tid; idx < kBSlotBytes / 16; idx += kSumThreads) {
+            const uint32_t off = idx * 16;
+            const uint4 b0 = lds128(b_stage + 0 * kBSlotBytes + off);
+            const uint4 b1 = lds128(b_stage + 1 * kBSlotBytes + off);
+            const uint4 b2 = lds128(b_stage + 2 * kBSlotBytes + off);
+            const uint4 b3 = lds128(b_stage + 3 * kBSlotBytes + off);
+            const uint4 h0 = half4(b0), h1 = half4(b1), h3 = half4(b3), q1 = quarter4(b1);
+            sts128(b_stage + 0 * kBSlotBytes + off, sub4(b0, b3));
+            sts128(b_stage + 1 * kBSlotBytes + off, add4(b0, h1));
+            sts128(b_stage + 2 * kBSlotBytes + off, sub4(h1, b3));
+            sts128(b_stage + 3 * kBSlotBytes + off, add4(sub4(h0, b2), sub4(q1, h3)));
+            sts128(b_stage + 4 * kBSlotBytes + off, add4(h1, b3));
+            sts128(b_stage + 5 * kBSlotBytes + off, sub4(b0, h1));
+            sts128(b_stage + 6 * kBSlotBytes + off, sub4(add4(h0, b2), add4(q1, h3)));
           }
         } else {
           // Dual formula operand sums (strassen_pallas.py:466-517).
@@ -1055,7 +1107,7 @@ GemmParams base_params(int64_t m, int64_t n, int64_t k, int32_t bm, int32_t bn, 
 }
 
 void apply_options(GemmParams& p, int formula, int perm, const int32_t* schedule) {
-  p.formula = formula == SB_FORMULA_DUAL ? 1 : 0;
+  p.formula = formula == SB_FORMULA_DUAL ? 1 : formula == SB_FORMULA_POWERS ? 2 : 0;
   p.swap_m = perm & 1;
   p.swap_k = (perm >> 1) & 1;
   p.swap_n = (perm >> 2) & 1;
@@ -1097,9 +1149,11 @@ int sb_strassen_gemm_ex(sb_stream_t stream_, const void* a, const void* b, void*
   const int formula = opt ? opt->formula_variant : SB_FORMULA_CLASSICAL;
   const int perm = opt ? opt->block_permutation : 0;
   const int32_t* schedule = opt ? opt->panel_schedule : nullptr;
-  if (formula == SB_FORMULA_POWERS)
-    return fail(SB_ERR_UNSUPPORTED, "formula_variant='powers' is not built for B200");
-  if (formula != SB_FORMULA_CLASSICAL && formula != SB_FORMULA_DUAL)
+  if (formula == SB_FORMULA_POWERS && epi != SB_EPI_NONE)
+    return fail(SB_ERR_EPILOGUE, "fused epilogues require a quadrant-basis formula");
+  if (formula == SB_FORMULA_POWERS && schedule)
+    return fail(SB_ERR_UNSUPPORTED, "exact classical panels need a quadrant-basis formula");
+  if (formula != SB_FORMULA_CLASSICAL && formula != SB_FORMULA_DUAL && formula != SB_FORMULA_POWERS)
     return fail(SB_ERR_RANK, "formula_variant must be 'classical', 'dual', or 'powers'");
   if (perm < 0 || perm > 7) return fail(SB_ERR_RANK, "block_permutation must be an integer from 0 through 7");
   if (schedule && (reinterpret_cast<uintptr_t>(schedule) & 3u))

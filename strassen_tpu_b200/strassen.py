@@ -10,8 +10,7 @@ accepted and validated but do not change the B200 arithmetic, which keeps the
 seven products in separate fp32 TMEM accumulators over the whole K range and
 recombines them once.  The research options ``formula_variant="dual"``,
 ``block_permutation`` and exact classical panels (``classical_panels`` /
-``panel_schedule``) run on the same kernel; ``formula_variant="powers"`` is not
-built.  ``bm``/``bn``/``bk`` keep their reference meaning: they
+``panel_schedule``) and ``formula_variant="powers"`` run on the same kernel.  ``bm``/``bn``/``bk`` keep their reference meaning: they
 define the Strassen block whose quadrants are paired, so results follow the
 reference's pairing of operands.
 
@@ -248,8 +247,8 @@ def strassen_matmul(
             "oracle/ and is test infrastructure only")
     if a.dtype != torch.bfloat16:
         raise NotImplementedError("the B200 kernel computes bf16 inputs; FP32 inputs are not built")
-    if formula_variant == "powers":
-        raise NotImplementedError("formula_variant='powers' is not built for B200")
+    if formula_variant == "powers" and panel_schedule is not None:
+        raise NotImplementedError("exact classical panels need a quadrant-basis formula")
     if not (a.is_cuda and b.is_cuda):
         raise ValueError("strassen_matmul runs on a CUDA device; got CPU tensors (no CPU fallback)")
 

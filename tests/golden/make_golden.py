@@ -314,6 +314,13 @@ def cases():
          classical_panels=(0,))
     gemm("residual_dual_exact1", 256, 1024, 512, (256, 256, 512), seed=61,
          epilogue="residual_add", formula_variant="dual", classical_panels=(1,))
+    gemm("powers_512", 512, 512, 512, (256, 256, 256), seed=62, formula_variant="powers")
+    gemm("powers_interleaved_f32", 256, 1024, 512, (256, 256, 256), seed=63,
+         formula_variant="powers", interleave_products=True, output_dtype="float32")
+    gemm("powers_blockperm3", 512, 512, 512, (256, 256, 256), seed=64, formula_variant="powers",
+         block_permutation=3)
+    gemm("int_powers_perm4", 64, 768, 512, (32, 256, 256), kind="int", seed=65,
+         formula_variant="powers", block_permutation=4, output_dtype="float32")
     return out
 
 

@@ -95,15 +95,15 @@ def test_no_cpu_path():
 def test_unbuilt_reference_options_refuse_loudly():
     with pytest.raises(NotImplementedError, match="FP32 inputs"):
         call(*mats(dtype=torch.float32))
-    with pytest.raises(NotImplementedError, match="powers"):
-        call(formula_variant="powers")
+    with pytest.raises(NotImplementedError, match="quadrant-basis"):
+        call(formula_variant="powers", panel_schedule=[1])
 
 
 def test_research_options_reach_the_device_check():
     # dual / block_permutation / exact panels are built: on CPU tensors they
     # fail only at the device check, after validation.
     for kw in (dict(formula_variant="dual"), dict(block_permutation=3), dict(classical_panels=(0,)),
-               dict(panel_schedule=[1])):
+               dict(panel_schedule=[1]), dict(formula_variant="powers")):
         with pytest.raises(ValueError, match="no CPU fallback"):
             call(**kw)
 
