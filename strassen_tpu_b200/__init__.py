@@ -1,8 +1,8 @@
 """B200-native (sm_100a) tile-local Strassen GEMM with fused Qwen3 epilogues.
 
 Drop-in for the reference operator API ``strassen_pallas`` (sarsid/strassen-tpu):
-``strassen_matmul``, ``native_matmul``, ``check_tiling`` and the weight/table
-layout helpers.  The kernels live in ``csrc/`` behind the C ABI declared in
+``strassen_matmul``, ``native_matmul``, ``tuned_matmul``, ``check_tiling`` and the
+weight/table layout helpers.  The kernels live in ``csrc/`` behind the C ABI declared in
 ``include/strassen_b200.h``.
 """
 
@@ -25,11 +25,12 @@ from .strassen import (
     strassen_matmul_lhs_transposed,
     workspace_bytes,
 )
+from .tuning import tuned_matmul
 
 __all__ = [
     "TUNED_BM", "TUNED_BN", "TUNED_BK",
     "check_tiling", "classical_matmul", "native_matmul", "rms_norm", "strassen_matmul",
-    "strassen_matmul_lhs_transposed",
+    "strassen_matmul_lhs_transposed", "tuned_matmul",
     "workspace_bytes",
     "rope_layout_tables", "rope_layout_to_heads", "rope_scale_layout", "rope_weight_layout",
     "swiglu_weight_layout",
