@@ -63,6 +63,18 @@ constexpr int kBlockN = 64;   // product columns per CTA = TMEM columns per prod
 #ifndef SB_STAGES
 #define SB_STAGES 5
 #endif
+#ifndef SB_TS_STAGES
+#define SB_TS_STAGES 6
+#endif
+#ifndef SB_TS_AK
+#define SB_TS_AK 64
+#endif
+#ifndef SB_TS_ASTAGES
+#define SB_TS_ASTAGES 2
+#endif
+#ifndef SB_TMEM_A
+#define SB_TMEM_A 1
+#endif
 #ifndef SB_C_BLOCK_K
 #define SB_C_BLOCK_K 64
 #endif
@@ -78,17 +90,21 @@ constexpr int kBarrierBytes = 256;
 constexpr int kRasterGroup = 16;  // product-row tiles per column sweep (L2 reuse)
 static_assert(7 * kBlockN <= (int)kTmemCols, "seven accumulators must fit in TMEM");
 
-// Pipeline geometry.  A stage holds `kSlotsPerSide` A tiles (128 x BK, K-major)
-// and as many B tiles (BK x 64, N-major): the four raw quadrants first, then
-// (Strassen only) the operand sums.
-template <int kBK, int kNumStages, int kSlotsPerSide>
+// Pipeline geometry.  A stage holds `kASlots` A tiles (128 x BK, K-major) and
+// `kBSlots` B tiles (BK x 64, N-major): the four raw quadrants first, then
+// (Strassen only) the operand sums formed in shared memory.
+template <int kBK, int kNumStages, int kASlots, int kBSlots>
 struct PipeCfg {
   static constexpr int BK = kBK;
   static constexpr int STAGES = kNumStages;
-  static constexpr int SLOTS = kSlotsPerSide;
   static constexpr int A_SLOT = kBlockM * kBK * 2;
   static constexpr int B_SLOT = kBK * kBlockN * 2;
-  static constexpr int STAGE_BYTES = SLOTS * (A_SLOT + B_SLOT);
+  static constexpr int B_OFFSET = kASlots * A_SLOT;  // B tiles follow the A tiles
+  static constexpr int STAGE_BYTES = kASlots * A_SLOT + kBSlots * B_SLOT;
+  static constexpr int A_STAGES = 0;  // A shares the stage with B
+  static constexpr int A_STAGE_BYTES = 0;
+  static constexpr int B_BASE = 0;
+  static constexpr int DATA_BYTES = kNumStages * STAGE_BYTES;
   static constexpr int RAW_TX = 4 * (A_SLOT + B_SLOT);
   static constexpr int SMEM = STAGES * STAGE_BYTES + kBarrierBytes + 1024;  // + alignment slack
   // A: K-major, one BK-wide row per swizzle row (32/64/128 bytes); 8-row core
@@ -108,10 +124,63 @@ struct PipeCfg {
   static_assert(SMEM <= 227 * 1024, "shared memory budget");
   static_assert(kNumStages <= 8, "barrier area holds at most 8 stages");
 };
-using StrassenPipe = PipeCfg<SB_BLOCK_K, SB_STAGES, 7>;
-using ClassicalPipe = PipeCfg<SB_C_BLOCK_K, SB_C_STAGES, 4>;
-template <bool kStrassen>
-using PipeFor = typename std::conditional<kStrassen, StrassenPipe, ClassicalPipe>::type;
+using StrassenPipe = PipeCfg<SB_BLOCK_K, SB_STAGES, 7, 7>;
+using ClassicalPipe = PipeCfg<SB_C_BLOCK_K, SB_C_STAGES, 4, 4>;
+
+// Geometry of the default Strassen kernel (see uses_tmem_a): A and B have
+// separate pipelines.  An A stage holds the four raw A quadrant tiles of kAK
+// product columns (128 x kAK, K-major, kAK*2-byte swizzle) and serves kAK/16
+// K steps; a B stage holds one 16-deep step: four raw B quadrant tiles plus
+// the five B sums (16 x 64 each, N-major, 128-byte swizzle).  Wide A rows keep
+// the TMA row count per step low (128-byte rows: 128 + 64 rows per step
+// instead of 512 + 64 at 32-byte rows): the TMA engine moves roughly one row
+// per clock, which bound the 16-wide design.
+template <int kAK, int kAStages, int kBStages>
+struct TsPipeCfg {
+  static constexpr int BK = 16;
+  static constexpr int AK = kAK;
+  static constexpr int STAGES = kBStages;
+  static constexpr int A_STAGES = kAStages;
+  static constexpr int A_SLOT = kBlockM * kAK * 2;
+  static constexpr int A_STAGE_BYTES = 4 * A_SLOT;
+  static constexpr int B_SLOT = 16 * kBlockN * 2;
+  static constexpr int B_OFFSET = 0;
+  static constexpr int STAGE_BYTES = 7 * B_SLOT;  // one B stage
+  static constexpr int B_BASE = kAStages * A_STAGE_BYTES;
+  static constexpr int RAW_TX = 4 * B_SLOT;
+  static constexpr int DATA_BYTES = B_BASE + kBStages * STAGE_BYTES;
+  static constexpr int SMEM = DATA_BYTES + kBarrierBytes + 1024;
+  static constexpr uint32_t A_ROW = kAK * 2;
+  static constexpr uint32_t A_LAYOUT = A_ROW == 32 ? kLayoutSwizzle32B
+                                       : A_ROW == 64 ? kLayoutSwizzle64B : kLayoutSwizzle128B;
+  static constexpr uint32_t A_SBO = 8 * A_ROW;
+  static constexpr uint32_t A_LBO = 16;
+  static constexpr uint32_t B_LAYOUT = kLayoutSwizzle128B;
+  static constexpr uint32_t B_SBO = 1024;
+  static constexpr uint32_t B_LBO = 16 * 128;
+  static_assert(kAK == 16 || kAK == 32 || kAK == 64, "A group must be one swizzle row");
+  static_assert(A_STAGE_BYTES % 1024 == 0 && STAGE_BYTES % 1024 == 0, "1024-byte stage alignment");
+  static_assert(SMEM <= 227 * 1024, "shared memory budget");
+  static_assert((3 * kBStages + 2 + 2 * kAStages) * 8 + 8 <= kBarrierBytes, "barrier area");
+};
+using StrassenTsPipe = TsPipeCfg<SB_TS_AK, SB_TS_ASTAGES, SB_TS_STAGES>;
+constexpr int kTsAK = SB_TS_AK;
+
+// The default Strassen instantiation (classical formula, no research options,
+// A not transposed) keeps four of the five A operand sums in TMEM: a ring of
+// kRingSlots slots of 128 lanes x 8 columns (one 128 x 16 bf16 operand) after
+// the seven accumulators, two K steps deep, and issues those four products
+// as A-from-TMEM MMAs, which takes their A operand off shared memory.
+template <bool kStrassen, bool kOpts, bool kATrans>
+constexpr bool uses_tmem_a() { return SB_TMEM_A && kStrassen && !kOpts && !kATrans; }
+constexpr int kRingSlots = 8;
+constexpr uint32_t kRingCol0 = 7 * kBlockN;  // 448
+static_assert(kRingCol0 + 8 * kRingSlots <= kTmemCols, "operand ring must fit in TMEM");
+
+template <bool kStrassen, bool kTs = false>
+using PipeFor = typename std::conditional<
+    kStrassen, typename std::conditional<kTs, StrassenTsPipe, StrassenPipe>::type,
+    ClassicalPipe>::type;
 
 constexpr uint32_t kIdesc = umma_idesc_bf16_f32(kBlockM, kBlockN, false, true);
 constexpr uint32_t kIdescNegA = kIdesc | (1u << 13);  // D (+)= -A * B
@@ -334,25 +403,29 @@ template <bool kStrassen, int kEpi, bool kOutF32, bool kOpts, bool kATrans = fal
 __global__ void __launch_bounds__(kThreads, 1)
     strassen_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a,
                          const __grid_constant__ CUtensorMap tmap_b, const GemmParams p) {
-  using P = PipeFor<kStrassen>;
+  constexpr bool kTs = uses_tmem_a<kStrassen, kOpts, kATrans>();
+  using P = PipeFor<kStrassen, kTs>;
   constexpr int kStages = P::STAGES;
   constexpr int kStageBytes = P::STAGE_BYTES;
   constexpr int kASlotBytes = P::A_SLOT;
   constexpr int kBSlotBytes = P::B_SLOT;
-  constexpr int kSlots = P::SLOTS;
   constexpr int kBlockK = P::BK;
+  constexpr int kAStages = P::A_STAGES;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_addr = smem_addr(smem_raw);
   uint8_t* smem = smem_raw + ((1024u - (raw_addr & 1023u)) & 1023u);
   const uint32_t smem_base = smem_addr(smem);
 
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kStages * kStageBytes);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + P::DATA_BYTES);
   const uint32_t full_bar = smem_addr(bars);                 // [kStages] TMA landed
   const uint32_t sums_bar = smem_addr(bars + kStages);       // [kStages] operand sums ready
   const uint32_t empty_bar = smem_addr(bars + 2 * kStages);  // [kStages] MMAs done reading
   const uint32_t acc_bar = smem_addr(bars + 3 * kStages);    // accumulators final
   const uint32_t qss_bar = smem_addr(bars + 3 * kStages + 1);  // q/k partial sums written
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 3 * kStages + 2);
+  const uint32_t a_full = smem_addr(bars + 3 * kStages + 2);   // [kAStages] A group landed
+  const uint32_t a_empty = a_full + 8 * kAStages;              // [kAStages] MMAs done with it
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 3 * kStages + 2 + 2 * kAStages);
+  static_assert((3 * kStages + 2 + 2 * kAStages) * 8 + 8 <= kBarrierBytes, "barrier area");
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
 
   const int warp = threadIdx.x >> 5;
@@ -374,11 +447,15 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
       mbar_init(full_bar + 8 * s, 1);
-      mbar_init(sums_bar + 8 * s, kSumWarps);
+      mbar_init(sums_bar + 8 * s, kTs ? 4 : kSumWarps);  // kTs: the set owning the step
       mbar_init(empty_bar + 8 * s, 1);
     }
     mbar_init(acc_bar, 1);
     mbar_init(qss_bar, kSumWarps);
+    for (int s = 0; s < kAStages; ++s) {
+      mbar_init(a_full + 8 * s, 1);
+      mbar_init(a_empty + 8 * s, 1);
+    }
     *abort_flag = 0;
     fence_mbar_init();
     fence_proxy_async_smem();
@@ -395,7 +472,62 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (warp == 0) {
     // ------------------------------------------------------------ TMA producer
-    if (lane == 0) {
+    if constexpr (kTs) {
+     if (lane == 0) {
+      // A every kAK/16 steps into the A ring, B every step into the B ring.
+      constexpr int kGroup = kTsAK / 16;
+      int a_last[kAStages > 0 ? kAStages : 1];
+      int b_last[kStages];
+#pragma unroll
+      for (int s = 0; s < kAStages; ++s) a_last[s] = -1;
+#pragma unroll
+      for (int s = 0; s < kStages; ++s) b_last[s] = -1;
+      const int a_row_base = t0 % p.half_bm;
+      const int a_block = t0 / p.half_bm;
+      const int j_block = u0 / p.half_bn;
+      const int b_col0 = j_block * p.bn + (u0 % p.half_bn);
+      bool ok = true;
+      for (int c = 0; c < p.num_chunks && ok; ++c) {
+        const int kap = c * 16;
+        const int panel = kap / p.half_bk;
+        const int kin = kap - panel * p.half_bk;
+        if (c % kGroup == 0) {
+          const int g = c / kGroup;
+          const int sa = g % kAStages;
+          if (!mbar_wait(a_empty + 8 * sa, ((g / kAStages) & 1u) ^ 1u, abort_flag, p.err, kErrWaitEmpty)) break;
+          const uint32_t fa = a_full + 8 * sa;
+          mbar_arrive_expect_tx(fa, P::A_STAGE_BYTES);
+          const uint32_t a_stage = smem_base + sa * P::A_STAGE_BYTES;
+#pragma unroll
+          for (int qk = 0; qk < 2; ++qk)
+#pragma unroll
+            for (int qr = 0; qr < 2; ++qr)
+              tma_load_3d(a_stage + (2 * qr + qk) * kASlotBytes, &tmap_a, fa,
+                          panel * p.bk + qk * p.half_bk + kin, qr * p.half_bm + a_row_base, a_block);
+          a_last[sa] = g;
+        }
+        const int s = c % kStages;
+        if (!mbar_wait(empty_bar + 8 * s, ((c / kStages) & 1u) ^ 1u, abort_flag, p.err, kErrWaitEmpty)) break;
+        const uint32_t fb = full_bar + 8 * s;
+        mbar_arrive_expect_tx(fb, P::RAW_TX);
+        const uint32_t b_stage = smem_base + P::B_BASE + s * kStageBytes;
+#pragma unroll
+        for (int qk = 0; qk < 2; ++qk)
+#pragma unroll
+          for (int qc = 0; qc < 2; ++qc)
+            tma_load_2d(b_stage + (2 * qk + qc) * kBSlotBytes, &tmap_b, fb, b_col0 + qc * p.half_bn,
+                        panel * p.bk + qk * p.half_bk + kin);
+        b_last[s] = c;
+      }
+      // Drain: never leave a TMA write in flight past teardown.
+#pragma unroll
+      for (int s = 0; s < kAStages; ++s)
+        if (a_last[s] >= 0) mbar_wait_drain(a_full + 8 * s, (a_last[s] / kAStages) & 1u);
+#pragma unroll
+      for (int s = 0; s < kStages; ++s)
+        if (b_last[s] >= 0) mbar_wait_drain(full_bar + 8 * s, (b_last[s] / kStages) & 1u);
+     }
+    } else if (lane == 0) {
       int last_issued[kStages];
 #pragma unroll
       for (int s = 0; s < kStages; ++s) last_issued[s] = -1;
@@ -416,10 +548,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         // Slot (2*qr + qk) of A holds the block's quadrant (qr^swap_m, qk^swap_k);
         // slot (2*qk + qc) of B holds (qk^swap_k, qc^swap_n): the reference's
         // block_permutation (strassen_pallas.py:205-226).
-#pragma unroll
         const int swap_m = kOpts ? p.swap_m : 0;
         const int swap_k = kOpts ? p.swap_k : 0;
         const int swap_n = kOpts ? p.swap_n : 0;
+#pragma unroll
         for (int qk = 0; qk < 2; ++qk) {
           const int kcol = panel * p.bk + (qk ^ swap_k) * p.half_bk + kin;
 #pragma unroll
@@ -441,7 +573,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
 #pragma unroll
           for (int qc = 0; qc < 2; ++qc) {
-            tma_load_2d(stage + kSlots * kASlotBytes + (2 * qk + qc) * kBSlotBytes, &tmap_b, fb,
+            tma_load_2d(stage + P::B_OFFSET + (2 * qk + qc) * kBSlotBytes, &tmap_b, fb,
                         b_col0 + (qc ^ swap_n) * p.half_bn, kcol);
           }
         }
@@ -455,7 +587,47 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
-    if (lane == 0) {
+    if (kTs && lane == 0) {
+      // One wait per K step: the sum warps arrive on sums_bar only after their
+      // A group and B stage landed, so it also covers the TMA data.  The issue
+      // queue is shallow, so every synchronisation in this thread idles the
+      // tensor pipe: one wait and one commit per step, descriptors advanced by
+      // adding (byte offset >> 4) to precomputed stage-0 descriptors.
+      constexpr int kGroup = kTsAK / 16;
+      constexpr uint64_t kA = kASlotBytes >> 4, kB = kBSlotBytes >> 4;
+      const uint64_t a_d0 = umma_smem_desc(smem_base, P::A_LBO, P::A_SBO, P::A_LAYOUT);
+      const uint64_t b_d0 = umma_smem_desc(smem_base + P::B_BASE, P::B_LBO, P::B_SBO, P::B_LAYOUT);
+      int s = 0, sa = 0, kk_a = 0;
+      uint32_t ph = 0;
+      for (int c = 0; c < p.num_chunks; ++c) {
+        if (!mbar_wait(sums_bar + 8 * s, ph, abort_flag, p.err, kErrWaitSums)) break;
+        tc_fence_after();
+        const uint64_t ad = a_d0 + (uint32_t)((sa * P::A_STAGE_BYTES + kk_a * 32) >> 4);
+        const uint64_t bd = b_d0 + (uint32_t)((s * kStageBytes) >> 4);
+        const uint32_t acc = c != 0 ? 1u : 0u;
+        const uint32_t ring = tmem_base + kRingCol0 + 32 * (c & 1);
+        umma_bf16_ts(tmem_base + 0 * kBlockN, ring + 0, bd + 4 * kB, kIdesc, acc);        // (a0+a3)(b0+b3)
+        umma_bf16_ts(tmem_base + 1 * kBlockN, ring + 8, bd, kIdesc, acc);                 // (a2+a3) b0
+        umma_bf16_ss(tmem_base + 2 * kBlockN, ad, bd + 1 * kB, kIdesc, acc);              // a0 (b1-b3)
+        umma_bf16_ss(tmem_base + 3 * kBlockN, ad + 3 * kA, bd + 2 * kB, kIdesc, acc);     // a3 (b2-b0)
+        umma_bf16_ss(tmem_base + 4 * kBlockN, ad + 1 * kA, bd + 3 * kB, kIdesc, acc);     // (a0+a1) b3
+        umma_bf16_ts(tmem_base + 5 * kBlockN, ring + 16, bd + 5 * kB, kIdesc, acc);       // (a2-a0)(b0+b1)
+        umma_bf16_ts(tmem_base + 6 * kBlockN, ring + 24, bd + 6 * kB, kIdesc, acc);       // (a1-a3)(b2+b3)
+        // Frees B stage s and, for the A-sum warps, ring half c & 1 (two steps on).
+        umma_commit(empty_bar + 8 * s);
+        if (kk_a == kGroup - 1) umma_commit(a_empty + 8 * sa);
+        if (++s == kStages) {
+          s = 0;
+          ph ^= 1u;
+        }
+        if (++kk_a == kGroup) {
+          kk_a = 0;
+          if (++sa == kAStages) sa = 0;
+        }
+      }
+      // Always commit: the epilogue (or the teardown drain) waits on it.
+      umma_commit(acc_bar);
+    } else if (!kTs && lane == 0) {
       uint32_t written = 0;  // accumulators that already hold a product (accumulate flag)
       // Operand slot byte offsets of the seven products, resolved once.
       uint32_t a_off[7], b_off[7];
@@ -475,7 +647,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         tc_fence_after();
         const uint32_t a_stage = smem_base + s * kStageBytes;
-        const uint32_t b_stage = a_stage + kSlots * kASlotBytes;
+        const uint32_t b_stage = a_stage + P::B_OFFSET;
         const bool exact = kStrassen && kOpts && exact_chunk(p, c, kBlockK);
 #pragma unroll
         for (int kk = 0; kk < kBlockK / 16; ++kk) {
@@ -527,7 +699,82 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int sum_tid = threadIdx.x - kFirstSumWarp * 32;  // 0..255
     bool ok = true;
     // ------------------------------------------------------------ operand sums
-    if constexpr (kStrassen) {
+    if constexpr (kTs) {
+      // Two sets of four warps take alternate K steps (set = step & 1), so each
+      // warp's per-step chain (loads, ring wait, TMEM stores, fences) has two
+      // steps of time.  Within a set, warp w owns TMEM lane quarter w % 4.
+      // A sums: each thread owns one product row and reads that row's two
+      // 16-byte chunks of step kk (placed by the kAK*2-byte swizzle) from the four
+      // raw A quadrants, conflict-free; a0+a1 goes back to shared memory (slot 1),
+      // the other four sums to ring half (step & 1) in TMEM.  B sums: one 16-byte
+      // chunk of every B slot per thread, in place in shared memory.
+      constexpr int kGroup = kTsAK / 16;
+      constexpr uint32_t kRow = P::A_ROW;                        // bytes per tile row
+      static_assert(kBSlotBytes == 128 * 16, "one B chunk per thread of a set");
+      const int set = (warp - kFirstSumWarp) >> 2;
+      const int q = warp & 3;
+      const uint32_t row = 32 * q + lane;
+      const uint32_t xr = (row * kRow / 128) & (kRow / 16 - 1);  // swizzle of this row
+      const uint32_t tmem_lane = tmem_base + ((uint32_t)(32 * q) << 16) + kRingCol0;
+      const uint32_t b_off = 16 * row;
+      for (int c = set; c < p.num_chunks; c += 2) {
+        const int s = c % kStages;
+        const int g = c / kGroup;
+        const int sa = g % kAStages;
+        const uint32_t kk_a = c - g * kGroup;
+        // This set's first step of A group g waits for the group to land.
+        if (kk_a < 2 &&
+            !warp_wait(a_full + 8 * sa, (g / kAStages) & 1u, abort_flag, p.err, kErrWaitRaw)) {
+          ok = false;
+          break;
+        }
+        const uint32_t lo_off = kRow * row + 16 * ((2 * kk_a) ^ xr);
+        const uint32_t hi_off = kRow * row + 16 * ((2 * kk_a + 1) ^ xr);
+        const uint32_t a_stage = smem_base + sa * P::A_STAGE_BYTES;
+        uint4 lo[4], hi[4];
+#pragma unroll
+        for (int t = 0; t < 4; ++t) {
+          lo[t] = lds128(a_stage + t * kASlotBytes + lo_off);
+          hi[t] = lds128(a_stage + t * kASlotBytes + hi_off);
+        }
+        sts128(a_stage + 1 * kASlotBytes + lo_off, add4(lo[0], lo[1]));
+        sts128(a_stage + 1 * kASlotBytes + hi_off, add4(hi[0], hi[1]));
+        if (!warp_wait(full_bar + 8 * s, (c / kStages) & 1u, abort_flag, p.err, kErrWaitRaw)) {
+          ok = false;
+          break;
+        }
+        const uint32_t b_stage = smem_base + P::B_BASE + s * kStageBytes;
+        {
+          const uint4 b0 = lds128(b_stage + 0 * kBSlotBytes + b_off);
+          const uint4 b1 = lds128(b_stage + 1 * kBSlotBytes + b_off);
+          const uint4 b2 = lds128(b_stage + 2 * kBSlotBytes + b_off);
+          const uint4 b3 = lds128(b_stage + 3 * kBSlotBytes + b_off);
+          sts128(b_stage + 4 * kBSlotBytes + b_off, add4(b0, b3));
+          sts128(b_stage + 5 * kBSlotBytes + b_off, add4(b0, b1));
+          sts128(b_stage + 6 * kBSlotBytes + b_off, add4(b2, b3));
+          sts128(b_stage + 1 * kBSlotBytes + b_off, sub4(b1, b3));
+          sts128(b_stage + 2 * kBSlotBytes + b_off, sub4(b2, b0));
+        }
+        // Ring half c & 1 is free once the MMAs of step c - 2 completed: the
+        // commit that frees B stage (c - 2) % kStages.
+        if (c >= 2 && !warp_wait(empty_bar + 8 * ((c - 2) % kStages), ((c - 2) / kStages) & 1u,
+                                 abort_flag, p.err, kErrWaitEmpty)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t ring = tmem_lane + 32 * (c & 1);
+        tmem_store_8(ring + 0, add4(lo[0], lo[3]), add4(hi[0], hi[3]));   // a0+a3 (P1)
+        tmem_store_8(ring + 8, add4(lo[2], lo[3]), add4(hi[2], hi[3]));   // a2+a3 (P2)
+        tmem_store_8(ring + 16, sub4(lo[2], lo[0]), sub4(hi[2], hi[0]));  // a2-a0 (P6)
+        tmem_store_8(ring + 24, sub4(lo[1], lo[3]), sub4(hi[1], hi[3]));  // a1-a3 (P7)
+        tmem_store_wait();
+        fence_proxy_async_smem();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(sums_bar + 8 * s);
+      }
+    } else if constexpr (kStrassen) {
       for (int c = 0; c < p.num_chunks; ++c) {
         const int s = c % kStages;
         const uint32_t ph = (c / kStages) & 1u;
@@ -536,7 +783,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           break;
         }
         const uint32_t a_stage = smem_base + s * kStageBytes;
-        const uint32_t b_stage = a_stage + kSlots * kASlotBytes;
+        const uint32_t b_stage = a_stage + P::B_OFFSET;
         if (kOpts && exact_chunk(p, c, kBlockK)) {
           // Exact panels multiply the raw quadrants: leave them untouched.
         } else if (!kOpts || p.formula == 0) {
@@ -942,16 +1189,16 @@ template <bool kStrassen, int kEpi, bool kOutF32, bool kOpts, bool kATrans = fal
 int launch_typed(cudaStream_t stream, const CUtensorMap& ta, const CUtensorMap& tb,
                  const GemmParams& p) {
   auto kernel = strassen_gemm_kernel<kStrassen, kEpi, kOutF32, kOpts, kATrans>;
+  constexpr int kSmem = PipeFor<kStrassen, uses_tmem_a<kStrassen, kOpts, kATrans>()>::SMEM;
   static std::once_flag once;
   static cudaError_t attr_err = cudaSuccess;
   std::call_once(once, [&]() {
-    attr_err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                    PipeFor<kStrassen>::SMEM);
+    attr_err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
   });
   if (attr_err != cudaSuccess)
     return fail(SB_ERR_CUDA, std::string("cudaFuncSetAttribute: ") + cudaGetErrorString(attr_err));
   const unsigned grid = (unsigned)(p.tiles_m * p.tiles_n);
-  kernel<<<grid, kThreads, PipeFor<kStrassen>::SMEM, stream>>>(ta, tb, p);
+  kernel<<<grid, kThreads, kSmem, stream>>>(ta, tb, p);
   const cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return fail(SB_ERR_CUDA, std::string("kernel launch: ") + cudaGetErrorString(e));
   return SB_OK;
@@ -974,6 +1221,10 @@ int dispatch_strassen(int epi, bool out_f32, cudaStream_t stream, const CUtensor
     default: return fail(SB_ERR_EPILOGUE, "unknown epilogue kind");
   }
 }
+
+// A tile width (K) of the Strassen A tensor map: the default kernel reads
+// kTsAK-wide A groups, the research-option kernel 16-wide chunks.
+int strassen_a_chunk(bool options) { return SB_TMEM_A && !options ? kTsAK : StrassenPipe::BK; }
 
 int dispatch(bool strassen, int epi, bool out_f32, cudaStream_t stream, const CUtensorMap& ta,
              const CUtensorMap& tb, const GemmParams& p) {
@@ -1043,7 +1294,9 @@ int validate_core(const void* a, const void* b, const void* c, int64_t m, int64_
 }
 
 int make_maps(const void* a, const void* b, int64_t m, int64_t n, int64_t k, int64_t lda,
-              int64_t ldb, int32_t bm, int bk_chunk, CUtensorMap* ta, CUtensorMap* tb) {
+              int64_t ldb, int32_t bm, int bk_chunk, CUtensorMap* ta, CUtensorMap* tb,
+              int b_chunk = 0) {
+  if (b_chunk == 0) b_chunk = bk_chunk;
   const int a_row_bytes = bk_chunk * 2;
   EncodeTiledFn enc = encode_fn();
   if (!enc) return fail(SB_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
@@ -1067,7 +1320,7 @@ int make_maps(const void* a, const void* b, int64_t m, int64_t n, int64_t k, int
   {
     cuuint64_t dims[2] = {(cuuint64_t)n, (cuuint64_t)k};
     cuuint64_t strides[1] = {(cuuint64_t)ldb * 2};
-    cuuint32_t box[2] = {(cuuint32_t)kBlockN, (cuuint32_t)bk_chunk};
+    cuuint32_t box[2] = {(cuuint32_t)kBlockN, (cuuint32_t)b_chunk};
     cuuint32_t estr[2] = {1, 1};
     CUresult r = enc(tb, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(b), dims, strides, box,
                      estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
@@ -1196,7 +1449,8 @@ int sb_strassen_gemm_ex(sb_stream_t stream_, const void* a, const void* b, void*
   if (st != SB_OK) return st;
 
   CUtensorMap ta, tb;
-  st = make_maps(a, b, m, n, k, lda, ldb, bm, StrassenPipe::BK, &ta, &tb);
+  st = make_maps(a, b, m, n, k, lda, ldb, bm, strassen_a_chunk(formula != 0 || perm != 0 || schedule), &ta,
+                 &tb, StrassenPipe::BK);
   if (st != SB_OK) return st;
 
   if (epi == SB_EPI_NORM_RESIDUAL_ADD) {
@@ -1314,7 +1568,7 @@ extern "C" int sb_strassen_gemm_norm_residual_noalloc(sb_stream_t stream_, const
   st = noalloc_scratch_address(&scratch);
   if (st != SB_OK) return st;
   CUtensorMap ta, tb;
-  st = make_maps(a, b, m, n, k, lda, ldb, bm, StrassenPipe::BK, &ta, &tb);
+  st = make_maps(a, b, m, n, k, lda, ldb, bm, strassen_a_chunk(false), &ta, &tb, StrassenPipe::BK);
   if (st != SB_OK) return st;
   GemmParams p = base_params(m, n, k, bm, bn, bk, scratch, n, StrassenPipe::BK);
   st = dispatch(true, SB_EPI_NONE, true, stream, ta, tb, p);
