@@ -66,12 +66,6 @@ constexpr int kBlockN = 64;   // product columns per CTA = TMEM columns per prod
 #ifndef SB_TS_STAGES
 #define SB_TS_STAGES 6
 #endif
-#ifndef SB_TS_AK
-#define SB_TS_AK 64
-#endif
-#ifndef SB_TS_ASTAGES
-#define SB_TS_ASTAGES 2
-#endif
 #ifndef SB_TMEM_A
 #define SB_TMEM_A 1
 #endif
@@ -86,7 +80,10 @@ constexpr int kSumWarps = 8;
 constexpr int kSumThreads = kSumWarps * 32;
 constexpr int kThreads = (kFirstSumWarp + kSumWarps) * 32;  // 384
 constexpr uint32_t kTmemCols = 512;
-constexpr int kBarrierBytes = 256;
+#ifndef SB_BARRIER_BYTES
+#define SB_BARRIER_BYTES 256
+#endif
+constexpr int kBarrierBytes = SB_BARRIER_BYTES;
 constexpr int kRasterGroup = 16;  // product-row tiles per column sweep (L2 reuse)
 static_assert(7 * kBlockN <= (int)kTmemCols, "seven accumulators must fit in TMEM");
 
@@ -127,44 +124,39 @@ struct PipeCfg {
 using StrassenPipe = PipeCfg<SB_BLOCK_K, SB_STAGES, 7, 7>;
 using ClassicalPipe = PipeCfg<SB_C_BLOCK_K, SB_C_STAGES, 4, 4>;
 
-// Geometry of the default Strassen kernel (see uses_tmem_a): A and B have
-// separate pipelines.  An A stage holds the four raw A quadrant tiles of kAK
-// product columns (128 x kAK, K-major, kAK*2-byte swizzle) and serves kAK/16
-// K steps; a B stage holds one 16-deep step: four raw B quadrant tiles plus
-// the five B sums (16 x 64 each, N-major, 128-byte swizzle).  Wide A rows keep
-// the TMA row count per step low (128-byte rows: 128 + 64 rows per step
-// instead of 512 + 64 at 32-byte rows): the TMA engine moves roughly one row
-// per clock, which bound the 16-wide design.
-template <int kAK, int kAStages, int kBStages>
+// Geometry of the default Strassen kernel (see uses_tmem_a).  A stage holds one
+// 16-deep K step: the four raw A quadrant tiles (128 x 16, K-major, 32-byte
+// swizzle; a1's slot is overwritten with a0+a1) and the four raw B quadrant
+// tiles plus the five B sums (16 x 64, N-major, 128-byte swizzle).  The other
+// four A sums live in TMEM, so a stage is 30 KB and the ring is seven deep.
+// Each operand arrives in one TMA copy per step (make_ts_maps): the copy
+// engine's per-instruction cost, not its bandwidth, bounded four copies each.
+template <int kNumStages>
 struct TsPipeCfg {
   static constexpr int BK = 16;
-  static constexpr int AK = kAK;
-  static constexpr int STAGES = kBStages;
-  static constexpr int A_STAGES = kAStages;
-  static constexpr int A_SLOT = kBlockM * kAK * 2;
-  static constexpr int A_STAGE_BYTES = 4 * A_SLOT;
+  static constexpr int STAGES = kNumStages;
+  static constexpr int A_STAGES = 0;
+  static constexpr int A_STAGE_BYTES = 0;
+  static constexpr int B_BASE = 0;
+  static constexpr int A_SLOT = kBlockM * 16 * 2;
   static constexpr int B_SLOT = 16 * kBlockN * 2;
-  static constexpr int B_OFFSET = 0;
-  static constexpr int STAGE_BYTES = 7 * B_SLOT;  // one B stage
-  static constexpr int B_BASE = kAStages * A_STAGE_BYTES;
-  static constexpr int RAW_TX = 4 * B_SLOT;
-  static constexpr int DATA_BYTES = B_BASE + kBStages * STAGE_BYTES;
+  static constexpr int B_OFFSET = 4 * A_SLOT;
+  static constexpr int STAGE_BYTES = 4 * A_SLOT + 7 * B_SLOT;
+  static constexpr int RAW_TX = 4 * (A_SLOT + B_SLOT);
+  static constexpr int DATA_BYTES = kNumStages * STAGE_BYTES;
   static constexpr int SMEM = DATA_BYTES + kBarrierBytes + 1024;
-  static constexpr uint32_t A_ROW = kAK * 2;
-  static constexpr uint32_t A_LAYOUT = A_ROW == 32 ? kLayoutSwizzle32B
-                                       : A_ROW == 64 ? kLayoutSwizzle64B : kLayoutSwizzle128B;
+  static constexpr uint32_t A_ROW = 32;
+  static constexpr uint32_t A_LAYOUT = kLayoutSwizzle32B;
   static constexpr uint32_t A_SBO = 8 * A_ROW;
   static constexpr uint32_t A_LBO = 16;
   static constexpr uint32_t B_LAYOUT = kLayoutSwizzle128B;
   static constexpr uint32_t B_SBO = 1024;
   static constexpr uint32_t B_LBO = 16 * 128;
-  static_assert(kAK == 16 || kAK == 32 || kAK == 64, "A group must be one swizzle row");
-  static_assert(A_STAGE_BYTES % 1024 == 0 && STAGE_BYTES % 1024 == 0, "1024-byte stage alignment");
+  static_assert(STAGE_BYTES % 1024 == 0 && B_OFFSET % 1024 == 0, "1024-byte stage alignment");
   static_assert(SMEM <= 227 * 1024, "shared memory budget");
-  static_assert((3 * kBStages + 2 + 2 * kAStages) * 8 + 8 <= kBarrierBytes, "barrier area");
+  static_assert((3 * kNumStages + 2) * 8 + 8 <= kBarrierBytes, "barrier area");
 };
-using StrassenTsPipe = TsPipeCfg<SB_TS_AK, SB_TS_ASTAGES, SB_TS_STAGES>;
-constexpr int kTsAK = SB_TS_AK;
+using StrassenTsPipe = TsPipeCfg<SB_TS_STAGES>;
 
 // The default Strassen instantiation (classical formula, no research options,
 // A not transposed) keeps four of the five A operand sums in TMEM: a ring of
@@ -410,7 +402,6 @@ __global__ void __launch_bounds__(kThreads, 1)
   constexpr int kASlotBytes = P::A_SLOT;
   constexpr int kBSlotBytes = P::B_SLOT;
   constexpr int kBlockK = P::BK;
-  constexpr int kAStages = P::A_STAGES;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_addr = smem_addr(smem_raw);
   uint8_t* smem = smem_raw + ((1024u - (raw_addr & 1023u)) & 1023u);
@@ -422,10 +413,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t empty_bar = smem_addr(bars + 2 * kStages);  // [kStages] MMAs done reading
   const uint32_t acc_bar = smem_addr(bars + 3 * kStages);    // accumulators final
   const uint32_t qss_bar = smem_addr(bars + 3 * kStages + 1);  // q/k partial sums written
-  const uint32_t a_full = smem_addr(bars + 3 * kStages + 2);   // [kAStages] A group landed
-  const uint32_t a_empty = a_full + 8 * kAStages;              // [kAStages] MMAs done with it
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 3 * kStages + 2 + 2 * kAStages);
-  static_assert((3 * kStages + 2 + 2 * kAStages) * 8 + 8 <= kBarrierBytes, "barrier area");
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 3 * kStages + 2);
+  static_assert((3 * kStages + 2) * 8 + 8 <= kBarrierBytes, "barrier area");
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
 
   const int warp = threadIdx.x >> 5;
@@ -452,10 +441,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     mbar_init(acc_bar, 1);
     mbar_init(qss_bar, kSumWarps);
-    for (int s = 0; s < kAStages; ++s) {
-      mbar_init(a_full + 8 * s, 1);
-      mbar_init(a_empty + 8 * s, 1);
-    }
     *abort_flag = 0;
     fence_mbar_init();
     fence_proxy_async_smem();
@@ -474,58 +459,31 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ------------------------------------------------------------ TMA producer
     if constexpr (kTs) {
      if (lane == 0) {
-      // A every kAK/16 steps into the A ring, B every step into the B ring.
-      constexpr int kGroup = kTsAK / 16;
-      int a_last[kAStages > 0 ? kAStages : 1];
-      int b_last[kStages];
+      int last_issued[kStages];
 #pragma unroll
-      for (int s = 0; s < kAStages; ++s) a_last[s] = -1;
-#pragma unroll
-      for (int s = 0; s < kStages; ++s) b_last[s] = -1;
+      for (int s = 0; s < kStages; ++s) last_issued[s] = -1;
       const int a_row_base = t0 % p.half_bm;
       const int a_block = t0 / p.half_bm;
       const int j_block = u0 / p.half_bn;
       const int b_col0 = j_block * p.bn + (u0 % p.half_bn);
-      bool ok = true;
-      for (int c = 0; c < p.num_chunks && ok; ++c) {
-        const int kap = c * 16;
-        const int panel = kap / p.half_bk;
-        const int kin = kap - panel * p.half_bk;
-        if (c % kGroup == 0) {
-          const int g = c / kGroup;
-          const int sa = g % kAStages;
-          if (!mbar_wait(a_empty + 8 * sa, ((g / kAStages) & 1u) ^ 1u, abort_flag, p.err, kErrWaitEmpty)) break;
-          const uint32_t fa = a_full + 8 * sa;
-          mbar_arrive_expect_tx(fa, P::A_STAGE_BYTES);
-          const uint32_t a_stage = smem_base + sa * P::A_STAGE_BYTES;
-#pragma unroll
-          for (int qk = 0; qk < 2; ++qk)
-#pragma unroll
-            for (int qr = 0; qr < 2; ++qr)
-              tma_load_3d(a_stage + (2 * qr + qk) * kASlotBytes, &tmap_a, fa,
-                          panel * p.bk + qk * p.half_bk + kin, qr * p.half_bm + a_row_base, a_block);
-          a_last[sa] = g;
-        }
+      for (int c = 0; c < p.num_chunks; ++c) {
         const int s = c % kStages;
         if (!mbar_wait(empty_bar + 8 * s, ((c / kStages) & 1u) ^ 1u, abort_flag, p.err, kErrWaitEmpty)) break;
+        const int kap = c * 16;
+        const int panel = kap / p.half_bk;
+        const int kcol = panel * p.bk + (kap - panel * p.half_bk);
         const uint32_t fb = full_bar + 8 * s;
+        const uint32_t stage = smem_base + s * kStageBytes;
         mbar_arrive_expect_tx(fb, P::RAW_TX);
-        const uint32_t b_stage = smem_base + P::B_BASE + s * kStageBytes;
-#pragma unroll
-        for (int qk = 0; qk < 2; ++qk)
-#pragma unroll
-          for (int qc = 0; qc < 2; ++qc)
-            tma_load_2d(b_stage + (2 * qk + qc) * kBSlotBytes, &tmap_b, fb, b_col0 + qc * p.half_bn,
-                        panel * p.bk + qk * p.half_bk + kin);
-        b_last[s] = c;
+        // One copy per operand lands all four quadrants in slot order (make_ts_maps).
+        tma_load_5d(stage, &tmap_a, fb, kcol, a_row_base, a_block, 0, 0);
+        tma_load_4d(stage + P::B_OFFSET, &tmap_b, fb, b_col0, kcol, 0, 0);
+        last_issued[s] = c;
       }
       // Drain: never leave a TMA write in flight past teardown.
 #pragma unroll
-      for (int s = 0; s < kAStages; ++s)
-        if (a_last[s] >= 0) mbar_wait_drain(a_full + 8 * s, (a_last[s] / kAStages) & 1u);
-#pragma unroll
       for (int s = 0; s < kStages; ++s)
-        if (b_last[s] >= 0) mbar_wait_drain(full_bar + 8 * s, (b_last[s] / kStages) & 1u);
+        if (last_issued[s] >= 0) mbar_wait_drain(full_bar + 8 * s, (last_issued[s] / kStages) & 1u);
      }
     } else if (lane == 0) {
       int last_issued[kStages];
@@ -588,21 +546,20 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
     if (kTs && lane == 0) {
-      // One wait per K step: the sum warps arrive on sums_bar only after their
-      // A group and B stage landed, so it also covers the TMA data.  The issue
+      // One wait per K step: the sum warps arrive on sums_bar only after the
+      // stage's TMA copies landed, so it also covers the raw tiles.  The issue
       // queue is shallow, so every synchronisation in this thread idles the
       // tensor pipe: one wait and one commit per step, descriptors advanced by
       // adding (byte offset >> 4) to precomputed stage-0 descriptors.
-      constexpr int kGroup = kTsAK / 16;
       constexpr uint64_t kA = kASlotBytes >> 4, kB = kBSlotBytes >> 4;
       const uint64_t a_d0 = umma_smem_desc(smem_base, P::A_LBO, P::A_SBO, P::A_LAYOUT);
-      const uint64_t b_d0 = umma_smem_desc(smem_base + P::B_BASE, P::B_LBO, P::B_SBO, P::B_LAYOUT);
-      int s = 0, sa = 0, kk_a = 0;
+      const uint64_t b_d0 = umma_smem_desc(smem_base + P::B_OFFSET, P::B_LBO, P::B_SBO, P::B_LAYOUT);
+      int s = 0;
       uint32_t ph = 0;
       for (int c = 0; c < p.num_chunks; ++c) {
         if (!mbar_wait(sums_bar + 8 * s, ph, abort_flag, p.err, kErrWaitSums)) break;
         tc_fence_after();
-        const uint64_t ad = a_d0 + (uint32_t)((sa * P::A_STAGE_BYTES + kk_a * 32) >> 4);
+        const uint64_t ad = a_d0 + (uint32_t)((s * kStageBytes) >> 4);
         const uint64_t bd = b_d0 + (uint32_t)((s * kStageBytes) >> 4);
         const uint32_t acc = c != 0 ? 1u : 0u;
         const uint32_t ring = tmem_base + kRingCol0 + 32 * (c & 1);
@@ -613,16 +570,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         umma_bf16_ss(tmem_base + 4 * kBlockN, ad + 1 * kA, bd + 3 * kB, kIdesc, acc);     // (a0+a1) b3
         umma_bf16_ts(tmem_base + 5 * kBlockN, ring + 16, bd + 5 * kB, kIdesc, acc);       // (a2-a0)(b0+b1)
         umma_bf16_ts(tmem_base + 6 * kBlockN, ring + 24, bd + 6 * kB, kIdesc, acc);       // (a1-a3)(b2+b3)
-        // Frees B stage s and, for the A-sum warps, ring half c & 1 (two steps on).
+        // Frees stage s and, for the A-sum warps, ring half c & 1 (two steps on).
         umma_commit(empty_bar + 8 * s);
-        if (kk_a == kGroup - 1) umma_commit(a_empty + 8 * sa);
         if (++s == kStages) {
           s = 0;
           ph ^= 1u;
-        }
-        if (++kk_a == kGroup) {
-          kk_a = 0;
-          if (++sa == kAStages) sa = 0;
         }
       }
       // Always commit: the epilogue (or the teardown drain) waits on it.
@@ -704,33 +656,28 @@ __global__ void __launch_bounds__(kThreads, 1)
       // warp's per-step chain (loads, ring wait, TMEM stores, fences) has two
       // steps of time.  Within a set, warp w owns TMEM lane quarter w % 4.
       // A sums: each thread owns one product row and reads that row's two
-      // 16-byte chunks of step kk (placed by the kAK*2-byte swizzle) from the four
-      // raw A quadrants, conflict-free; a0+a1 goes back to shared memory (slot 1),
+      // 16-byte chunks from the four raw A quadrants, conflict-free (8 rows per
+      // wavefront); a0+a1 goes back to shared memory (slot 1),
       // the other four sums to ring half (step & 1) in TMEM.  B sums: one 16-byte
       // chunk of every B slot per thread, in place in shared memory.
-      constexpr int kGroup = kTsAK / 16;
-      constexpr uint32_t kRow = P::A_ROW;                        // bytes per tile row
       static_assert(kBSlotBytes == 128 * 16, "one B chunk per thread of a set");
       const int set = (warp - kFirstSumWarp) >> 2;
       const int q = warp & 3;
       const uint32_t row = 32 * q + lane;
-      const uint32_t xr = (row * kRow / 128) & (kRow / 16 - 1);  // swizzle of this row
+      // Row `row` of a 32-byte-swizzled A tile: its two 16-byte chunks swap
+      // places on rows with bit 2 set.
+      const uint32_t sw = (row >> 2) & 1u;
+      const uint32_t lo_off = 32 * row + 16 * sw;
+      const uint32_t hi_off = 32 * row + 16 * (sw ^ 1u);
       const uint32_t tmem_lane = tmem_base + ((uint32_t)(32 * q) << 16) + kRingCol0;
       const uint32_t b_off = 16 * row;
       for (int c = set; c < p.num_chunks; c += 2) {
         const int s = c % kStages;
-        const int g = c / kGroup;
-        const int sa = g % kAStages;
-        const uint32_t kk_a = c - g * kGroup;
-        // This set's first step of A group g waits for the group to land.
-        if (kk_a < 2 &&
-            !warp_wait(a_full + 8 * sa, (g / kAStages) & 1u, abort_flag, p.err, kErrWaitRaw)) {
+        if (!warp_wait(full_bar + 8 * s, (c / kStages) & 1u, abort_flag, p.err, kErrWaitRaw)) {
           ok = false;
           break;
         }
-        const uint32_t lo_off = kRow * row + 16 * ((2 * kk_a) ^ xr);
-        const uint32_t hi_off = kRow * row + 16 * ((2 * kk_a + 1) ^ xr);
-        const uint32_t a_stage = smem_base + sa * P::A_STAGE_BYTES;
+        const uint32_t a_stage = smem_base + s * kStageBytes;
         uint4 lo[4], hi[4];
 #pragma unroll
         for (int t = 0; t < 4; ++t) {
@@ -739,11 +686,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         sts128(a_stage + 1 * kASlotBytes + lo_off, add4(lo[0], lo[1]));
         sts128(a_stage + 1 * kASlotBytes + hi_off, add4(hi[0], hi[1]));
-        if (!warp_wait(full_bar + 8 * s, (c / kStages) & 1u, abort_flag, p.err, kErrWaitRaw)) {
-          ok = false;
-          break;
-        }
-        const uint32_t b_stage = smem_base + P::B_BASE + s * kStageBytes;
+        const uint32_t b_stage = a_stage + P::B_OFFSET;
         {
           const uint4 b0 = lds128(b_stage + 0 * kBSlotBytes + b_off);
           const uint4 b1 = lds128(b_stage + 1 * kBSlotBytes + b_off);
@@ -755,12 +698,19 @@ __global__ void __launch_bounds__(kThreads, 1)
           sts128(b_stage + 1 * kBSlotBytes + b_off, sub4(b1, b3));
           sts128(b_stage + 2 * kBSlotBytes + b_off, sub4(b2, b0));
         }
+        // Shared-memory sums are complete: order them for the tensor core now,
+        // so only the TMEM stores follow the ring wait.
+        fence_proxy_async_smem();
         // Ring half c & 1 is free once the MMAs of step c - 2 completed: the
-        // commit that frees B stage (c - 2) % kStages.
-        if (c >= 2 && !warp_wait(empty_bar + 8 * ((c - 2) % kStages), ((c - 2) / kStages) & 1u,
-                                 abort_flag, p.err, kErrWaitEmpty)) {
-          ok = false;
-          break;
+        // commit that frees B stage (c - 2) % kStages.  Every lane waits itself
+        // (no lane-0 poll and broadcast on this path).
+        if (c >= 2) {
+          const bool waited = mbar_wait(empty_bar + 8 * ((c - 2) % kStages), ((c - 2) / kStages) & 1u,
+                                        abort_flag, p.err, kErrWaitEmpty);
+          if (!__all_sync(0xffffffffu, waited)) {
+            ok = false;
+            break;
+          }
         }
         tc_fence_after();
         const uint32_t ring = tmem_lane + 32 * (c & 1);
@@ -769,7 +719,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         tmem_store_8(ring + 16, sub4(lo[2], lo[0]), sub4(hi[2], hi[0]));  // a2-a0 (P6)
         tmem_store_8(ring + 24, sub4(lo[1], lo[3]), sub4(hi[1], hi[3]));  // a1-a3 (P7)
         tmem_store_wait();
-        fence_proxy_async_smem();
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(sums_bar + 8 * s);
@@ -1222,10 +1171,6 @@ int dispatch_strassen(int epi, bool out_f32, cudaStream_t stream, const CUtensor
   }
 }
 
-// A tile width (K) of the Strassen A tensor map: the default kernel reads
-// kTsAK-wide A groups, the research-option kernel 16-wide chunks.
-int strassen_a_chunk(bool options) { return SB_TMEM_A && !options ? kTsAK : StrassenPipe::BK; }
-
 int dispatch(bool strassen, int epi, bool out_f32, cudaStream_t stream, const CUtensorMap& ta,
              const CUtensorMap& tb, const GemmParams& p) {
   if (!strassen) {
@@ -1294,9 +1239,7 @@ int validate_core(const void* a, const void* b, const void* c, int64_t m, int64_
 }
 
 int make_maps(const void* a, const void* b, int64_t m, int64_t n, int64_t k, int64_t lda,
-              int64_t ldb, int32_t bm, int bk_chunk, CUtensorMap* ta, CUtensorMap* tb,
-              int b_chunk = 0) {
-  if (b_chunk == 0) b_chunk = bk_chunk;
+              int64_t ldb, int32_t bm, int bk_chunk, CUtensorMap* ta, CUtensorMap* tb) {
   const int a_row_bytes = bk_chunk * 2;
   EncodeTiledFn enc = encode_fn();
   if (!enc) return fail(SB_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
@@ -1320,7 +1263,7 @@ int make_maps(const void* a, const void* b, int64_t m, int64_t n, int64_t k, int
   {
     cuuint64_t dims[2] = {(cuuint64_t)n, (cuuint64_t)k};
     cuuint64_t strides[1] = {(cuuint64_t)ldb * 2};
-    cuuint32_t box[2] = {(cuuint32_t)kBlockN, (cuuint32_t)b_chunk};
+    cuuint32_t box[2] = {(cuuint32_t)kBlockN, (cuuint32_t)bk_chunk};
     cuuint32_t estr[2] = {1, 1};
     CUresult r = enc(tb, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(b), dims, strides, box,
                      estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
@@ -1328,6 +1271,56 @@ int make_maps(const void* a, const void* b, int64_t m, int64_t n, int64_t k, int
     if (r != CUDA_SUCCESS) return fail(SB_ERR_CUDA, "cuTensorMapEncodeTiled(B) failed: " + std::to_string((int)r));
   }
   return SB_OK;
+}
+
+// Tensor maps of the default Strassen kernel: one TMA copy per A group and per
+// B step.  The quadrant offsets become tensor dimensions (strides need not
+// grow with the dimension index), ordered so the copy lays the four quadrant
+// tiles out contiguously in slot order:
+//   A: dims (k, row in half-block, block, qk, qr), strides (1, lda, bm*lda,
+//      half_bk, half_bm*lda) elements; box {16, rows, blocks, 2, 2} -> slot
+//      2*qr + qk, each tile `blocks` x `rows` = 128 rows of 16 columns.
+//   B: dims (n, k, qc, qk), strides (1, ldb, half_bn, half_bk*ldb); box
+//      {64, 16, 2, 2} -> slot 2*qk + qc, each 16 rows of 64 columns.
+int make_ts_maps(const void* a, const void* b, int64_t m, int64_t n, int64_t k, int64_t lda,
+                 int64_t ldb, int32_t bm, int32_t bn, int32_t bk, CUtensorMap* ta, CUtensorMap* tb) {
+  EncodeTiledFn enc = encode_fn();
+  if (!enc) return fail(SB_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
+  const int64_t half_bm = bm / 2, half_bn = bn / 2, half_bk = bk / 2;
+  const uint32_t rows = half_bm >= kBlockM ? kBlockM : (uint32_t)half_bm;
+  const uint32_t blocks = half_bm >= kBlockM ? 1 : (uint32_t)(kBlockM / half_bm);
+  {
+    cuuint64_t dims[5] = {(cuuint64_t)k, (cuuint64_t)half_bm, (cuuint64_t)(m / bm), 2, 2};
+    cuuint64_t strides[4] = {(cuuint64_t)(lda * 2), (cuuint64_t)(bm * lda * 2), (cuuint64_t)(half_bk * 2),
+                             (cuuint64_t)(half_bm * lda * 2)};
+    cuuint32_t box[5] = {16, rows, blocks, 2, 2};
+    cuuint32_t estr[5] = {1, 1, 1, 1, 1};
+    CUresult r = enc(ta, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 5, const_cast<void*>(a), dims, strides, box, estr,
+                     CU_TENSOR_MAP_INTERLEAVE_NONE,
+                     CU_TENSOR_MAP_SWIZZLE_32B,
+                     CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(SB_ERR_CUDA, "cuTensorMapEncodeTiled(A, 5-D) failed: " + std::to_string((int)r));
+  }
+  {
+    cuuint64_t dims[4] = {(cuuint64_t)n, (cuuint64_t)k, 2, 2};
+    cuuint64_t strides[3] = {(cuuint64_t)(ldb * 2), (cuuint64_t)(half_bn * 2), (cuuint64_t)(half_bk * ldb * 2)};
+    cuuint32_t box[4] = {(cuuint32_t)kBlockN, 16, 2, 2};
+    cuuint32_t estr[4] = {1, 1, 1, 1};
+    CUresult r = enc(tb, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(b), dims, strides, box, estr,
+                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                     CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(SB_ERR_CUDA, "cuTensorMapEncodeTiled(B, 4-D) failed: " + std::to_string((int)r));
+  }
+  return SB_OK;
+}
+
+// Tensor maps for a Strassen launch: the default kernel's (make_ts_maps) unless
+// research options select the 16-wide-chunk kernel.
+int make_strassen_maps(bool options, const void* a, const void* b, int64_t m, int64_t n, int64_t k,
+                       int64_t lda, int64_t ldb, int32_t bm, int32_t bn, int32_t bk, CUtensorMap* ta,
+                       CUtensorMap* tb) {
+  if (SB_TMEM_A && !options) return make_ts_maps(a, b, m, n, k, lda, ldb, bm, bn, bk, ta, tb);
+  return make_maps(a, b, m, n, k, lda, ldb, bm, StrassenPipe::BK, ta, tb);
 }
 
 GemmParams base_params(int64_t m, int64_t n, int64_t k, int32_t bm, int32_t bn, int32_t bk, void* c,
@@ -1449,8 +1442,8 @@ int sb_strassen_gemm_ex(sb_stream_t stream_, const void* a, const void* b, void*
   if (st != SB_OK) return st;
 
   CUtensorMap ta, tb;
-  st = make_maps(a, b, m, n, k, lda, ldb, bm, strassen_a_chunk(formula != 0 || perm != 0 || schedule), &ta,
-                 &tb, StrassenPipe::BK);
+  st = make_strassen_maps(formula != 0 || perm != 0 || schedule, a, b, m, n, k, lda, ldb, bm, bn, bk, &ta,
+                          &tb);
   if (st != SB_OK) return st;
 
   if (epi == SB_EPI_NORM_RESIDUAL_ADD) {
@@ -1568,7 +1561,7 @@ extern "C" int sb_strassen_gemm_norm_residual_noalloc(sb_stream_t stream_, const
   st = noalloc_scratch_address(&scratch);
   if (st != SB_OK) return st;
   CUtensorMap ta, tb;
-  st = make_maps(a, b, m, n, k, lda, ldb, bm, strassen_a_chunk(false), &ta, &tb, StrassenPipe::BK);
+  st = make_strassen_maps(false, a, b, m, n, k, lda, ldb, bm, bn, bk, &ta, &tb);
   if (st != SB_OK) return st;
   GemmParams p = base_params(m, n, k, bm, bn, bk, scratch, n, StrassenPipe::BK);
   st = dispatch(true, SB_EPI_NONE, true, stream, ta, tb, p);
