@@ -129,8 +129,8 @@ using ClassicalPipe = PipeCfg<SB_C_BLOCK_K, SB_C_STAGES, 4, 4>;
 // swizzle; a1's slot is overwritten with a0+a1) and the four raw B quadrant
 // tiles plus the five B sums (16 x 64, N-major, 128-byte swizzle).  The other
 // four A sums live in TMEM, so a stage is 30 KB and the ring is seven deep.
-// Each operand arrives in one TMA copy per step (make_ts_maps): the copy
-// engine's per-instruction cost, not its bandwidth, bounded four copies each.
+// Each operand arrives in one TMA copy per step (make_ts_maps) instead of one
+// copy per quadrant.
 template <int kNumStages>
 struct TsPipeCfg {
   static constexpr int BK = 16;
@@ -673,7 +673,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t b_off = 16 * row;
       for (int c = set; c < p.num_chunks; c += 2) {
         const int s = c % kStages;
-        if (!warp_wait(full_bar + 8 * s, (c / kStages) & 1u, abort_flag, p.err, kErrWaitRaw)) {
+        // Every lane waits itself: cheaper than a lane-0 poll and broadcast.
+        if (!__all_sync(0xffffffffu, mbar_wait(full_bar + 8 * s, (c / kStages) & 1u, abort_flag, p.err,
+                                               kErrWaitRaw))) {
           ok = false;
           break;
         }
