@@ -25,7 +25,6 @@ from .strassen import (
     strassen_matmul_lhs_transposed,
     workspace_bytes,
 )
-from .tuning import tuned_matmul
 
 __all__ = [
     "TUNED_BM", "TUNED_BN", "TUNED_BK",
@@ -35,3 +34,12 @@ __all__ = [
     "rope_layout_tables", "rope_layout_to_heads", "rope_scale_layout", "rope_weight_layout",
     "swiglu_weight_layout",
 ]
+
+
+def __getattr__(name):
+    # tuned_matmul lives in .tuning, imported on first use so that
+    # `python -m strassen_tpu_b200.tuning` does not import the module twice.
+    if name == "tuned_matmul":
+        from .tuning import tuned_matmul
+        return tuned_matmul
+    raise AttributeError(f"module {__name__!r} has no attribute {name!r}")
