@@ -56,6 +56,9 @@ def parse():
     p.add_argument("--backend", default="strassen", choices=["strassen", "native"],
                    help="decoder GEMM sites: sm_100a Strassen kernels or the cuBLAS classical arm")
     p.add_argument("--layers", type=int, default=None, help="decoder layers (default: the model's)")
+    p.add_argument("--chunks", type=int, default=None,
+                   help="decoder: token chunks pipelined so all-reduces overlap compute "
+                        "(default: 2 with more than one rank, else 1)")
     return p.parse_args()
 
 
@@ -388,13 +391,15 @@ def run_decoder(args):
         barrier()
         return max_over_ranks(s.elapsed_time(e))
 
+    chunks = args.chunks if args.chunks is not None else (2 if world > 1 else 1)
+
     with ClockSampler(device.index) as clocks:
-        ms = timed(lambda: model.forward(tokens, rope), args.steps, args.warmup) / args.steps
+        ms = timed(lambda: model.forward(tokens, rope, chunks=chunks), args.steps, args.warmup) / args.steps
     logits_host = torch.empty(batch, cfg.vocab, dtype=torch.bfloat16).pin_memory()
 
     def e2e_step():
         t = tokens_host.to(device, non_blocking=True)
-        logits_host.copy_(model.forward(t, rope), non_blocking=True)
+        logits_host.copy_(model.forward(t, rope, chunks=chunks), non_blocking=True)
 
     e2e_ms = timed(e2e_step, max(2, args.steps // 2), 1) / max(2, args.steps // 2)
     n_layers = len(model.blocks)
@@ -402,7 +407,8 @@ def run_decoder(args):
     strassen_sites = sorted(k for k, v in model.blocks[0].sites.items() if v.strassen)
     launches = 0
     if args.backend == "strassen":
-        launches = n_layers * (2 + len(strassen_sites))  # two RMSNorm rows + one GEMM per site
+        # two RMSNorm row passes + one GEMM per Strassen site, per block and token chunk
+        launches = n_layers * (2 + len(strassen_sites)) * (chunks if batch % chunks == 0 else 1)
     if world > 1:
         barrier()
         dist.destroy_process_group()
@@ -417,7 +423,7 @@ def run_decoder(args):
         "config": {"workload": args.workload, "model": args.workload, "global_batch": batch,
                    "seq_len": seq, "layers": n_layers, "parallelism": f"tp{world}",
                    "backend": args.backend, "strassen_sites": strassen_sites,
-                   "lm_head": "last position per sequence"},
+                   "token_chunks": chunks, "lm_head": "last position per sequence"},
         "achieved_tflops": flops / (ms * 1e-3) / 1e12,
         "e2e": {"value": tok / (e2e_ms * 1e-3), "unit": "tokens/s",
                 "h2d_bytes_per_step": tok * 8, "d2h_bytes_per_step": batch * cfg.vocab * 2},

@@ -85,6 +85,13 @@ class TensorParallel:
             self.dist.all_reduce(x, group=self.group)
         return x
 
+    def all_reduce_async(self, x: torch.Tensor):
+        """Start an in-place sum of x over the ranks; returns a handle whose wait()
+        orders the caller's stream after it (None on one rank)."""
+        if self.world > 1:
+            return self.dist.all_reduce(x, group=self.group, async_op=True)
+        return None
+
 
 def _pick_bn(width: int, preferred: int, minimum: int) -> int | None:
     """Largest bn <= preferred that is a multiple of `minimum` and of 256 and divides width."""
@@ -236,8 +243,9 @@ def _plain(layer: Qwen3Layer, name: str, h, residual=None):
     return out
 
 
-def layer_forward(layer: Qwen3Layer, x: torch.Tensor, batch: int, seq: int, rope) -> torch.Tensor:
-    """One decoder block on x [batch*seq, hidden] (bf16); returns the new hidden state."""
+def _attention_half(layer: Qwen3Layer, x: torch.Tensor, batch: int, seq: int, rope) -> torch.Tensor:
+    """ln1 -> q/k/v (fused qk_norm_rope) -> causal attention -> o projection with the
+    residual on rank 0: this rank's partial sum of the new hidden state."""
     cfg, tp = layer.cfg, layer.tp
     cos, sin, cos_laid, sin_laid = rope
     norm = sp.rms_norm if layer.backend == "strassen" else (lambda a, b, eps: rms_norm_torch(a, b, eps))
@@ -255,7 +263,14 @@ def layer_forward(layer: Qwen3Layer, x: torch.Tensor, batch: int, seq: int, rope
         v4 = v4.repeat_interleave(rep, dim=1)
     attn = F.scaled_dot_product_attention(q4, k4, v4, is_causal=True)
     attn = attn.transpose(1, 2).reshape(batch * seq, hq * hd)
-    x1 = tp.all_reduce(_plain(layer, "o", attn, residual=x if tp.rank == 0 else None))
+    return _plain(layer, "o", attn, residual=x if tp.rank == 0 else None)
+
+
+def _mlp_half(layer: Qwen3Layer, x1: torch.Tensor) -> torch.Tensor:
+    """ln2 -> gate/up (fused SwiGLU) -> down projection with the residual on rank 0:
+    this rank's partial sum of the block output."""
+    cfg, tp = layer.cfg, layer.tp
+    norm = sp.rms_norm if layer.backend == "strassen" else (lambda a, b, eps: rms_norm_torch(a, b, eps))
     h2 = norm(x1, layer.ln2, cfg.rms_eps)
     up = layer.sites["up"]
     if up.strassen:
@@ -265,7 +280,62 @@ def layer_forward(layer: Qwen3Layer, x: torch.Tensor, batch: int, seq: int, rope
         gu = sp.native_matmul(h2, up.weight).float()
         gate, upv = gu.chunk(2, dim=-1)
         g = (F.silu(gate) * upv).to(torch.bfloat16)
-    return tp.all_reduce(_plain(layer, "down", g, residual=x1 if tp.rank == 0 else None))
+    return _plain(layer, "down", g, residual=x1 if tp.rank == 0 else None)
+
+
+def layer_forward(layer: Qwen3Layer, x: torch.Tensor, batch: int, seq: int, rope) -> torch.Tensor:
+    """One decoder block on x [batch*seq, hidden] (bf16); returns the new hidden state.
+
+    The composition of benchmark_qwen3_32b_layer.py:344-398 with the row-parallel
+    o and down projections each followed by one all-reduce."""
+    tp = layer.tp
+    x1 = tp.all_reduce(_attention_half(layer, x, batch, seq, rope))
+    return tp.all_reduce(_mlp_half(layer, x1))
+
+
+def _chunk_rope(rope, lo: int, hi: int):
+    """Rows lo:hi of the per-token rope tables (the laid-out ones included)."""
+    cos, sin, cos_laid, sin_laid = rope
+    return (cos[lo:hi], sin[lo:hi], {k: v[lo:hi] for k, v in cos_laid.items()},
+            {k: v[lo:hi] for k, v in sin_laid.items()})
+
+
+def forward_blocks_chunked(blocks, x: torch.Tensor, batch: int, seq: int, rope, chunks: int) -> torch.Tensor:
+    """All decoder blocks on x, software-pipelined over `chunks` groups of whole
+    sequences so each chunk's all-reduces overlap the other chunks' compute.
+
+    Per block and chunk the math is exactly layer_forward's (attention never
+    crosses a sequence, every other op is per token); only the order changes:
+    chunk i's o-projection all-reduce runs while chunk i+1 computes attention,
+    and its down-projection all-reduce while the other chunks compute, up to the
+    next block's use of chunk i.
+    """
+    if chunks <= 1 or batch % chunks:
+        for blk in blocks:
+            x = layer_forward(blk, x, batch, seq, rope)
+        return x
+    tp = blocks[0].tp
+    per = batch // chunks
+    rows = per * seq
+    xs = [x[i * rows:(i + 1) * rows] for i in range(chunks)]
+    ropes = [_chunk_rope(rope, i * rows, (i + 1) * rows) for i in range(chunks)]
+    pending = [None] * chunks  # all-reduce in flight on xs[i]
+    for blk in blocks:
+        mids = []
+        for i in range(chunks):
+            if pending[i] is not None:
+                pending[i].wait()
+            part = _attention_half(blk, xs[i], per, seq, ropes[i])
+            mids.append((part, tp.all_reduce_async(part)))
+        for i, (x1, work) in enumerate(mids):
+            if work is not None:
+                work.wait()
+            xs[i] = _mlp_half(blk, x1)
+            pending[i] = tp.all_reduce_async(xs[i])
+    for work in pending:
+        if work is not None:
+            work.wait()
+    return torch.cat(xs)
 
 
 class Qwen3Prefill:
@@ -296,13 +366,16 @@ class Qwen3Prefill:
                     cos_laid[s.bn], sin_laid[s.bn] = c.contiguous(), si.contiguous()
         return cos, sin, cos_laid, sin_laid
 
-    def forward(self, tokens: torch.Tensor, rope=None) -> torch.Tensor:
-        """tokens [batch, seq] int64 -> logits [batch, vocab] of the last positions."""
+    def forward(self, tokens: torch.Tensor, rope=None, chunks: int = 1) -> torch.Tensor:
+        """tokens [batch, seq] int64 -> logits [batch, vocab] of the last positions.
+
+        chunks > 1 pipelines the blocks over groups of whole sequences so that
+        the all-reduces overlap compute (forward_blocks_chunked); batch must be a
+        multiple of chunks, else the blocks run unchunked."""
         batch, seq = tokens.shape
         rope = rope if rope is not None else self.rope(batch, seq)
         x = self.embed[tokens.reshape(-1)]
-        for blk in self.blocks:
-            x = layer_forward(blk, x, batch, seq, rope)
+        x = forward_blocks_chunked(self.blocks, x, batch, seq, rope, chunks)
         last = x.view(batch, seq, -1)[:, -1]
         last = rms_norm_torch(last, self.final_norm, self.cfg.rms_eps)
         return sp.native_matmul(last, self.lm_head)

@@ -36,13 +36,13 @@ def _tokens():
     return torch.randint(0, CFG.vocab, (BATCH, SEQ), generator=g)
 
 
-def _tp_worker(rank, world, port, out_path):
+def _tp_worker(rank, world, port, out_path, chunks=1):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=60))
     try:
         tp = qwen3.TensorParallel()
         model = qwen3.Qwen3Prefill(CFG, tp, "cpu", backend="native")
-        logits = model.forward(_tokens())
+        logits = model.forward(_tokens(), chunks=chunks)
         if rank == 0:
             torch.save(logits, out_path)
     finally:
@@ -124,3 +124,25 @@ def test_dead_rank_surfaces_as_an_error_not_a_hang(tmp_path):
     outcome, seconds = result.read_text().split()
     assert outcome.startswith("error:"), outcome
     assert float(seconds) < 30
+
+
+def test_chunked_pipeline_is_exact_on_one_rank():
+    # Chunks are whole sequences: every op is per token or per sequence, so the
+    # pipelined order changes nothing.
+    model = qwen3.Qwen3Prefill(CFG, qwen3.TensorParallel(), "cpu", backend="native")
+    tok = torch.randint(0, CFG.vocab, (4, SEQ), generator=torch.Generator().manual_seed(9))
+    want = model.forward(tok)
+    for chunks in (2, 4):
+        assert torch.equal(model.forward(tok, chunks=chunks), want)
+    assert torch.equal(model.forward(tok, chunks=3), want)  # 4 % 3: falls back to unchunked
+
+
+def test_tp2_chunked_matches_unchunked_on_cpu_ranks(tmp_path):
+    outs = []
+    for chunks in (1, 2):
+        out = tmp_path / f"tp2_c{chunks}.pt"
+        mp.spawn(_tp_worker, args=(2, _free_port(), str(out), chunks), nprocs=2, join=True)
+        outs.append(torch.load(out).float())
+    # The all-reduces sum the same partials; only their message sizes differ.
+    rel = (outs[1] - outs[0]).norm() / outs[0].norm()
+    assert rel < 1e-2, rel.item()
