@@ -387,6 +387,156 @@ __device__ __forceinline__ void read_quadrants(uint32_t tmem_row, int col, Quad8
   }
 }
 
+// Epilogue of one 128 x 64 product tile, run by the eight epilogue warps once
+// the accumulators are final: reads M1..M7 (or the quadrant accumulators) per
+// TMEM lane, recombines the quadrants and applies the fused epilogue
+// (strassen_pallas.py:739-879).  Product rows start at t0, columns at u0.
+template <bool kStrassen, int kEpi, bool kOutF32, bool kOpts>
+__device__ __forceinline__ void tile_epilogue(const GemmParams& p, uint32_t tmem_base, int t0, int u0,
+                                              int warp, int lane, uint8_t* smem, uint32_t qss_bar,
+                                              volatile int* abort_flag) {
+  const int q = warp & 3;                  // TMEM lane quarter this warp may read
+  const int h = (warp - kFirstSumWarp) >> 2;  // which 32-column half of the tile
+  const int row_in_tile = 32 * q + lane;
+  const int t = t0 + row_in_tile;
+  const bool row_ok = t < p.Mp;
+  const int blk_i = t / p.half_bm;
+  const int rp = t - blk_i * p.half_bm;
+  const int64_t row_top = (int64_t)blk_i * p.bm + rp;
+  const int64_t row_bot = row_top + p.half_bm;
+  const int j_block = u0 / p.half_bn;
+  const int cp_base = u0 - j_block * p.half_bn;  // column inside the half block
+  const int64_t col_left0 = (int64_t)j_block * p.bn + cp_base;
+  const uint32_t tmem_row = tmem_base + ((uint32_t)(32 * q) << 16);
+  const bool all_exact = kStrassen && kOpts && all_panels_exact(p);
+
+  if constexpr (kEpi == SB_EPI_QK_NORM_ROPE) {
+    // Per-head sum of squares over both halves of every head
+    // (strassen_pallas.py:793-835).  A head's a-half lies in quadrant 0/2,
+    // its b-half at the same offset in quadrant 1/3.  Pass 1 writes this
+    // thread's partial sums per head slot, pass 2 normalises and rotates.
+    float* qss = reinterpret_cast<float*>(smem);  // stage memory is idle now
+    bool return_early = false;
+    auto qidx = [&](int hh, int tb, int slot) { return ((hh * 2 + tb) * kBlockM + row_in_tile) * 8 + slot; };
+#pragma unroll
+    for (int slot = 0; slot < 8; ++slot) {
+      qss[qidx(h, 0, slot)] = 0.f;
+      qss[qidx(h, 1, slot)] = 0.f;
+    }
+#pragma unroll 1
+    for (int j = 0; j < 4; ++j) {
+      const int col = 32 * h + 8 * j;
+      Quad8 v;
+      read_quadrants<kStrassen, kOpts>(tmem_row, col, v, p, all_exact);
+      const int slot = col / p.half_head;
+      float st = 0.f, sbm = 0.f;
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        st += v.c[0][e] * v.c[0][e] + v.c[1][e] * v.c[1][e];
+        sbm += v.c[2][e] * v.c[2][e] + v.c[3][e] * v.c[3][e];
+      }
+      qss[qidx(h, 0, slot)] += st;
+      qss[qidx(h, 1, slot)] += sbm;
+    }
+    // Exchange partial sums between the two column halves (bounded wait).
+    __syncwarp();
+    if (lane == 0) mbar_arrive(qss_bar);
+    if (!warp_wait(qss_bar, 0, abort_flag, p.err, kErrWaitAcc)) return_early = true;
+    if (!return_early) {
+#pragma unroll 1
+    for (int j = 0; j < 4; ++j) {
+      const int col = 32 * h + 8 * j;
+      Quad8 v;
+      read_quadrants<kStrassen, kOpts>(tmem_row, col, v, p, all_exact);
+      const int slot = col / p.half_head;
+      const int cp = cp_base + col;
+#pragma unroll
+      for (int tb = 0; tb < 2; ++tb) {
+        const float sums = qss[qidx(0, tb, slot)] + qss[qidx(1, tb, slot)];
+        const float recip = 1.0f / sqrtf(sums * p.inv_head_dim + p.eps);
+        const int64_t row = tb ? row_bot : row_top;
+        float outa[8], outb[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          const float sa = load_aux(p.rope_scale, cp + e, p.aux_f32);
+          const float sbv = load_aux(p.rope_scale, p.half_bn + cp + e, p.aux_f32);
+          const float cs = row_ok ? load_aux(p.rope_cos, row * p.ld_rope + cp + e, p.aux_f32) : 0.f;
+          const float sn = row_ok ? load_aux(p.rope_sin, row * p.ld_rope + cp + e, p.aux_f32) : 0.f;
+          const float na = v.c[2 * tb][e] * recip * sa;
+          const float nb = v.c[2 * tb + 1][e] * recip * sbv;
+          outa[e] = na * cs - nb * sn;
+          outb[e] = nb * cs + na * sn;
+        }
+        if (row_ok) {
+          store8<kOutF32>(p.C, row * p.ldc + col_left0 + col, outa);
+          store8<kOutF32>(p.C, row * p.ldc + col_left0 + p.half_bn + col, outb);
+        }
+      }
+    }
+    }
+  } else {
+#pragma unroll 1
+    for (int j = 0; j < 4; ++j) {
+      const int col = 32 * h + 8 * j;
+      Quad8 v;
+      read_quadrants<kStrassen, kOpts>(tmem_row, col, v, p, all_exact);
+      if (!row_ok) continue;
+      const int64_t cl = col_left0 + col;
+      const int64_t cr = cl + p.half_bn;
+      if constexpr (kEpi == SB_EPI_SWIGLU || kEpi == SB_EPI_GEGLU) {
+        // strassen_pallas.py:762-777: quadrants 0/2 gate, 1/3 up; output
+        // column J*bn/2 + c'.
+        float top[8], bot[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          if constexpr (kEpi == SB_EPI_SWIGLU) {
+            top[e] = silu_f32(v.c[0][e]) * v.c[1][e];
+            bot[e] = silu_f32(v.c[2][e]) * v.c[3][e];
+          } else {
+            top[e] = gelu_tanh_f32(v.c[0][e]) * v.c[1][e];
+            bot[e] = gelu_tanh_f32(v.c[2][e]) * v.c[3][e];
+          }
+        }
+        const int64_t oc = (int64_t)j_block * p.half_bn + cp_base + col;
+        store8<kOutF32>(p.C, row_top * p.ldc + oc, top);
+        store8<kOutF32>(p.C, row_bot * p.ldc + oc, bot);
+      } else {
+        if constexpr (kEpi == SB_EPI_RESIDUAL_ADD) {
+          // strassen_pallas.py:778-792
+          float r[8];
+          load8(p.residual, row_top * p.ldr + cl, p.residual_f32, r);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) v.c[0][e] += r[e];
+          load8(p.residual, row_top * p.ldr + cr, p.residual_f32, r);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) v.c[1][e] += r[e];
+          load8(p.residual, row_bot * p.ldr + cl, p.residual_f32, r);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) v.c[2][e] += r[e];
+          load8(p.residual, row_bot * p.ldr + cr, p.residual_f32, r);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) v.c[3][e] += r[e];
+        } else if constexpr (kEpi == SB_EPI_BIAS_ADD) {
+          // strassen_pallas.py:867-874
+#pragma unroll
+          for (int e = 0; e < 8; ++e) {
+            const float bl = load_aux(p.bias, cl + e, p.aux_f32);
+            const float br = load_aux(p.bias, cr + e, p.aux_f32);
+            v.c[0][e] += bl;
+            v.c[2][e] += bl;
+            v.c[1][e] += br;
+            v.c[3][e] += br;
+          }
+        }
+        store8<kOutF32>(p.C, row_top * p.ldc + cl, v.c[0]);
+        store8<kOutF32>(p.C, row_top * p.ldc + cr, v.c[1]);
+        store8<kOutF32>(p.C, row_bot * p.ldc + cl, v.c[2]);
+        store8<kOutF32>(p.C, row_bot * p.ldc + cr, v.c[3]);
+      }
+    }
+  }
+}
+
 // kOpts compiles in the research options (dual formula, block permutation,
 // exact panels); the default launch uses the lean classical instantiation.
 // kATrans: A is stored transposed, (K, M) row-major (strassen_matmul_lhs_transposed);
@@ -839,146 +989,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ------------------------------------------------------------ epilogue
     if (ok && warp_wait(acc_bar, 0, abort_flag, p.err, kErrWaitAcc)) {
       tc_fence_after();
-      const int q = warp & 3;                  // TMEM lane quarter this warp may read
-      const int h = (warp - kFirstSumWarp) >> 2;  // which 32-column half of the tile
-      const int row_in_tile = 32 * q + lane;
-      const int t = t0 + row_in_tile;
-      const bool row_ok = t < p.Mp;
-      const int blk_i = t / p.half_bm;
-      const int rp = t - blk_i * p.half_bm;
-      const int64_t row_top = (int64_t)blk_i * p.bm + rp;
-      const int64_t row_bot = row_top + p.half_bm;
-      const int j_block = u0 / p.half_bn;
-      const int cp_base = u0 - j_block * p.half_bn;  // column inside the half block
-      const int64_t col_left0 = (int64_t)j_block * p.bn + cp_base;
-      const uint32_t tmem_row = tmem_base + ((uint32_t)(32 * q) << 16);
-      const bool all_exact = kStrassen && kOpts && all_panels_exact(p);
-
-      if constexpr (kEpi == SB_EPI_QK_NORM_ROPE) {
-        // Per-head sum of squares over both halves of every head
-        // (strassen_pallas.py:793-835).  A head's a-half lies in quadrant 0/2,
-        // its b-half at the same offset in quadrant 1/3.  Pass 1 writes this
-        // thread's partial sums per head slot, pass 2 normalises and rotates.
-        float* qss = reinterpret_cast<float*>(smem);  // stage memory is idle now
-        bool return_early = false;
-        auto qidx = [&](int hh, int tb, int slot) { return ((hh * 2 + tb) * kBlockM + row_in_tile) * 8 + slot; };
-#pragma unroll
-        for (int slot = 0; slot < 8; ++slot) {
-          qss[qidx(h, 0, slot)] = 0.f;
-          qss[qidx(h, 1, slot)] = 0.f;
-        }
-#pragma unroll 1
-        for (int j = 0; j < 4; ++j) {
-          const int col = 32 * h + 8 * j;
-          Quad8 v;
-          read_quadrants<kStrassen, kOpts>(tmem_row, col, v, p, all_exact);
-          const int slot = col / p.half_head;
-          float st = 0.f, sbm = 0.f;
-#pragma unroll
-          for (int e = 0; e < 8; ++e) {
-            st += v.c[0][e] * v.c[0][e] + v.c[1][e] * v.c[1][e];
-            sbm += v.c[2][e] * v.c[2][e] + v.c[3][e] * v.c[3][e];
-          }
-          qss[qidx(h, 0, slot)] += st;
-          qss[qidx(h, 1, slot)] += sbm;
-        }
-        // Exchange partial sums between the two column halves (bounded wait).
-        __syncwarp();
-        if (lane == 0) mbar_arrive(qss_bar);
-        if (!warp_wait(qss_bar, 0, abort_flag, p.err, kErrWaitAcc)) return_early = true;
-        if (!return_early) {
-#pragma unroll 1
-        for (int j = 0; j < 4; ++j) {
-          const int col = 32 * h + 8 * j;
-          Quad8 v;
-          read_quadrants<kStrassen, kOpts>(tmem_row, col, v, p, all_exact);
-          const int slot = col / p.half_head;
-          const int cp = cp_base + col;
-#pragma unroll
-          for (int tb = 0; tb < 2; ++tb) {
-            const float sums = qss[qidx(0, tb, slot)] + qss[qidx(1, tb, slot)];
-            const float recip = 1.0f / sqrtf(sums * p.inv_head_dim + p.eps);
-            const int64_t row = tb ? row_bot : row_top;
-            float outa[8], outb[8];
-#pragma unroll
-            for (int e = 0; e < 8; ++e) {
-              const float sa = load_aux(p.rope_scale, cp + e, p.aux_f32);
-              const float sbv = load_aux(p.rope_scale, p.half_bn + cp + e, p.aux_f32);
-              const float cs = row_ok ? load_aux(p.rope_cos, row * p.ld_rope + cp + e, p.aux_f32) : 0.f;
-              const float sn = row_ok ? load_aux(p.rope_sin, row * p.ld_rope + cp + e, p.aux_f32) : 0.f;
-              const float na = v.c[2 * tb][e] * recip * sa;
-              const float nb = v.c[2 * tb + 1][e] * recip * sbv;
-              outa[e] = na * cs - nb * sn;
-              outb[e] = nb * cs + na * sn;
-            }
-            if (row_ok) {
-              store8<kOutF32>(p.C, row * p.ldc + col_left0 + col, outa);
-              store8<kOutF32>(p.C, row * p.ldc + col_left0 + p.half_bn + col, outb);
-            }
-          }
-        }
-        }
-      } else {
-#pragma unroll 1
-        for (int j = 0; j < 4; ++j) {
-          const int col = 32 * h + 8 * j;
-          Quad8 v;
-          read_quadrants<kStrassen, kOpts>(tmem_row, col, v, p, all_exact);
-          if (!row_ok) continue;
-          const int64_t cl = col_left0 + col;
-          const int64_t cr = cl + p.half_bn;
-          if constexpr (kEpi == SB_EPI_SWIGLU || kEpi == SB_EPI_GEGLU) {
-            // strassen_pallas.py:762-777: quadrants 0/2 gate, 1/3 up; output
-            // column J*bn/2 + c'.
-            float top[8], bot[8];
-#pragma unroll
-            for (int e = 0; e < 8; ++e) {
-              if constexpr (kEpi == SB_EPI_SWIGLU) {
-                top[e] = silu_f32(v.c[0][e]) * v.c[1][e];
-                bot[e] = silu_f32(v.c[2][e]) * v.c[3][e];
-              } else {
-                top[e] = gelu_tanh_f32(v.c[0][e]) * v.c[1][e];
-                bot[e] = gelu_tanh_f32(v.c[2][e]) * v.c[3][e];
-              }
-            }
-            const int64_t oc = (int64_t)j_block * p.half_bn + cp_base + col;
-            store8<kOutF32>(p.C, row_top * p.ldc + oc, top);
-            store8<kOutF32>(p.C, row_bot * p.ldc + oc, bot);
-          } else {
-            if constexpr (kEpi == SB_EPI_RESIDUAL_ADD) {
-              // strassen_pallas.py:778-792
-              float r[8];
-              load8(p.residual, row_top * p.ldr + cl, p.residual_f32, r);
-#pragma unroll
-              for (int e = 0; e < 8; ++e) v.c[0][e] += r[e];
-              load8(p.residual, row_top * p.ldr + cr, p.residual_f32, r);
-#pragma unroll
-              for (int e = 0; e < 8; ++e) v.c[1][e] += r[e];
-              load8(p.residual, row_bot * p.ldr + cl, p.residual_f32, r);
-#pragma unroll
-              for (int e = 0; e < 8; ++e) v.c[2][e] += r[e];
-              load8(p.residual, row_bot * p.ldr + cr, p.residual_f32, r);
-#pragma unroll
-              for (int e = 0; e < 8; ++e) v.c[3][e] += r[e];
-            } else if constexpr (kEpi == SB_EPI_BIAS_ADD) {
-              // strassen_pallas.py:867-874
-#pragma unroll
-              for (int e = 0; e < 8; ++e) {
-                const float bl = load_aux(p.bias, cl + e, p.aux_f32);
-                const float br = load_aux(p.bias, cr + e, p.aux_f32);
-                v.c[0][e] += bl;
-                v.c[2][e] += bl;
-                v.c[1][e] += br;
-                v.c[3][e] += br;
-              }
-            }
-            store8<kOutF32>(p.C, row_top * p.ldc + cl, v.c[0]);
-            store8<kOutF32>(p.C, row_top * p.ldc + cr, v.c[1]);
-            store8<kOutF32>(p.C, row_bot * p.ldc + cl, v.c[2]);
-            store8<kOutF32>(p.C, row_bot * p.ldc + cr, v.c[3]);
-          }
-        }
-      }
+      tile_epilogue<kStrassen, kEpi, kOutF32, kOpts>(p, tmem_base, t0, u0, warp, lane, smem, qss_bar,
+                                                     abort_flag);
     }
   }
 
