@@ -164,7 +164,7 @@ using StrassenTsPipe = TsPipeCfg<SB_TS_STAGES>;
 // the seven accumulators, two K steps deep, and issues those four products
 // as A-from-TMEM MMAs, which takes their A operand off shared memory.
 template <bool kStrassen, bool kOpts, bool kATrans>
-constexpr bool uses_tmem_a() { return SB_TMEM_A && kStrassen && !kOpts && !kATrans; }
+constexpr bool uses_tmem_a() { return SB_TMEM_A && kStrassen && !kATrans; }
 constexpr int kRingSlots = 8;
 constexpr uint32_t kRingCol0 = 7 * kBlockN;  // 448
 static_assert(kRingCol0 + 8 * kRingSlots <= kTmemCols, "operand ring must fit in TMEM");
@@ -208,6 +208,19 @@ __constant__ int kExactA[12] = {0, 1, 0, 1, 2, 3, 2, 3, 0, 1, 2, 3};
 __constant__ int kExactB[12] = {0, 2, 1, 3, 0, 2, 1, 3, 1, 3, 0, 2};
 __constant__ int kExactNeg[2][12] = {{0, 0, 0, 0, 0, 0, 0, 0, 1, 1, 0, 0},
                                      {0, 0, 0, 0, 0, 0, 0, 0, 0, 0, 1, 1}};
+// The same exact-panel schedule as compile-time tables, for the MMA issuer of
+// the TMEM-ring layout (resolved into registers outside its loop).
+__device__ constexpr int kExactAccC[2][12] = {{6, 6, 2, 2, 1, 1, 5, 5, 5, 5, 5, 5}, {6, 6, 1, 1, 2, 2, 5, 5, 5, 5, 5, 5}};
+__device__ constexpr int kExactAC[12] = {0, 1, 0, 1, 2, 3, 2, 3, 0, 1, 2, 3};
+__device__ constexpr int kExactBC[12] = {0, 2, 1, 3, 0, 2, 1, 3, 1, 3, 0, 2};
+__device__ constexpr int kExactNegC[2][12] = {{0, 0, 0, 0, 0, 0, 0, 0, 1, 1, 0, 0}, {0, 0, 0, 0, 0, 0, 0, 0, 0, 0, 1, 1}};
+// TMEM-ring layout, per formula (classical, dual, powers) and product: the ring
+// slot of its A operand (-1: shared memory), its shared-memory A slot, its B
+// slot.  Slots 0-3 of the classical/dual rows are quadrant positions, which the
+// block permutation remaps; powers operands sit in fixed slots.
+__device__ constexpr int kProdRing[3][7] = {{0, 1, -1, -1, -1, 2, 3}, {0, -1, 1, -1, -1, 2, 3}, {0, 1, -1, -1, -1, 2, 3}};
+__device__ constexpr int kProdA[3][7] = {{0, 0, 0, 3, 1, 0, 0}, {0, 0, 0, 1, 3, 0, 0}, {0, 0, 0, 1, 2, 0, 0}};
+__device__ constexpr int kProdB[3][7] = {{4, 0, 1, 2, 3, 5, 6}, {4, 1, 0, 3, 2, 5, 6}, {0, 1, 2, 3, 4, 5, 6}};
 // Classical control: C0+=a0b0, C0+=a1b2, C1+=a0b1, C1+=a1b3, C2+=a2b0, C2+=a3b2,
 // C3+=a2b1, C3+=a3b3 (strassen_pallas.py:575-586 order).
 __constant__ int kCAslot[8] = {0, 1, 0, 1, 2, 3, 2, 3};
@@ -704,6 +717,40 @@ __global__ void __launch_bounds__(kThreads, 1)
       constexpr uint64_t kA = kASlotBytes >> 4, kB = kBSlotBytes >> 4;
       const uint64_t a_d0 = umma_smem_desc(smem_base, P::A_LBO, P::A_SBO, P::A_LAYOUT);
       const uint64_t b_d0 = umma_smem_desc(smem_base + P::B_OFFSET, P::B_LBO, P::B_SBO, P::B_LAYOUT);
+      // Research options: per product, the A operand (ring columns, or a shared-
+      // memory descriptor offset) and the B descriptor offset, resolved once into
+      // registers for the formula and block permutation; likewise the exact-step
+      // schedule.  The loop then only adds them to the stage descriptors.
+      uint32_t r_off[7], e_acc[12], e_neg[12];
+      uint64_t a_off[7], b_off[7], ea_off[12], eb_off[12];
+      bool from_ring[7];
+      uint32_t written = 0;  // accumulators holding a product (exact steps skip some)
+      bool exact_step = false;
+      if constexpr (kOpts) {
+        const int f = p.formula;
+        const int xa = 2 * p.swap_m + p.swap_k, xb = 2 * p.swap_k + p.swap_n;
+#pragma unroll
+        for (int i = 0; i < 7; ++i) {
+          const int rr = f == 0 ? kProdRing[0][i] : f == 1 ? kProdRing[1][i] : kProdRing[2][i];
+          int as = f == 0 ? kProdA[0][i] : f == 1 ? kProdA[1][i] : kProdA[2][i];
+          int bs = f == 0 ? kProdB[0][i] : f == 1 ? kProdB[1][i] : kProdB[2][i];
+          if (f != 2) {
+            as ^= xa;
+            if (bs < 4) bs ^= xb;
+          }
+          from_ring[i] = rr >= 0;
+          r_off[i] = rr >= 0 ? 8 * rr : 0;
+          a_off[i] = (uint64_t)as * kA;
+          b_off[i] = (uint64_t)bs * kB;
+        }
+#pragma unroll
+        for (int e = 0; e < 12; ++e) {
+          e_acc[e] = f == 1 ? kExactAccC[1][e] : kExactAccC[0][e];
+          e_neg[e] = f == 1 ? kExactNegC[1][e] : kExactNegC[0][e];
+          ea_off[e] = (uint64_t)(kExactAC[e] ^ xa) * kA;
+          eb_off[e] = (uint64_t)(kExactBC[e] ^ xb) * kB;
+        }
+      }
       int s = 0;
       uint32_t ph = 0;
       for (int c = 0; c < p.num_chunks; ++c) {
@@ -713,6 +760,35 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint64_t bd = b_d0 + (uint32_t)((s * kStageBytes) >> 4);
         const uint32_t acc = c != 0 ? 1u : 0u;
         const uint32_t ring = tmem_base + kRingCol0 + 32 * (c & 1);
+        if constexpr (kOpts) {
+          // The schedule entry changes only at K-panel boundaries.
+          if (p.panel_schedule != nullptr && (c * 16) % p.half_bk == 0) exact_step = exact_chunk(p, c, 16);
+          if (exact_step) {
+            // Exact classical step on the raw quadrants (see kExactAcc).
+#pragma unroll
+            for (int e = 0; e < 12; ++e) {
+              umma_bf16_ss(tmem_base + e_acc[e] * kBlockN, ad + ea_off[e], bd + eb_off[e],
+                           e_neg[e] ? kIdescNegA : kIdesc, (written >> e_acc[e]) & 1u);
+              written |= 1u << e_acc[e];
+            }
+          } else {
+#pragma unroll
+            for (int i = 0; i < 7; ++i) {
+              const uint32_t a_acc = (written >> i) & 1u;
+              if (from_ring[i])
+                umma_bf16_ts(tmem_base + i * kBlockN, ring + r_off[i], bd + b_off[i], kIdesc, a_acc);
+              else
+                umma_bf16_ss(tmem_base + i * kBlockN, ad + a_off[i], bd + b_off[i], kIdesc, a_acc);
+            }
+            written = 0x7Fu;
+          }
+          umma_commit(empty_bar + 8 * s);
+          if (++s == kStages) {
+            s = 0;
+            ph ^= 1u;
+          }
+          continue;
+        }
         umma_bf16_ts(tmem_base + 0 * kBlockN, ring + 0, bd + 4 * kB, kIdesc, acc);        // (a0+a3)(b0+b3)
         umma_bf16_ts(tmem_base + 1 * kBlockN, ring + 8, bd, kIdesc, acc);                 // (a2+a3) b0
         umma_bf16_ss(tmem_base + 2 * kBlockN, ad, bd + 1 * kB, kIdesc, acc);              // a0 (b1-b3)
@@ -807,9 +883,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       // steps of time.  Within a set, warp w owns TMEM lane quarter w % 4.
       // A sums: each thread owns one product row and reads that row's two
       // 16-byte chunks from the four raw A quadrants, conflict-free (8 rows per
-      // wavefront); a0+a1 goes back to shared memory (slot 1),
-      // the other four sums to ring half (step & 1) in TMEM.  B sums: one 16-byte
-      // chunk of every B slot per thread, in place in shared memory.
+      // wavefront); one A operand goes back to shared memory, four to ring half
+      // (step & 1) in TMEM.  B sums: one 16-byte chunk of every B slot per
+      // thread, in place in shared memory.
       static_assert(kBSlotBytes == 128 * 16, "one B chunk per thread of a set");
       const int set = (warp - kFirstSumWarp) >> 2;
       const int q = warp & 3;
@@ -821,6 +897,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t hi_off = 32 * row + 16 * (sw ^ 1u);
       const uint32_t tmem_lane = tmem_base + ((uint32_t)(32 * q) << 16) + kRingCol0;
       const uint32_t b_off = 16 * row;
+      const uint32_t xa = kOpts ? 2 * p.swap_m + p.swap_k : 0;  // block permutation
+      const uint32_t xb = kOpts ? 2 * p.swap_k + p.swap_n : 0;
+      bool exact = false;  // this step lies in an exact classical panel
       for (int c = set; c < p.num_chunks; c += 2) {
         const int s = c % kStages;
         // Every lane waits itself: cheaper than a lane-0 poll and broadcast.
@@ -830,47 +909,100 @@ __global__ void __launch_bounds__(kThreads, 1)
           break;
         }
         const uint32_t a_stage = smem_base + s * kStageBytes;
-        uint4 lo[4], hi[4];
-#pragma unroll
-        for (int t = 0; t < 4; ++t) {
-          lo[t] = lds128(a_stage + t * kASlotBytes + lo_off);
-          hi[t] = lds128(a_stage + t * kASlotBytes + hi_off);
-        }
-        sts128(a_stage + 1 * kASlotBytes + lo_off, add4(lo[0], lo[1]));
-        sts128(a_stage + 1 * kASlotBytes + hi_off, add4(hi[0], hi[1]));
         const uint32_t b_stage = a_stage + P::B_OFFSET;
-        {
-          const uint4 b0 = lds128(b_stage + 0 * kBSlotBytes + b_off);
-          const uint4 b1 = lds128(b_stage + 1 * kBSlotBytes + b_off);
-          const uint4 b2 = lds128(b_stage + 2 * kBSlotBytes + b_off);
-          const uint4 b3 = lds128(b_stage + 3 * kBSlotBytes + b_off);
-          sts128(b_stage + 4 * kBSlotBytes + b_off, add4(b0, b3));
-          sts128(b_stage + 5 * kBSlotBytes + b_off, add4(b0, b1));
-          sts128(b_stage + 6 * kBSlotBytes + b_off, add4(b2, b3));
-          sts128(b_stage + 1 * kBSlotBytes + b_off, sub4(b1, b3));
-          sts128(b_stage + 2 * kBSlotBytes + b_off, sub4(b2, b0));
+        // Research options: operand a_j / b_j of the block permutation sits in
+        // slot j ^ xa / j ^ xb; an exact classical step multiplies the raw
+        // quadrants and needs no sums.
+        // The schedule entry changes only at K-panel boundaries (a set sees a
+        // boundary step or the step after it, hence the two-step window).
+        if (kOpts && p.panel_schedule != nullptr && (c * 16) % p.half_bk < 32) exact = exact_chunk(p, c, 16);
+        uint4 rlo[4], rhi[4];  // the four A operands for the TMEM ring
+        if (!exact) {
+          uint4 lo[4], hi[4];
+#pragma unroll
+          for (int t = 0; t < 4; ++t) {
+            lo[t] = lds128(a_stage + (t ^ xa) * kASlotBytes + lo_off);
+            hi[t] = lds128(a_stage + (t ^ xa) * kASlotBytes + hi_off);
+          }
+          uint4 b[4];
+#pragma unroll
+          for (int t = 0; t < 4; ++t) b[t] = lds128(b_stage + (t ^ xb) * kBSlotBytes + b_off);
+          const int formula = kOpts ? p.formula : 0;
+          if (formula == 0) {
+            // Classical (strassen_pallas.py:324-379): a0+a1 over a1; ring
+            // a0+a3, a2+a3, a2-a0, a1-a3.
+            sts128(a_stage + (1 ^ xa) * kASlotBytes + lo_off, add4(lo[0], lo[1]));
+            sts128(a_stage + (1 ^ xa) * kASlotBytes + hi_off, add4(hi[0], hi[1]));
+            rlo[0] = add4(lo[0], lo[3]); rhi[0] = add4(hi[0], hi[3]);
+            rlo[1] = add4(lo[2], lo[3]); rhi[1] = add4(hi[2], hi[3]);
+            rlo[2] = sub4(lo[2], lo[0]); rhi[2] = sub4(hi[2], hi[0]);
+            rlo[3] = sub4(lo[1], lo[3]); rhi[3] = sub4(hi[1], hi[3]);
+            sts128(b_stage + 4 * kBSlotBytes + b_off, add4(b[0], b[3]));
+            sts128(b_stage + 5 * kBSlotBytes + b_off, add4(b[0], b[1]));
+            sts128(b_stage + 6 * kBSlotBytes + b_off, add4(b[2], b[3]));
+            sts128(b_stage + (1 ^ xb) * kBSlotBytes + b_off, sub4(b[1], b[3]));
+            sts128(b_stage + (2 ^ xb) * kBSlotBytes + b_off, sub4(b[2], b[0]));
+          } else if (formula == 1) {
+            // Dual (strassen_pallas.py:466-517): a1-a0 over a1; ring a0+a3,
+            // a2-a3, a0+a2, a1+a3.
+            sts128(a_stage + (1 ^ xa) * kASlotBytes + lo_off, sub4(lo[1], lo[0]));
+            sts128(a_stage + (1 ^ xa) * kASlotBytes + hi_off, sub4(hi[1], hi[0]));
+            rlo[0] = add4(lo[0], lo[3]); rhi[0] = add4(hi[0], hi[3]);
+            rlo[1] = sub4(lo[2], lo[3]); rhi[1] = sub4(hi[2], hi[3]);
+            rlo[2] = add4(lo[0], lo[2]); rhi[2] = add4(hi[0], hi[2]);
+            rlo[3] = add4(lo[1], lo[3]); rhi[3] = add4(hi[1], hi[3]);
+            sts128(b_stage + 4 * kBSlotBytes + b_off, add4(b[0], b[3]));
+            sts128(b_stage + 5 * kBSlotBytes + b_off, sub4(b[1], b[0]));
+            sts128(b_stage + 6 * kBSlotBytes + b_off, sub4(b[2], b[3]));
+            sts128(b_stage + (1 ^ xb) * kBSlotBytes + b_off, add4(b[1], b[3]));
+            sts128(b_stage + (2 ^ xb) * kBSlotBytes + b_off, add4(b[0], b[2]));
+          } else {
+            // Power-of-two formula (strassen_pallas.py:398-464), each bf16 op
+            // rounded in the reference's order: A3, A4, A5 into slots 0-2, ring
+            // A1, A2, A6, A7; B1..B7 into B slots 0-6.
+            const uint4 h1l = half4(lo[1]), h2l = half4(lo[2]), h3l = half4(lo[3]), q3l = quarter4(lo[3]);
+            const uint4 h1h = half4(hi[1]), h2h = half4(hi[2]), h3h = half4(hi[3]), q3h = quarter4(hi[3]);
+            rlo[0] = sub4(lo[2], lo[1]); rhi[0] = sub4(hi[2], hi[1]);
+            rlo[1] = add4(sub4(lo[0], h2l), sub4(h1l, q3l)); rhi[1] = add4(sub4(hi[0], h2h), sub4(h1h, q3h));
+            rlo[2] = add4(sub4(lo[0], h1l), sub4(h2l, q3l)); rhi[2] = add4(sub4(hi[0], h1h), sub4(h2h, q3h));
+            rlo[3] = add4(lo[1], h3l); rhi[3] = add4(hi[1], h3h);
+            sts128(a_stage + 0 * kASlotBytes + lo_off, sub4(lo[2], h3l));
+            sts128(a_stage + 0 * kASlotBytes + hi_off, sub4(hi[2], h3h));
+            sts128(a_stage + 1 * kASlotBytes + lo_off, sub4(lo[1], h3l));
+            sts128(a_stage + 1 * kASlotBytes + hi_off, sub4(hi[1], h3h));
+            sts128(a_stage + 2 * kASlotBytes + lo_off, add4(lo[2], h3l));
+            sts128(a_stage + 2 * kASlotBytes + hi_off, add4(hi[2], h3h));
+            const uint4 h0 = half4(b[0]), h1 = half4(b[1]), h3 = half4(b[3]), q1 = quarter4(b[1]);
+            sts128(b_stage + 0 * kBSlotBytes + b_off, sub4(b[0], b[3]));
+            sts128(b_stage + 1 * kBSlotBytes + b_off, add4(b[0], h1));
+            sts128(b_stage + 2 * kBSlotBytes + b_off, sub4(h1, b[3]));
+            sts128(b_stage + 3 * kBSlotBytes + b_off, add4(sub4(h0, b[2]), sub4(q1, h3)));
+            sts128(b_stage + 4 * kBSlotBytes + b_off, add4(h1, b[3]));
+            sts128(b_stage + 5 * kBSlotBytes + b_off, sub4(b[0], h1));
+            sts128(b_stage + 6 * kBSlotBytes + b_off, sub4(add4(h0, b[2]), add4(q1, h3)));
+          }
         }
         // Shared-memory sums are complete: order them for the tensor core now,
         // so only the TMEM stores follow the ring wait.
         fence_proxy_async_smem();
-        // Ring half c & 1 is free once the MMAs of step c - 2 completed: the
-        // commit that frees B stage (c - 2) % kStages.  Every lane waits itself
-        // (no lane-0 poll and broadcast on this path).
-        if (c >= 2) {
-          const bool waited = mbar_wait(empty_bar + 8 * ((c - 2) % kStages), ((c - 2) / kStages) & 1u,
-                                        abort_flag, p.err, kErrWaitEmpty);
-          if (!__all_sync(0xffffffffu, waited)) {
-            ok = false;
-            break;
+        if (!exact) {
+          // Ring half c & 1 is free once the MMAs of step c - 2 completed: the
+          // commit that frees stage (c - 2) % kStages.  Every lane waits itself
+          // (no lane-0 poll and broadcast on this path).
+          if (c >= 2) {
+            const bool waited = mbar_wait(empty_bar + 8 * ((c - 2) % kStages), ((c - 2) / kStages) & 1u,
+                                          abort_flag, p.err, kErrWaitEmpty);
+            if (!__all_sync(0xffffffffu, waited)) {
+              ok = false;
+              break;
+            }
           }
+          tc_fence_after();
+          const uint32_t ring = tmem_lane + 32 * (c & 1);
+#pragma unroll
+          for (int j = 0; j < 4; ++j) tmem_store_8(ring + 8 * j, rlo[j], rhi[j]);
+          tmem_store_wait();
         }
-        tc_fence_after();
-        const uint32_t ring = tmem_lane + 32 * (c & 1);
-        tmem_store_8(ring + 0, add4(lo[0], lo[3]), add4(hi[0], hi[3]));   // a0+a3 (P1)
-        tmem_store_8(ring + 8, add4(lo[2], lo[3]), add4(hi[2], hi[3]));   // a2+a3 (P2)
-        tmem_store_8(ring + 16, sub4(lo[2], lo[0]), sub4(hi[2], hi[0]));  // a2-a0 (P6)
-        tmem_store_8(ring + 24, sub4(lo[1], lo[3]), sub4(hi[1], hi[3]));  // a1-a3 (P7)
-        tmem_store_wait();
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(sums_bar + 8 * s);
@@ -1333,7 +1465,8 @@ int make_ts_maps(const void* a, const void* b, int64_t m, int64_t n, int64_t k, 
 int make_strassen_maps(bool options, const void* a, const void* b, int64_t m, int64_t n, int64_t k,
                        int64_t lda, int64_t ldb, int32_t bm, int32_t bn, int32_t bk, CUtensorMap* ta,
                        CUtensorMap* tb) {
-  if (SB_TMEM_A && !options) return make_ts_maps(a, b, m, n, k, lda, ldb, bm, bn, bk, ta, tb);
+  (void)options;
+  if (SB_TMEM_A) return make_ts_maps(a, b, m, n, k, lda, ldb, bm, bn, bk, ta, tb);
   return make_maps(a, b, m, n, k, lda, ldb, bm, StrassenPipe::BK, ta, tb);
 }
 
