@@ -158,11 +158,13 @@ struct TsPipeCfg {
 };
 using StrassenTsPipe = TsPipeCfg<SB_TS_STAGES>;
 
-// The default Strassen instantiation (classical formula, no research options,
-// A not transposed) keeps four of the five A operand sums in TMEM: a ring of
-// kRingSlots slots of 128 lanes x 8 columns (one 128 x 16 bf16 operand) after
-// the seven accumulators, two K steps deep, and issues those four products
-// as A-from-TMEM MMAs, which takes their A operand off shared memory.
+// Strassen launches with A stored row-major (the default and the research
+// options) keep four of the five A operand sums in TMEM: a ring of kRingSlots
+// slots of 128 lanes x 8 columns (one 128 x 16 bf16 operand) after the seven
+// accumulators, two K steps deep, and issue those four products as
+// A-from-TMEM MMAs, which takes their A operand off shared memory.  The
+// transposed-A launch (strassen_matmul_lhs_transposed) keeps the earlier layout
+// with all ten sums in shared memory.
 template <bool kStrassen, bool kOpts, bool kATrans>
 constexpr bool uses_tmem_a() { return SB_TMEM_A && kStrassen && !kATrans; }
 constexpr int kRingSlots = 8;
@@ -189,31 +191,16 @@ constexpr uint32_t kIdescAT = umma_idesc_bf16_f32(kBlockM, kBlockN, true, true);
 //   P5=(a0+a1)b3       P6=(a2-a0)(b0+b1)           P7=(a1-a3)(b2+b3)
 __constant__ int kASlot[7] = {4, 5, 0, 3, 1, 2, 6};
 __constant__ int kBSlot[7] = {4, 0, 1, 2, 3, 5, 6};
-// Dual formula (strassen_pallas.py:466-517), same in-place slot scheme:
-//   Q1=(a0+a3)(b0+b3)  Q2=a0(b1+b3)  Q3=(a2-a3)b0  Q4=(a1-a0)b3
-//   Q5=a3(b0+b2)       Q6=(a0+a2)(b1-b0)           Q7=(a1+a3)(b2-b3)
-//   A: 1 <- a1-a0  2 <- a2-a3  4 <- a0+a3  5 <- a0+a2  6 <- a1+a3
-//   B: 1 <- b1+b3  2 <- b0+b2  4 <- b0+b3  5 <- b1-b0  6 <- b2-b3
-__constant__ int kDualASlot[7] = {4, 0, 2, 1, 3, 5, 6};
-__constant__ int kDualBSlot[7] = {4, 1, 0, 3, 2, 5, 6};
 // Exact classical panel (strassen_pallas.py:575-586) expressed in the seven
 // accumulators, so the unchanged recombination yields C0 += a0b0+a1b2,
 // C1 += a0b1+a1b3, C2 += a2b0+a3b2, C3 += a2b1+a3b3:
 //   classical: acc6 += E0, acc2 += E1, acc1 += E2, acc5 += E3 - E1 + E2
 //   dual:      acc6 += E0, acc1 += E1, acc2 += E2, acc5 += E3 + E1 - E2
 // Entries: accumulator, A raw slot, B raw slot, negate (for the two formulas).
-__constant__ int kExactAcc[2][12] = {{6, 6, 2, 2, 1, 1, 5, 5, 5, 5, 5, 5},
-                                     {6, 6, 1, 1, 2, 2, 5, 5, 5, 5, 5, 5}};
-__constant__ int kExactA[12] = {0, 1, 0, 1, 2, 3, 2, 3, 0, 1, 2, 3};
-__constant__ int kExactB[12] = {0, 2, 1, 3, 0, 2, 1, 3, 1, 3, 0, 2};
-__constant__ int kExactNeg[2][12] = {{0, 0, 0, 0, 0, 0, 0, 0, 1, 1, 0, 0},
-                                     {0, 0, 0, 0, 0, 0, 0, 0, 0, 0, 1, 1}};
-// The same exact-panel schedule as compile-time tables, for the MMA issuer of
-// the TMEM-ring layout (resolved into registers outside its loop).
-__device__ constexpr int kExactAccC[2][12] = {{6, 6, 2, 2, 1, 1, 5, 5, 5, 5, 5, 5}, {6, 6, 1, 1, 2, 2, 5, 5, 5, 5, 5, 5}};
-__device__ constexpr int kExactAC[12] = {0, 1, 0, 1, 2, 3, 2, 3, 0, 1, 2, 3};
-__device__ constexpr int kExactBC[12] = {0, 2, 1, 3, 0, 2, 1, 3, 1, 3, 0, 2};
-__device__ constexpr int kExactNegC[2][12] = {{0, 0, 0, 0, 0, 0, 0, 0, 1, 1, 0, 0}, {0, 0, 0, 0, 0, 0, 0, 0, 0, 0, 1, 1}};
+__device__ constexpr int kExactAcc[2][12] = {{6, 6, 2, 2, 1, 1, 5, 5, 5, 5, 5, 5}, {6, 6, 1, 1, 2, 2, 5, 5, 5, 5, 5, 5}};
+__device__ constexpr int kExactA[12] = {0, 1, 0, 1, 2, 3, 2, 3, 0, 1, 2, 3};
+__device__ constexpr int kExactB[12] = {0, 2, 1, 3, 0, 2, 1, 3, 1, 3, 0, 2};
+__device__ constexpr int kExactNeg[2][12] = {{0, 0, 0, 0, 0, 0, 0, 0, 1, 1, 0, 0}, {0, 0, 0, 0, 0, 0, 0, 0, 0, 0, 1, 1}};
 // TMEM-ring layout, per formula (classical, dual, powers) and product: the ring
 // slot of its A operand (-1: shared memory), its shared-memory A slot, its B
 // slot.  Slots 0-3 of the classical/dual rows are quadrant positions, which the
@@ -550,8 +537,9 @@ __device__ __forceinline__ void tile_epilogue(const GemmParams& p, uint32_t tmem
   }
 }
 
-// kOpts compiles in the research options (dual formula, block permutation,
-// exact panels); the default launch uses the lean classical instantiation.
+// kOpts compiles in the research options (dual and power-of-two formulas,
+// block permutation, exact panels); the default launch uses the lean classical
+// instantiation.
 // kATrans: A is stored transposed, (K, M) row-major (strassen_matmul_lhs_transposed);
 // its tiles arrive M-major and feed the MMA as an MN-major operand.
 template <bool kStrassen, int kEpi, bool kOutF32, bool kOpts, bool kATrans = false>
@@ -559,6 +547,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     strassen_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a,
                          const __grid_constant__ CUtensorMap tmap_b, const GemmParams p) {
   constexpr bool kTs = uses_tmem_a<kStrassen, kOpts, kATrans>();
+  static_assert(!kOpts || kTs, "research options run on the TMEM-ring layout");
   using P = PipeFor<kStrassen, kTs>;
   constexpr int kStages = P::STAGES;
   constexpr int kStageBytes = P::STAGE_BYTES;
@@ -666,15 +655,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int panel = kap / p.half_bk;
         const int kin = kap - panel * p.half_bk;
         const uint32_t stage = smem_base + s * kStageBytes;
-        // Slot (2*qr + qk) of A holds the block's quadrant (qr^swap_m, qk^swap_k);
-        // slot (2*qk + qc) of B holds (qk^swap_k, qc^swap_n): the reference's
-        // block_permutation (strassen_pallas.py:205-226).
-        const int swap_m = kOpts ? p.swap_m : 0;
-        const int swap_k = kOpts ? p.swap_k : 0;
-        const int swap_n = kOpts ? p.swap_n : 0;
+        // Slot (2*qr + qk) of A holds the block's quadrant (qr, qk), slot
+        // (2*qk + qc) of B its quadrant (qk, qc).
 #pragma unroll
         for (int qk = 0; qk < 2; ++qk) {
-          const int kcol = panel * p.bk + (qk ^ swap_k) * p.half_bk + kin;
+          const int kcol = panel * p.bk + qk * p.half_bk + kin;
 #pragma unroll
           for (int qr = 0; qr < 2; ++qr) {
             if constexpr (kATrans) {
@@ -684,18 +669,18 @@ __global__ void __launch_bounds__(kThreads, 1)
               for (int h = 0; h < 2; ++h) {
                 const int t = t0 + 64 * h;
                 const int blk = t / p.half_bm;
-                const int m_coord = blk * p.bm + (qr ^ swap_m) * p.half_bm + (t - blk * p.half_bm);
+                const int m_coord = blk * p.bm + qr * p.half_bm + (t - blk * p.half_bm);
                 tma_load_2d(stage + (2 * qr + qk) * kASlotBytes + h * 2048, &tmap_a, fb, m_coord, kcol);
               }
             } else {
               tma_load_3d(stage + (2 * qr + qk) * kASlotBytes, &tmap_a, fb, kcol,
-                          (qr ^ swap_m) * p.half_bm + a_row_base, a_block);
+                          qr * p.half_bm + a_row_base, a_block);
             }
           }
 #pragma unroll
           for (int qc = 0; qc < 2; ++qc) {
             tma_load_2d(stage + P::B_OFFSET + (2 * qk + qc) * kBSlotBytes, &tmap_b, fb,
-                        b_col0 + (qc ^ swap_n) * p.half_bn, kcol);
+                        b_col0 + qc * p.half_bn, kcol);
           }
         }
         last_issued[s] = c;
@@ -708,7 +693,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
-    if (kTs && lane == 0) {
+    if constexpr (kTs) {
+     if (lane == 0) {
       // One wait per K step: the sum warps arrive on sums_bar only after the
       // stage's TMA copies landed, so it also covers the raw tiles.  The issue
       // queue is shallow, so every synchronisation in this thread idles the
@@ -745,10 +731,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
 #pragma unroll
         for (int e = 0; e < 12; ++e) {
-          e_acc[e] = f == 1 ? kExactAccC[1][e] : kExactAccC[0][e];
-          e_neg[e] = f == 1 ? kExactNegC[1][e] : kExactNegC[0][e];
-          ea_off[e] = (uint64_t)(kExactAC[e] ^ xa) * kA;
-          eb_off[e] = (uint64_t)(kExactBC[e] ^ xb) * kB;
+          e_acc[e] = f == 1 ? kExactAcc[1][e] : kExactAcc[0][e];
+          e_neg[e] = f == 1 ? kExactNeg[1][e] : kExactNeg[0][e];
+          ea_off[e] = (uint64_t)(kExactA[e] ^ xa) * kA;
+          eb_off[e] = (uint64_t)(kExactB[e] ^ xb) * kB;
         }
       }
       int s = 0;
@@ -805,16 +791,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       // Always commit: the epilogue (or the teardown drain) waits on it.
       umma_commit(acc_bar);
-    } else if (!kTs && lane == 0) {
-      uint32_t written = 0;  // accumulators that already hold a product (accumulate flag)
+     }
+    } else if (lane == 0) {
       // Operand slot byte offsets of the seven products, resolved once.
       uint32_t a_off[7], b_off[7];
 #pragma unroll
       for (int i = 0; i < 7; ++i) {
-        const int fa = !kOpts || p.formula == 0 ? kASlot[i] : p.formula == 1 ? kDualASlot[i] : i;
-        const int fb = !kOpts || p.formula == 0 ? kBSlot[i] : p.formula == 1 ? kDualBSlot[i] : i;
-        a_off[i] = fa * kASlotBytes;
-        b_off[i] = fb * kBSlotBytes;
+        a_off[i] = kASlot[i] * kASlotBytes;
+        b_off[i] = kBSlot[i] * kBSlotBytes;
       }
       for (int c = 0; c < p.num_chunks; ++c) {
         const int s = c % kStages;
@@ -826,35 +810,18 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_after();
         const uint32_t a_stage = smem_base + s * kStageBytes;
         const uint32_t b_stage = a_stage + P::B_OFFSET;
-        const bool exact = kStrassen && kOpts && exact_chunk(p, c, kBlockK);
 #pragma unroll
         for (int kk = 0; kk < kBlockK / 16; ++kk) {
           if constexpr (kStrassen) {
-            if (!exact) {
 #pragma unroll
-              for (int i = 0; i < 7; ++i) {
-                const uint64_t ad = kATrans
-                    ? umma_smem_desc(a_stage + a_off[i] + kk * 2048, 2048, 1024, kLayoutSwizzle128B)
-                    : umma_smem_desc(a_stage + a_off[i] + kk * 32, P::A_LBO, P::A_SBO, P::A_LAYOUT);
-                const uint64_t bd = umma_smem_desc(b_stage + b_off[i] + kk * 2048,
-                                                   P::B_LBO, P::B_SBO, P::B_LAYOUT);
-                umma_bf16_ss(tmem_base + i * kBlockN, ad, bd, kATrans ? kIdescAT : kIdesc,
-                             (written >> i) & 1u);
-              }
-              written = 0x7Fu;
-            } else {
-              // Exact classical panel on the raw quadrants (no operand sums).
-#pragma unroll
-              for (int e = 0; e < 12; ++e) {
-                const int acc = kExactAcc[p.formula][e];
-                const uint64_t ad = umma_smem_desc(a_stage + kExactA[e] * kASlotBytes + kk * 32,
-                                                   P::A_LBO, P::A_SBO, P::A_LAYOUT);
-                const uint64_t bd = umma_smem_desc(b_stage + kExactB[e] * kBSlotBytes + kk * 2048,
-                                                   P::B_LBO, P::B_SBO, P::B_LAYOUT);
-                umma_bf16_ss(tmem_base + acc * kBlockN, ad, bd,
-                             kExactNeg[p.formula][e] ? kIdescNegA : kIdesc, (written >> acc) & 1u);
-                written |= 1u << acc;
-              }
+            for (int i = 0; i < 7; ++i) {
+              const uint64_t ad = kATrans
+                  ? umma_smem_desc(a_stage + a_off[i] + kk * 2048, 2048, 1024, kLayoutSwizzle128B)
+                  : umma_smem_desc(a_stage + a_off[i] + kk * 32, P::A_LBO, P::A_SBO, P::A_LAYOUT);
+              const uint64_t bd = umma_smem_desc(b_stage + b_off[i] + kk * 2048,
+                                                 P::B_LBO, P::B_SBO, P::B_LAYOUT);
+              umma_bf16_ss(tmem_base + i * kBlockN, ad, bd, kATrans ? kIdescAT : kIdesc,
+                           (c | kk) != 0 ? 1u : 0u);
             }
           } else {
 #pragma unroll
@@ -1017,99 +984,33 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         const uint32_t a_stage = smem_base + s * kStageBytes;
         const uint32_t b_stage = a_stage + P::B_OFFSET;
-        if (kOpts && exact_chunk(p, c, kBlockK)) {
-          // Exact panels multiply the raw quadrants: leave them untouched.
-        } else if (!kOpts || p.formula == 0) {
+        {
 #pragma unroll
-          for (int idx = sum_tid; idx < kASlotBytes / 16; idx += kSumThreads) {
-            const uint32_t off = idx * 16;
-            const uint4 a0 = lds128(a_stage + 0 * kASlotBytes + off);
-            const uint4 a1 = lds128(a_stage + 1 * kASlotBytes + off);
-            const uint4 a2 = lds128(a_stage + 2 * kASlotBytes + off);
-            const uint4 a3 = lds128(a_stage + 3 * kASlotBytes + off);
-            sts128(a_stage + 4 * kASlotBytes + off, add4(a0, a3));
-            sts128(a_stage + 5 * kASlotBytes + off, add4(a2, a3));
-            sts128(a_stage + 6 * kASlotBytes + off, sub4(a1, a3));
-            sts128(a_stage + 1 * kASlotBytes + off, add4(a0, a1));
-            sts128(a_stage + 2 * kASlotBytes + off, sub4(a2, a0));
-          }
+        for (int idx = sum_tid; idx < kASlotBytes / 16; idx += kSumThreads) {
+          const uint32_t off = idx * 16;
+          const uint4 a0 = lds128(a_stage + 0 * kASlotBytes + off);
+          const uint4 a1 = lds128(a_stage + 1 * kASlotBytes + off);
+          const uint4 a2 = lds128(a_stage + 2 * kASlotBytes + off);
+          const uint4 a3 = lds128(a_stage + 3 * kASlotBytes + off);
+          sts128(a_stage + 4 * kASlotBytes + off, add4(a0, a3));
+          sts128(a_stage + 5 * kASlotBytes + off, add4(a2, a3));
+          sts128(a_stage + 6 * kASlotBytes + off, sub4(a1, a3));
+          sts128(a_stage + 1 * kASlotBytes + off, add4(a0, a1));
+          sts128(a_stage + 2 * kASlotBytes + off, sub4(a2, a0));
+        }
 #pragma unroll
-          for (int idx = sum_tid; idx < kBSlotBytes / 16; idx += kSumThreads) {
-            const uint32_t off = idx * 16;
-            const uint4 b0 = lds128(b_stage + 0 * kBSlotBytes + off);
-            const uint4 b1 = lds128(b_stage + 1 * kBSlotBytes + off);
-            const uint4 b2 = lds128(b_stage + 2 * kBSlotBytes + off);
-            const uint4 b3 = lds128(b_stage + 3 * kBSlotBytes + off);
-            sts128(b_stage + 4 * kBSlotBytes + off, add4(b0, b3));
-            sts128(b_stage + 5 * kBSlotBytes + off, add4(b0, b1));
-            sts128(b_stage + 6 * kBSlotBytes + off, add4(b2, b3));
-            sts128(b_stage + 1 * kBSlotBytes + off, sub4(b1, b3));
-            sts128(b_stage + 2 * kBSlotBytes + off, sub4(b2, b0));
-          }
-        } else if (p.formula == 2) {
-          // Power-of-two formula (strassen_pallas.py:398-464): all seven operands
-          // per side are computed (each bf16 op rounds, in the reference's
-          // order) and written over slots 0..6, operand i-1 for product Ri.
-#pragma unroll
-          for (int idx = sum_tid; idx < kASlotBytes / 16; idx += kSumThreads) {
-            const uint32_t off = idx * 16;
-            const uint4 a0 = lds128(a_stage + 0 * kASlotBytes + off);
-            const uint4 a1 = lds128(a_stage + 1 * kASlotBytes + off);
-            const uint4 a2 = lds128(a_stage + 2 * kASlotBytes + off);
-            const uint4 a3 = lds128(a_stage + 3 * kASlotBytes + off);
-            const uint4 h1 = half4(a1), h2 = half4(a2), h3 = half4(a3), q3 = quarter4(a3);
-            sts128(a_stage + 0 * kASlotBytes + off, sub4(a2, a1));
-            sts128(a_stage + 1 * kASlotBytes + off, add4(sub4(a0, h2), sub4(h1, q3)));
-            sts128(a_stage + 2 * kASlotBytes + off, sub4(a2, h3));
-            sts128(a_stage + 3 * kASlotBytes + off, sub4(a1, h3));
-            sts128(a_stage + 4 * kASlotBytes + off, add4(a2, h3));
-            sts128(a_stage + 5 * kASlotBytes + off, add4(sub4(a0, h1), sub4(h2, q3)));
-            sts128(a_stage + 6 * kASlotBytes + off, add4(a1, h3));
-          }
-#pragma unroll
-          for (int idx = sum_tid; idx < kBSlotBytes / 16; idx += kSumThreads) {
-            const uint32_t off = idx * 16;
-            const uint4 b0 = lds128(b_stage + 0 * kBSlotBytes + off);
-            const uint4 b1 = lds128(b_stage + 1 * kBSlotBytes + off);
-            const uint4 b2 = lds128(b_stage + 2 * kBSlotBytes + off);
-            const uint4 b3 = lds128(b_stage + 3 * kBSlotBytes + off);
-            const uint4 h0 = half4(b0), h1 = half4(b1), h3 = half4(b3), q1 = quarter4(b1);
-            sts128(b_stage + 0 * kBSlotBytes + off, sub4(b0, b3));
-            sts128(b_stage + 1 * kBSlotBytes + off, add4(b0, h1));
-            sts128(b_stage + 2 * kBSlotBytes + off, sub4(h1, b3));
-            sts128(b_stage + 3 * kBSlotBytes + off, add4(sub4(h0, b2), sub4(q1, h3)));
-            sts128(b_stage + 4 * kBSlotBytes + off, add4(h1, b3));
-            sts128(b_stage + 5 * kBSlotBytes + off, sub4(b0, h1));
-            sts128(b_stage + 6 * kBSlotBytes + off, sub4(add4(h0, b2), add4(q1, h3)));
-          }
-        } else {
-          // Dual formula operand sums (strassen_pallas.py:466-517).
-#pragma unroll
-          for (int idx = sum_tid; idx < kASlotBytes / 16; idx += kSumThreads) {
-            const uint32_t off = idx * 16;
-            const uint4 a0 = lds128(a_stage + 0 * kASlotBytes + off);
-            const uint4 a1 = lds128(a_stage + 1 * kASlotBytes + off);
-            const uint4 a2 = lds128(a_stage + 2 * kASlotBytes + off);
-            const uint4 a3 = lds128(a_stage + 3 * kASlotBytes + off);
-            sts128(a_stage + 4 * kASlotBytes + off, add4(a0, a3));
-            sts128(a_stage + 5 * kASlotBytes + off, add4(a0, a2));
-            sts128(a_stage + 6 * kASlotBytes + off, add4(a1, a3));
-            sts128(a_stage + 1 * kASlotBytes + off, sub4(a1, a0));
-            sts128(a_stage + 2 * kASlotBytes + off, sub4(a2, a3));
-          }
-#pragma unroll
-          for (int idx = sum_tid; idx < kBSlotBytes / 16; idx += kSumThreads) {
-            const uint32_t off = idx * 16;
-            const uint4 b0 = lds128(b_stage + 0 * kBSlotBytes + off);
-            const uint4 b1 = lds128(b_stage + 1 * kBSlotBytes + off);
-            const uint4 b2 = lds128(b_stage + 2 * kBSlotBytes + off);
-            const uint4 b3 = lds128(b_stage + 3 * kBSlotBytes + off);
-            sts128(b_stage + 4 * kBSlotBytes + off, add4(b0, b3));
-            sts128(b_stage + 5 * kBSlotBytes + off, sub4(b1, b0));
-            sts128(b_stage + 6 * kBSlotBytes + off, sub4(b2, b3));
-            sts128(b_stage + 1 * kBSlotBytes + off, add4(b1, b3));
-            sts128(b_stage + 2 * kBSlotBytes + off, add4(b0, b2));
-          }
+        for (int idx = sum_tid; idx < kBSlotBytes / 16; idx += kSumThreads) {
+          const uint32_t off = idx * 16;
+          const uint4 b0 = lds128(b_stage + 0 * kBSlotBytes + off);
+          const uint4 b1 = lds128(b_stage + 1 * kBSlotBytes + off);
+          const uint4 b2 = lds128(b_stage + 2 * kBSlotBytes + off);
+          const uint4 b3 = lds128(b_stage + 3 * kBSlotBytes + off);
+          sts128(b_stage + 4 * kBSlotBytes + off, add4(b0, b3));
+          sts128(b_stage + 5 * kBSlotBytes + off, add4(b0, b1));
+          sts128(b_stage + 6 * kBSlotBytes + off, add4(b2, b3));
+          sts128(b_stage + 1 * kBSlotBytes + off, sub4(b1, b3));
+          sts128(b_stage + 2 * kBSlotBytes + off, sub4(b2, b0));
+        }
         }
         // Make the generic-proxy writes visible to the tensor core, then signal.
         fence_proxy_async_smem();
