@@ -332,6 +332,103 @@ def strassen_matmul(
     return out
 
 
+_SIDE_STREAMS: dict = {}
+
+
+def _side_streams(device: torch.device):
+    """The two copy streams of a device (host->device, device->host), created once."""
+    key = device.index
+    if key not in _SIDE_STREAMS:
+        _SIDE_STREAMS[key] = (torch.cuda.Stream(device), torch.cuda.Stream(device))
+    return _SIDE_STREAMS[key]
+
+
+_UNSTREAMED = ("residual", "bias", "rope_cos", "rope_sin", "rope_scale", "norm_scale", "out", "workspace")
+
+
+def strassen_matmul_streamed(a, b, *, bm=TUNED_BM, bn=TUNED_BN, bk=TUNED_BK, device=None, out=None,
+                             row_chunk=None, **kwargs):
+    """``strassen_matmul`` for host-resident operands, with the transfers overlapped.
+
+    ``a`` [M, K] and ``b`` [K, N] are CPU tensors (pinned memory makes the copies
+    asynchronous); the product lands in ``out``, a CPU tensor (pinned, allocated
+    when omitted).  B is copied to ``device`` first, then A in chunks of
+    ``row_chunk`` rows (a multiple of bm; default M/8 rounded to whole blocks) on
+    a copy stream.  Each chunk's GEMM runs on the current stream as soon as its
+    rows have landed, and its result rows return on a second copy stream while
+    later chunks compute, so the transfer time, not the sum of transfers and
+    compute, bounds the call.  Strassen block rows are independent: the result
+    equals one ``strassen_matmul`` call bit for bit.
+
+    The copies are asynchronous: ``out`` is complete once the current CUDA stream
+    has reached the end of this call (``torch.cuda.current_stream().synchronize()``).
+    Epilogues that read extra row-indexed operands (residual, rope tables,
+    norm_scale, bias) are not streamed; call ``strassen_matmul`` with device
+    tensors for those.  Other keyword arguments go to ``strassen_matmul``.
+    """
+    if a.dim() != 2 or b.dim() != 2:
+        raise ValueError("strassen_matmul expects two rank-2 matrices")
+    if a.is_cuda or b.is_cuda:
+        raise ValueError("strassen_matmul_streamed takes host (CPU) tensors; use strassen_matmul on device tensors")
+    for name in _UNSTREAMED:
+        if kwargs.get(name) is not None:
+            raise ValueError(f"{name}= is not streamed; call strassen_matmul with device tensors")
+    m, k = a.shape
+    k2, n = b.shape
+    if k != k2:
+        raise ValueError(f"inner dimensions disagree: {k} vs {k2}")
+    if m % bm:
+        raise ValueError(f"M={m} is not divisible by {bm}")
+    blocks = m // bm
+    if row_chunk is None:
+        per = max(1, blocks // 8)
+        while blocks % per:
+            per -= 1
+        row_chunk = per * bm
+    if row_chunk <= 0 or row_chunk % bm or m % row_chunk:
+        raise ValueError(f"row_chunk={row_chunk} must be a positive multiple of bm={bm} that divides M={m}")
+    dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+    out_dt = _as_torch_dtype(kwargs.get("output_dtype")) or torch.bfloat16
+    out_cols = n // 2 if kwargs.get("epilogue") in ("swiglu", "geglu") else n
+    if out is None:
+        out = torch.empty((m, out_cols), dtype=out_dt, pin_memory=True)
+    elif out.is_cuda or tuple(out.shape) != (m, out_cols) or out.dtype != out_dt or not out.is_contiguous():
+        raise ValueError(f"out must be a contiguous ({m}, {out_cols}) {_dtype_name(out_dt)} CPU tensor")
+
+    h2d, d2h = _side_streams(dev)
+    cur = torch.cuda.current_stream(dev)
+    a_dev = torch.empty((m, k), dtype=a.dtype, device=dev)
+    b_dev = torch.empty((k, n), dtype=b.dtype, device=dev)
+    c_dev = torch.empty((m, out_cols), dtype=out_dt, device=dev)
+    # The copy streams start after the work already queued on the current stream.
+    h2d.wait_stream(cur)
+    d2h.wait_stream(cur)
+    chunks = [(i, i + row_chunk) for i in range(0, m, row_chunk)]
+    landed = []
+    with torch.cuda.stream(h2d):
+        b_dev.copy_(b, non_blocking=True)
+        for lo, hi in chunks:
+            a_dev[lo:hi].copy_(a[lo:hi], non_blocking=True)
+            ev = torch.cuda.Event()
+            ev.record(h2d)
+            landed.append(ev)  # also implies B has landed (same stream, earlier)
+    for (lo, hi), ev in zip(chunks, landed):
+        cur.wait_event(ev)
+        strassen_matmul(a_dev[lo:hi], b_dev, bm=bm, bn=bn, bk=bk, out=c_dev[lo:hi], **kwargs)
+        done = torch.cuda.Event()
+        done.record(cur)
+        d2h.wait_event(done)
+        with torch.cuda.stream(d2h):
+            out[lo:hi].copy_(c_dev[lo:hi], non_blocking=True)
+    cur.wait_stream(d2h)
+    # The device buffers were allocated on the current stream but are used on the
+    # copy streams: keep the caching allocator from reusing them too early.
+    a_dev.record_stream(h2d)
+    b_dev.record_stream(h2d)
+    c_dev.record_stream(d2h)
+    return out
+
+
 def strassen_matmul_lhs_transposed(
     a,
     b,

@@ -130,3 +130,16 @@ def test_check_tiling_message():
     assert "bn=128 must be a multiple of 256" in msg
     assert "bk=100 must be a multiple of 256" in msg
     sb.check_tiling(16, 256, 256)
+
+
+def test_streamed_validates_before_touching_the_device():
+    a = torch.zeros(2048, 512, dtype=torch.bfloat16)
+    b = torch.zeros(512, 1024, dtype=torch.bfloat16)
+    with pytest.raises(ValueError, match="residual= is not streamed"):
+        sb.strassen_matmul_streamed(a, b, bm=1024, bn=1024, bk=512, epilogue="residual_add", residual=a)
+    with pytest.raises(ValueError, match="row_chunk=1536"):
+        sb.strassen_matmul_streamed(a, b, bm=1024, bn=1024, bk=512, row_chunk=1536)
+    with pytest.raises(ValueError, match="inner dimensions disagree"):
+        sb.strassen_matmul_streamed(a, b.t(), bm=1024, bn=1024, bk=512)
+    with pytest.raises(ValueError, match="is not divisible by"):
+        sb.strassen_matmul_streamed(a[:1536], b, bm=1024, bn=1024, bk=512)

@@ -266,3 +266,18 @@ def test_lhs_transposed_exact_integers():
         got = host(sb.strassen_matmul_lhs_transposed(dev_bf16(at), dev_bf16(b), bm=tile[0], bn=tile[1],
                                                      bk=tile[2], output_dtype=torch.float32))
         np.testing.assert_array_equal(got, at.T @ b, err_msg=str(tile))
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("epilogue, out_dtype", [(None, "bfloat16"), ("swiglu", "bfloat16"), (None, "float32")])
+def test_streamed_equals_one_call(epilogue, out_dtype):
+    # Host operands streamed in row chunks give exactly the single-call result.
+    import strassen_tpu_b200 as sp
+    g = torch.Generator().manual_seed(31)
+    a = torch.randn(2048, 1024, generator=g).to(torch.bfloat16).pin_memory()
+    b = torch.randn(1024, 1536, generator=g).to(torch.bfloat16).pin_memory()
+    kw = dict(bm=256, bn=512, bk=512, epilogue=epilogue, output_dtype=out_dtype)
+    got = sp.strassen_matmul_streamed(a, b, row_chunk=512, **kw)
+    torch.cuda.current_stream().synchronize()
+    want = sp.strassen_matmul(a.cuda(), b.cuda(), **kw).cpu()
+    assert torch.equal(got, want)
