@@ -1320,8 +1320,8 @@ int make_maps(const void* a, const void* b, int64_t m, int64_t n, int64_t k, int
   return SB_OK;
 }
 
-// Tensor maps of the default Strassen kernel: one TMA copy per A group and per
-// B step.  The quadrant offsets become tensor dimensions (strides need not
+// Tensor maps of the TMEM-ring Strassen kernel: one TMA copy per operand and
+// K step.  The quadrant offsets become tensor dimensions (strides need not
 // grow with the dimension index), ordered so the copy lays the four quadrant
 // tiles out contiguously in slot order:
 //   A: dims (k, row in half-block, block, qk, qr), strides (1, lda, bm*lda,
