@@ -56,6 +56,8 @@ def parse():
     p.add_argument("--backend", default="strassen", choices=["strassen", "native"],
                    help="decoder GEMM sites: sm_100a Strassen kernels or the cuBLAS classical arm")
     p.add_argument("--layers", type=int, default=None, help="decoder layers (default: the model's)")
+    p.add_argument("--eager", action="store_true",
+                   help="decoder: launch op by op instead of replaying a CUDA graph of the forward")
     p.add_argument("--chunks", type=int, default=None,
                    help="decoder: token chunks pipelined so all-reduces overlap compute "
                         "(default: 2 with more than one rank, else 1)")
@@ -392,14 +394,21 @@ def run_decoder(args):
         return max_over_ranks(s.elapsed_time(e))
 
     chunks = args.chunks if args.chunks is not None else (2 if world > 1 else 1)
+    if args.eager:
+        forward = lambda t: model.forward(t, rope, chunks=chunks)  # noqa: E731
+        captured = None
+    else:
+        # One CUDA graph of the whole prefill (kernels, torch ops, NCCL calls).
+        captured = qwen3.CapturedPrefill(model, tokens, rope, chunks=chunks)
+        forward = captured
 
     with ClockSampler(device.index) as clocks:
-        ms = timed(lambda: model.forward(tokens, rope, chunks=chunks), args.steps, args.warmup) / args.steps
+        ms = timed(lambda: forward(tokens), args.steps, args.warmup) / args.steps
     logits_host = torch.empty(batch, cfg.vocab, dtype=torch.bfloat16).pin_memory()
 
     def e2e_step():
         t = tokens_host.to(device, non_blocking=True)
-        logits_host.copy_(model.forward(t, rope, chunks=chunks), non_blocking=True)
+        logits_host.copy_(forward(t), non_blocking=True)
 
     e2e_ms = timed(e2e_step, max(2, args.steps // 2), 1) / max(2, args.steps // 2)
     n_layers = len(model.blocks)
@@ -409,6 +418,9 @@ def run_decoder(args):
     if args.backend == "strassen":
         # two RMSNorm row passes + one GEMM per Strassen site, per block and token chunk
         launches = n_layers * (2 + len(strassen_sites)) * (chunks if batch % chunks == 0 else 1)
+    if captured is not None:
+        torch.cuda.synchronize(device)
+        captured.release()  # a graph holding NCCL calls goes before the process group
     if world > 1:
         barrier()
         dist.destroy_process_group()
@@ -423,7 +435,8 @@ def run_decoder(args):
         "config": {"workload": args.workload, "model": args.workload, "global_batch": batch,
                    "seq_len": seq, "layers": n_layers, "parallelism": f"tp{world}",
                    "backend": args.backend, "strassen_sites": strassen_sites,
-                   "token_chunks": chunks, "lm_head": "last position per sequence"},
+                   "token_chunks": chunks, "cuda_graph": not args.eager,
+                   "lm_head": "last position per sequence"},
         "achieved_tflops": flops / (ms * 1e-3) / 1e12,
         "e2e": {"value": tok / (e2e_ms * 1e-3), "unit": "tokens/s",
                 "h2d_bytes_per_step": tok * 8, "d2h_bytes_per_step": batch * cfg.vocab * 2},

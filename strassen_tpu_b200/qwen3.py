@@ -381,6 +381,47 @@ class Qwen3Prefill:
         return sp.native_matmul(last, self.lm_head)
 
 
+class CapturedPrefill:
+    """A CUDA-graph capture of ``Qwen3Prefill.forward`` for one token shape.
+
+    Replaying the graph launches the whole prefill (every block, the kernels,
+    torch ops and the NCCL all-reduces) without per-op host work, which bounds
+    the chunk-pipelined forward at high TP.  Call with a tokens tensor of the
+    captured shape: it is copied into the graph's input, the graph is replayed
+    on the current stream, and the graph's logits tensor is returned (overwritten
+    by the next call).  ``release()`` frees the graph; a graph holding NCCL
+    calls must be released before the process group is destroyed.
+    """
+
+    def __init__(self, model: "Qwen3Prefill", tokens: torch.Tensor, rope=None, chunks: int = 1,
+                 warmup: int = 2):
+        self.model = model
+        self.tokens = tokens.clone()
+        batch, seq = tokens.shape
+        self.rope = rope if rope is not None else model.rope(batch, seq)
+        self.chunks = chunks
+        side = torch.cuda.Stream(tokens.device)
+        side.wait_stream(torch.cuda.current_stream(tokens.device))
+        with torch.cuda.stream(side):
+            for _ in range(warmup):
+                model.forward(self.tokens, self.rope, chunks=chunks)
+        torch.cuda.current_stream(tokens.device).wait_stream(side)
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph):
+            self.logits = model.forward(self.tokens, self.rope, chunks=chunks)
+
+    def __call__(self, tokens: torch.Tensor) -> torch.Tensor:
+        if tokens.shape != self.tokens.shape:
+            raise ValueError(f"captured for tokens {tuple(self.tokens.shape)}, got {tuple(tokens.shape)}")
+        self.tokens.copy_(tokens, non_blocking=True)
+        self.graph.replay()
+        return self.logits
+
+    def release(self) -> None:
+        self.graph = None
+        self.logits = None
+
+
 def prefill_flops(cfg: Qwen3Config, batch: int, seq: int, layers: int | None = None) -> float:
     """GEMM + causal-attention FLOPs of one prefill (LM head on last positions only)."""
     n = cfg.layers if layers is None else layers

@@ -48,3 +48,18 @@ def test_qwen3_8b_layer_strassen_vs_native():
     want = qwen3.layer_forward(native, x, batch, seq, rope)
     assert torch.isfinite(got.float()).all()
     assert _rel(got - x, want - x) < 3e-2
+
+
+@pytest.mark.gpu
+def test_captured_prefill_replays_the_eager_forward():
+    from strassen_tpu_b200 import qwen3
+    dev = torch.device("cuda", 0)
+    model = qwen3.Qwen3Prefill(qwen3.QWEN3_TINY, qwen3.TensorParallel(), dev, backend="strassen")
+    tok = torch.randint(0, qwen3.QWEN3_TINY.vocab, (4, 1024), generator=torch.Generator().manual_seed(3)).to(dev)
+    for chunks in (1, 2):
+        want = model.forward(tok, chunks=chunks)
+        cap = qwen3.CapturedPrefill(model, tok, chunks=chunks)
+        got = cap(tok).clone()
+        torch.cuda.synchronize()
+        cap.release()
+        assert torch.equal(got, want)
