@@ -165,7 +165,13 @@ using StrassenTsPipe = TsPipeCfg<SB_TS_STAGES>;
 // A-from-TMEM MMAs, which takes their A operand off shared memory.  The
 // transposed-A launch (strassen_matmul_lhs_transposed) keeps the earlier layout
 // with all ten sums in shared memory.
-template <bool kStrassen, bool kOpts, bool kATrans>
+// kOpts: 0 = the default instantiation; 1, 2, 3 = research options with the
+// classical, dual and power-of-two formula, compiled separately so the
+// formula's operand tables fold to constants.
+template <int kOpts>
+__host__ __device__ constexpr int kFormula() { return kOpts > 0 ? kOpts - 1 : 0; }
+
+template <bool kStrassen, int kOpts, bool kATrans>
 constexpr bool uses_tmem_a() { return SB_TMEM_A && kStrassen && !kATrans; }
 constexpr int kRingSlots = 8;
 constexpr uint32_t kRingCol0 = 7 * kBlockN;  // 448
@@ -316,7 +322,7 @@ struct Quad8 {
   float c[4][8];
 };
 
-template <bool kStrassen, bool kOpts>
+template <bool kStrassen, int kOpts>
 __device__ __forceinline__ void read_quadrants(uint32_t tmem_row, int col, Quad8& out,
                                                const GemmParams& p, bool all_exact) {
   if constexpr (kStrassen) {
@@ -327,7 +333,7 @@ __device__ __forceinline__ void read_quadrants(uint32_t tmem_row, int col, Quad8
 #pragma unroll
       for (int e = 0; e < 8; ++e) m[0][e] = m[3][e] = m[4][e] = 0.f;
     }
-    if (!kOpts || p.formula == 0) {
+    if (kFormula<kOpts>() == 0) {
 #pragma unroll
       for (int e = 0; e < 8; ++e) {
         // strassen_pallas.py:324-379 quadrant updates, summed once.
@@ -336,7 +342,7 @@ __device__ __forceinline__ void read_quadrants(uint32_t tmem_row, int col, Quad8
         out.c[2][e] = m[1][e] + m[3][e];
         out.c[3][e] = ((m[0][e] - m[1][e]) + m[2][e]) + m[5][e];
       }
-    } else if (p.formula == 2) {
+    } else if (kFormula<kOpts>() == 2) {
 #pragma unroll
       for (int e = 0; e < 8; ++e) {
         // Power-of-two formula: basis updates (strassen_pallas.py:398-464) then
@@ -391,7 +397,7 @@ __device__ __forceinline__ void read_quadrants(uint32_t tmem_row, int col, Quad8
 // the accumulators are final: reads M1..M7 (or the quadrant accumulators) per
 // TMEM lane, recombines the quadrants and applies the fused epilogue
 // (strassen_pallas.py:739-879).  Product rows start at t0, columns at u0.
-template <bool kStrassen, int kEpi, bool kOutF32, bool kOpts>
+template <bool kStrassen, int kEpi, bool kOutF32, int kOpts>
 __device__ __forceinline__ void tile_epilogue(const GemmParams& p, uint32_t tmem_base, int t0, int u0,
                                               int warp, int lane, uint8_t* smem, uint32_t qss_bar,
                                               volatile int* abort_flag) {
@@ -542,7 +548,7 @@ __device__ __forceinline__ void tile_epilogue(const GemmParams& p, uint32_t tmem
 // instantiation.
 // kATrans: A is stored transposed, (K, M) row-major (strassen_matmul_lhs_transposed);
 // its tiles arrive M-major and feed the MMA as an MN-major operand.
-template <bool kStrassen, int kEpi, bool kOutF32, bool kOpts, bool kATrans = false>
+template <bool kStrassen, int kEpi, bool kOutF32, int kOpts, bool kATrans = false>
 __global__ void __launch_bounds__(kThreads, 1)
     strassen_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a,
                          const __grid_constant__ CUtensorMap tmap_b, const GemmParams p) {
@@ -713,7 +719,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t written = 0;  // accumulators holding a product (exact steps skip some)
       bool exact_step = false;
       if constexpr (kOpts) {
-        const int f = p.formula;
+        constexpr int f = kFormula<kOpts>();
         const int xa = 2 * p.swap_m + p.swap_k, xb = 2 * p.swap_k + p.swap_n;
 #pragma unroll
         for (int i = 0; i < 7; ++i) {
@@ -894,7 +900,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           uint4 b[4];
 #pragma unroll
           for (int t = 0; t < 4; ++t) b[t] = lds128(b_stage + (t ^ xb) * kBSlotBytes + b_off);
-          const int formula = kOpts ? p.formula : 0;
+          constexpr int formula = kFormula<kOpts>();
           if (formula == 0) {
             // Classical (strassen_pallas.py:324-379): a0+a1 over a1; ring
             // a0+a3, a2+a3, a2-a0, a1-a3.
@@ -1181,7 +1187,7 @@ EncodeTiledFn encode_fn() {
 bool is_pow2(int64_t v) { return v > 0 && (v & (v - 1)) == 0; }
 bool aligned16(const void* ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15u) == 0; }
 
-template <bool kStrassen, int kEpi, bool kOutF32, bool kOpts, bool kATrans = false>
+template <bool kStrassen, int kEpi, bool kOutF32, int kOpts, bool kATrans = false>
 int launch_typed(cudaStream_t stream, const CUtensorMap& ta, const CUtensorMap& tb,
                  const GemmParams& p) {
   auto kernel = strassen_gemm_kernel<kStrassen, kEpi, kOutF32, kOpts, kATrans>;
@@ -1200,7 +1206,7 @@ int launch_typed(cudaStream_t stream, const CUtensorMap& ta, const CUtensorMap& 
   return SB_OK;
 }
 
-template <bool kOpts>
+template <int kOpts>
 int dispatch_strassen(int epi, bool out_f32, cudaStream_t stream, const CUtensorMap& ta,
                       const CUtensorMap& tb, const GemmParams& p) {
   switch (epi) {
@@ -1225,8 +1231,12 @@ int dispatch(bool strassen, int epi, bool out_f32, cudaStream_t stream, const CU
                    : launch_typed<false, SB_EPI_NONE, false, false>(stream, ta, tb, p);
   }
   const bool opts = p.formula != 0 || p.swap_m || p.swap_k || p.swap_n || p.panel_schedule;
-  return opts ? dispatch_strassen<true>(epi, out_f32, stream, ta, tb, p)
-              : dispatch_strassen<false>(epi, out_f32, stream, ta, tb, p);
+  if (!opts) return dispatch_strassen<0>(epi, out_f32, stream, ta, tb, p);
+  switch (p.formula) {
+    case 0: return dispatch_strassen<1>(epi, out_f32, stream, ta, tb, p);
+    case 1: return dispatch_strassen<2>(epi, out_f32, stream, ta, tb, p);
+    default: return dispatch_strassen<3>(epi, out_f32, stream, ta, tb, p);
+  }
 }
 
 int check_device() {
