@@ -213,6 +213,19 @@ SB_API const char* sb_last_error_message(void);
  */
 SB_API int sb_device_status(int32_t* device_error, int32_t reset);
 
+/*
+ * Failure-detection self-test (no counterpart in the reference): launches one
+ * CTA on `stream` whose first warp waits, with the same bounded wait the GEMM
+ * kernels use, on an mbarrier that nothing arrives on, while a second warp,
+ * starting half a limit later, waits on another such barrier until the CTA
+ * abort flag stops it.  After ~1 s the
+ * first wait gives up, sets the error word to SB_SELFTEST_ERROR_CODE and both
+ * warps return; sb_device_status then reports SB_ERR_DEVICE_TIMEOUT.  No fault,
+ * no trap: the context stays usable.
+ */
+#define SB_SELFTEST_ERROR_CODE 9
+SB_API int sb_wait_selftest(sb_stream_t stream);
+
 /* Library version string. */
 SB_API const char* sb_version(void);
 

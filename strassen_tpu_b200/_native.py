@@ -75,6 +75,7 @@ SIGNATURES = {
     "sb_status_string": (ctypes.c_char_p, [_c_int]),
     "sb_last_error_message": (ctypes.c_char_p, []),
     "sb_device_status": (_c_int, [ctypes.POINTER(_c_int), _c_int]),
+    "sb_wait_selftest": (_c_int, [ctypes.c_void_p]),
     "sb_version": (ctypes.c_char_p, []),
 }
 

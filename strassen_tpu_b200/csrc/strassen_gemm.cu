@@ -271,6 +271,7 @@ enum : int {
   kErrWaitSums = 2,
   kErrWaitEmpty = 3,
   kErrWaitAcc = 4,
+  kErrSelfTest = SB_SELFTEST_ERROR_CODE,
 };
 
 __device__ __forceinline__ float load_aux(const void* p, int64_t idx, int f32) {
@@ -1044,6 +1045,31 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
+// Failure-detection self-test (sb_wait_selftest): warp 0 waits on a barrier
+// nobody arrives on and gives up after the bounded-wait limit, raising the abort
+// flag; warp 1 starts waiting on another such barrier half a limit later, so it
+// leaves through the abort flag before its own limit.
+__global__ void __launch_bounds__(64, 1) wait_selftest_kernel(int* err) {
+  __shared__ uint64_t bars[2];
+  __shared__ int abort_word;
+  if (threadIdx.x == 0) {
+    mbar_init(smem_addr(&bars[0]), 1);
+    mbar_init(smem_addr(&bars[1]), 1);
+    abort_word = 0;
+    fence_mbar_init();
+  }
+  __syncthreads();
+  volatile int* abort_flag = &abort_word;
+  if (threadIdx.x == 0) mbar_wait(smem_addr(&bars[0]), 0, abort_flag, err, kErrSelfTest);
+  if (threadIdx.x == 32) {
+    const uint64_t t0 = global_timer_ns();
+    while (global_timer_ns() - t0 < kWaitTimeoutNs / 2) {
+    }
+    mbar_wait(smem_addr(&bars[1]), 0, abort_flag, err, kErrWaitRaw);
+  }
+  __syncthreads();
+}
+
 // Row pass of norm_residual_add (strassen_pallas.py:836-866): the GEMM has
 // written fp32 pre-norm rows to `x`; one CTA normalises one row:
 // out = bf16(x * rsqrt((sum(left^2) + sum(right^2)) / n + eps) * scale + residual).
@@ -1745,6 +1771,18 @@ int sb_device_status(int32_t* device_error, int32_t reset) {
     if (e != cudaSuccess) return fail(SB_ERR_CUDA, std::string("cudaMemcpyToSymbol: ") + cudaGetErrorString(e));
   }
   return v ? SB_ERR_DEVICE_TIMEOUT : SB_OK;
+}
+
+int sb_wait_selftest(sb_stream_t stream) {
+  int st = check_device();
+  if (st != SB_OK) return st;
+  int* err = nullptr;
+  cudaError_t e = cudaGetSymbolAddress(reinterpret_cast<void**>(&err), g_device_error);
+  if (e != cudaSuccess) return fail(SB_ERR_CUDA, std::string("cudaGetSymbolAddress: ") + cudaGetErrorString(e));
+  wait_selftest_kernel<<<1, 64, 0, static_cast<cudaStream_t>(stream)>>>(err);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return fail(SB_ERR_CUDA, std::string("selftest launch: ") + cudaGetErrorString(e));
+  return SB_OK;
 }
 
 const char* sb_version(void) { return "strassen_b200 0.1.0 (sm_100a, tcgen05)"; }
