@@ -339,12 +339,14 @@ def square_crossover(entries: Iterable[ShapeEntry]) -> int | None:
     return crossover
 
 
-# Shapes (m, k, n) of the default suite: the reference's square sweep, its
-# tuned projection shapes (strassen_pallas.py:54-62) and the Qwen3-8B prefill
-# sites at 16384 tokens, TP=1 (q, k/v, o, gate/up, down).
+# Shapes (m, k, n) of the default suite: the reference's square sweep and the
+# Qwen3-8B projection shapes at M=4096 tokens (the benchmark sweep), its tuned
+# projection shapes (strassen_pallas.py:54-62) and the Qwen3-8B prefill sites at
+# 16384 tokens, TP=1 (q, k/v, o, gate/up, down).
 SUITES = {
     "default": [
         (2048, 2048, 2048), (4096, 4096, 4096), (8192, 8192, 8192), (16384, 16384, 16384),
+        (4096, 4096, 4096), (4096, 4096, 1024), (4096, 4096, 12288), (4096, 12288, 4096),
         (8192, 4096, 8192), (8192, 4096, 12288), (8192, 4096, 28672), (8192, 14336, 4096),
         (16384, 4096, 4096), (16384, 4096, 1024), (16384, 4096, 24576), (16384, 12288, 4096),
     ],
@@ -377,7 +379,8 @@ def main(argv: Sequence[str] | None = None) -> None:
     ap.add_argument("--warmups", type=int, default=5)
     ap.add_argument("--out", required=True)
     args = ap.parse_args(argv)
-    shapes = list(SUITES[args.suite]) + [tuple(int(x) for x in s.split("x")) for s in args.shape]
+    shapes = list(dict.fromkeys(list(SUITES[args.suite]) +
+                                [tuple(int(x) for x in s.split("x")) for s in args.shape]))
     table = tune(shapes, runs=args.runs, warmups=args.warmups)
     table.save(args.out)
     print(f"wrote {args.out}: {len(table.shapes)} shapes, square crossover {table.square_crossover}")
