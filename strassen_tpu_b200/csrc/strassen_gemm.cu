@@ -1218,13 +1218,17 @@ int launch_typed(cudaStream_t stream, const CUtensorMap& ta, const CUtensorMap& 
                  const GemmParams& p) {
   auto kernel = strassen_gemm_kernel<kStrassen, kEpi, kOutF32, kOpts, kATrans>;
   constexpr int kSmem = PipeFor<kStrassen, uses_tmem_a<kStrassen, kOpts, kATrans>()>::SMEM;
-  static std::once_flag once;
-  static cudaError_t attr_err = cudaSuccess;
-  std::call_once(once, [&]() {
-    attr_err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
+  // The attribute is per device: set it once for each device this kernel runs on.
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64)
+    return fail(SB_ERR_DEVICE, "no usable current device");
+  static std::once_flag once[64];
+  static cudaError_t attr_err[64];
+  std::call_once(once[dev], [&]() {
+    attr_err[dev] = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
   });
-  if (attr_err != cudaSuccess)
-    return fail(SB_ERR_CUDA, std::string("cudaFuncSetAttribute: ") + cudaGetErrorString(attr_err));
+  if (attr_err[dev] != cudaSuccess)
+    return fail(SB_ERR_CUDA, std::string("cudaFuncSetAttribute: ") + cudaGetErrorString(attr_err[dev]));
   const unsigned grid = (unsigned)(p.tiles_m * p.tiles_n);
   kernel<<<grid, kThreads, kSmem, stream>>>(ta, tb, p);
   const cudaError_t e = cudaGetLastError();

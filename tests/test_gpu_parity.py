@@ -281,3 +281,17 @@ def test_streamed_equals_one_call(epilogue, out_dtype):
     torch.cuda.current_stream().synchronize()
     want = sp.strassen_matmul(a.cuda(), b.cuda(), **kw).cpu()
     assert torch.equal(got, want)
+
+
+@pytest.mark.gpu
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs in one process")
+def test_two_devices_in_one_process():
+    # Kernel attributes are per device: the second device must launch too.
+    import strassen_tpu_b200 as sp
+    g = torch.Generator().manual_seed(8)
+    a = torch.randn(1024, 1024, generator=g).to(torch.bfloat16)
+    b = torch.randn(1024, 1024, generator=g).to(torch.bfloat16)
+    outs = []
+    for dev in ("cuda:0", "cuda:1"):
+        outs.append(sp.strassen_matmul(a.to(dev), b.to(dev), bm=256, bn=256, bk=256).cpu())
+    assert torch.equal(outs[0], outs[1])
