@@ -8,11 +8,12 @@ the TPU compiler (``dot_precision``, ``allow_input_fusion``,
 ``vmem_limit_bytes``, ``interleave_products``, ``product_aware_*``) are
 accepted and validated but do not change the B200 arithmetic, which keeps the
 seven products in separate fp32 TMEM accumulators over the whole K range and
-recombines them once.  The research options ``formula_variant="dual"``,
-``block_permutation`` and exact classical panels (``classical_panels`` /
-``panel_schedule``) and ``formula_variant="powers"`` run on the same kernel.  ``bm``/``bn``/``bk`` keep their reference meaning: they
-define the Strassen block whose quadrants are paired, so results follow the
-reference's pairing of operands.
+recombines them once.  The research options (``formula_variant="dual"`` and
+``"powers"``, ``block_permutation``, exact classical panels via
+``classical_panels`` / ``panel_schedule``) run on the same kernel layout.
+``bm``/``bn``/``bk`` keep their reference meaning: they define the Strassen
+block whose quadrants are paired, so results follow the reference's pairing of
+operands.
 
 Tensors are ``torch.Tensor`` on a CUDA B200 device.  There is no CPU path:
 ``interpret=True`` and CPU tensors raise.
@@ -481,9 +482,13 @@ def strassen_matmul_lhs_transposed(
     if not (a.is_cuda and b.is_cuda):
         raise ValueError("strassen_matmul_lhs_transposed runs on a CUDA device; got CPU tensors (no CPU fallback)")
     device = a.device
-    a, b = _rowmajor(a), _rowmajor(b)
+    a, b = _rowmajor(a), _rowmajor(b.to(device))
     if out is None:
         out = torch.empty((m, n), dtype=out_dt, device=device)
+    elif tuple(out.shape) != (m, n) or out.dtype != out_dt or out.device != device:
+        raise ValueError(f"out must be a {(m, n)} {_dtype_name(out_dt)} tensor on {device}")
+    elif out.stride(1) != 1 or out.stride(0) % 8 or out.data_ptr() % 16:
+        raise ValueError("out must be row-major with a 16-byte aligned row stride")
     lib = _native.load()
     with torch.cuda.device(device):
         status = lib.sb_strassen_gemm_lhs_transposed(
