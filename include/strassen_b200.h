@@ -4,8 +4,9 @@
  * Every entry point takes plain device pointers, sizes and a CUDA stream and
  * returns an sb_status code; nothing throws and nothing traps.  Argument
  * errors are detected on the host before any launch.  The caller owns every
- * buffer: the library never allocates device memory.  Scratch space that an
- * epilogue needs (norm_residual_add) is passed in as `workspace`, sized by
+ * buffer: the library allocates device memory only in sb_p2p_buffer_alloc,
+ * whose job that is.  Scratch space that an epilogue needs
+ * (norm_residual_add) is passed in as `workspace`, sized by
  * sb_workspace_bytes().
  *
  * The single operator mirrors strassen_pallas.strassen_matmul
@@ -50,7 +51,8 @@ typedef enum sb_status {
   SB_ERR_WORKSPACE = 10,      /* workspace missing or too small                  */
   SB_ERR_CUDA = 11,           /* a CUDA runtime call failed                      */
   SB_ERR_DEVICE = 12,         /* device is not sm_100 (B200)                     */
-  SB_ERR_DEVICE_TIMEOUT = 13  /* a bounded in-kernel wait gave up                */
+  SB_ERR_DEVICE_TIMEOUT = 13, /* a bounded in-kernel wait gave up                */
+  SB_ERR_P2P = 14             /* peer-group argument error (sb_p2p_*)            */
 } sb_status;
 
 /* ---- dtypes ------------------------------------------------------------- */
@@ -225,6 +227,66 @@ SB_API int sb_device_status(int32_t* device_error, int32_t reset);
  */
 #define SB_SELFTEST_ERROR_CODE 9
 SB_API int sb_wait_selftest(sb_stream_t stream);
+
+/* ---- tensor-parallel row reduction over NVLink peer memory ------------- */
+/*
+ * The row-parallel projections of the tensor-parallel Qwen3 decoder (o and
+ * down) end in a sum of every rank's partial product plus the residual.
+ * sb_p2p_reduce computes that sum in one kernel over peer memory, in place of
+ * an NCCL all-reduce and a residual add.  No counterpart in the reference
+ * (its decoder runs on one device); its residual_add epilogue contract
+ * (strassen_pallas.py:778-792: fp32 sum, one bf16 rounding) is kept.
+ *
+ * Buffers are symmetric: every rank allocates the same three buffers with
+ * sb_p2p_buffer_alloc (zero-filled), ships the handles to the other ranks
+ * (any host channel), and opens the peers' handles with sb_p2p_buffer_open.
+ *   partial  bf16, >= offset + elems elements: this rank's partial product,
+ *            written by its GEMM before the call (stream order);
+ *   reduced  bf16, same size: the rank's reduced slice (internal);
+ *   flags    sb_p2p_flag_bytes(): barrier words and this rank's call counter.
+ */
+#define SB_P2P_MAX_RANKS 8
+#define SB_P2P_MAX_BLOCKS 256
+#define SB_P2P_ERROR_CODE 10 /* device error word after a barrier wait gave up */
+
+typedef struct sb_ipc_handle {
+  unsigned char bytes[64]; /* a cudaIpcMemHandle_t */
+} sb_ipc_handle;
+
+/* cudaMalloc + zero fill + IPC handle.  Free with sb_p2p_buffer_free. */
+SB_API int sb_p2p_buffer_alloc(size_t bytes, void** dev_ptr, sb_ipc_handle* handle);
+/* Maps another process's buffer on the current device (peer access enabled). */
+SB_API int sb_p2p_buffer_open(const sb_ipc_handle* handle, void** dev_ptr);
+SB_API int sb_p2p_buffer_close(void* dev_ptr);
+SB_API int sb_p2p_buffer_free(void* dev_ptr);
+SB_API size_t sb_p2p_flag_bytes(void);
+
+typedef struct sb_p2p_group {
+  int32_t rank;                         /* this process's rank                 */
+  int32_t world;                        /* 1 .. SB_P2P_MAX_RANKS               */
+  void* partial[SB_P2P_MAX_RANKS];      /* rank q's buffers, mapped here       */
+  void* reduced[SB_P2P_MAX_RANKS];
+  void* flags[SB_P2P_MAX_RANKS];
+} sb_p2p_group;
+
+/*
+ * out[i] = bf16( (sum over q = 0..world-1 of partial_q[offset + i]) + residual[i] )
+ * for 0 <= i < elems, in fp32 with the ranks summed in order, identical on
+ * every rank.  Two phases in one kernel: each rank reduces its slice of the
+ * elements from every rank's partial buffer (plain peer loads) into its
+ * reduced buffer, then gathers the other ranks' slices into `out`.  Each CTA
+ * meets its counterparts on the other ranks at a flag barrier before each
+ * phase; a wait gives up after 2 s, sets the device error word to
+ * SB_P2P_ERROR_CODE and the kernel returns (sb_device_status reports it).
+ * Every rank must make the same sequence of calls, with the same offset,
+ * elems and blocks, each on one stream per rank; calls may be captured in a
+ * CUDA graph (the call counter lives in device memory).  residual: bf16 or
+ * f32 (residual_dtype) or NULL; out: bf16.  offset and elems are multiples of
+ * 8; pointers 16-byte aligned; blocks in 1 .. SB_P2P_MAX_BLOCKS.
+ */
+SB_API int sb_p2p_reduce(sb_stream_t stream, const sb_p2p_group* group, int64_t offset,
+                         int64_t elems, const void* residual, int32_t residual_dtype, void* out,
+                         int32_t blocks);
 
 /* Library version string. */
 SB_API const char* sb_version(void);

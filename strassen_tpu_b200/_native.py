@@ -52,6 +52,29 @@ class SbOptions(ctypes.Structure):
     ]
 
 
+P2P_MAX_RANKS = 8
+P2P_MAX_BLOCKS = 256
+P2P_ERROR_CODE = 10
+
+
+class SbIpcHandle(ctypes.Structure):
+    """Mirror of ``struct sb_ipc_handle`` (a cudaIpcMemHandle_t)."""
+
+    _fields_ = [("bytes", ctypes.c_ubyte * 64)]
+
+
+class SbP2PGroup(ctypes.Structure):
+    """Mirror of ``struct sb_p2p_group``."""
+
+    _fields_ = [
+        ("rank", ctypes.c_int32),
+        ("world", ctypes.c_int32),
+        ("partial", ctypes.c_void_p * P2P_MAX_RANKS),
+        ("reduced", ctypes.c_void_p * P2P_MAX_RANKS),
+        ("flags", ctypes.c_void_p * P2P_MAX_RANKS),
+    ]
+
+
 SIGNATURES = {
     "sb_strassen_gemm": (_c_int, [_c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_i64, _c_i64, _c_i64,
                                   _c_i64, _c_i64, _c_i64, _c_int, _c_int, _c_int, _c_int,
@@ -76,6 +99,13 @@ SIGNATURES = {
     "sb_last_error_message": (ctypes.c_char_p, []),
     "sb_device_status": (_c_int, [ctypes.POINTER(_c_int), _c_int]),
     "sb_wait_selftest": (_c_int, [ctypes.c_void_p]),
+    "sb_p2p_buffer_alloc": (_c_int, [_c_size, ctypes.POINTER(_c_ptr), ctypes.POINTER(SbIpcHandle)]),
+    "sb_p2p_buffer_open": (_c_int, [ctypes.POINTER(SbIpcHandle), ctypes.POINTER(_c_ptr)]),
+    "sb_p2p_buffer_close": (_c_int, [_c_ptr]),
+    "sb_p2p_buffer_free": (_c_int, [_c_ptr]),
+    "sb_p2p_flag_bytes": (_c_size, []),
+    "sb_p2p_reduce": (_c_int, [_c_ptr, ctypes.POINTER(SbP2PGroup), _c_i64, _c_i64, _c_ptr, _c_int,
+                               _c_ptr, _c_int]),
     "sb_version": (ctypes.c_char_p, []),
 }
 
@@ -83,6 +113,7 @@ SIGNATURES = {
 SB_OK = 0
 SB_ERR_UNSUPPORTED = 8
 SB_ERR_DEVICE_TIMEOUT = 13
+SB_ERR_P2P = 14
 SB_BF16, SB_F32 = 0, 1
 FORMULAS = {"classical": 0, "dual": 1, "powers": 2}
 EPILOGUE_KINDS = {

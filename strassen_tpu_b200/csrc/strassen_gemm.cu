@@ -1756,6 +1756,7 @@ const char* sb_status_string(int32_t status) {
     case SB_ERR_CUDA: return "CUDA runtime error";
     case SB_ERR_DEVICE: return "device is not an sm_100 B200";
     case SB_ERR_DEVICE_TIMEOUT: return "bounded device wait timed out";
+    case SB_ERR_P2P: return "peer group argument error";
     default: return "unknown status";
   }
 }
@@ -1792,3 +1793,5 @@ int sb_wait_selftest(sb_stream_t stream) {
 const char* sb_version(void) { return "strassen_b200 0.1.0 (sm_100a, tcgen05)"; }
 
 }  // extern "C"
+
+#include "p2p_reduce.cuh"

@@ -1,0 +1,174 @@
+"""Tensor-parallel row reduction over NVLink peer memory (``sb_p2p_reduce``).
+
+The tensor-parallel decoder's row-parallel projections (o and down) leave one
+partial product per rank; the block output is their sum plus the residual.
+:class:`PeerReduce` owns the symmetric buffers that computation needs and runs
+it as one kernel over peer memory instead of an NCCL all-reduce:
+
+* every rank allocates a ``partial`` buffer ``[rows, cols]`` bf16, a ``reduced``
+  buffer of the same size and a flag buffer (``sb_p2p_buffer_alloc``), the
+  IPC handles go round with ``all_gather_object``, and every rank maps the
+  others' buffers (``sb_p2p_buffer_open``);
+* the row-parallel GEMM writes its partial straight into
+  :meth:`PeerReduce.partial_rows` (no copy);
+* :meth:`PeerReduce.reduce` launches ``sb_p2p_reduce`` on a side stream: each
+  rank sums its slice of the rows over every rank's partial (fp32, ranks in
+  order) plus the residual, then gathers the other slices.  The result is the
+  same bf16 tensor on every rank.
+
+Calls must come in the same order on every rank (the decoder's program order
+guarantees it); each rank's calls run on one stream, which keeps the buffers'
+reuse safe (see ``csrc/p2p_reduce.cuh``).  The reduce may be captured in a
+CUDA graph.  One process per GPU, all GPUs of one node (NVLink peers).
+"""
+
+from __future__ import annotations
+
+import ctypes
+
+import torch
+
+from . import _native
+
+
+class _DeviceArray:
+    """A raw device allocation exposed through ``__cuda_array_interface__``."""
+
+    def __init__(self, ptr: int, shape: tuple, typestr: str):
+        self.__cuda_array_interface__ = {"shape": shape, "typestr": typestr, "data": (ptr, False),
+                                         "version": 3, "strides": None}
+
+
+class _Pending:
+    """Handle of an asynchronous reduce: ``wait()`` orders the current stream after it."""
+
+    def __init__(self, event: torch.cuda.Event):
+        self.event = event
+
+    def wait(self) -> None:
+        torch.cuda.current_stream().wait_event(self.event)
+
+
+class PeerReduce:
+    """Symmetric buffers and the ``sb_p2p_reduce`` call for one process group.
+
+    ``rows`` x ``cols`` bounds every reduction (the decoder passes its token
+    count and hidden size).  ``group``: a ``torch.distributed`` group (None =
+    the default group, or a single rank when torch.distributed is not
+    initialised).  ``blocks`` CTAs per call (1..256), the same on every rank.
+    """
+
+    def __init__(self, rows: int, cols: int, device, group=None, blocks: int = 128):
+        import torch.distributed as dist
+
+        if cols % 8:
+            raise ValueError(f"cols must be a multiple of 8, got {cols}")
+        if not 1 <= blocks <= _native.P2P_MAX_BLOCKS:
+            raise ValueError(f"blocks must be 1..{_native.P2P_MAX_BLOCKS}, got {blocks}")
+        self.dist = dist if dist.is_available() and dist.is_initialized() else None
+        self.group = group
+        self.rank = self.dist.get_rank(group) if self.dist else 0
+        self.world = self.dist.get_world_size(group) if self.dist else 1
+        if self.world > _native.P2P_MAX_RANKS:
+            raise ValueError(f"at most {_native.P2P_MAX_RANKS} ranks, got {self.world}")
+        self.device = torch.device(device)
+        self.rows, self.cols, self.blocks = rows, cols, blocks
+        self.lib = _native.load()
+        self._own: list[int] = []
+        self._opened: list[int] = []
+        nbytes = rows * cols * 2
+        with torch.cuda.device(self.device):
+            own = [self._alloc(nbytes), self._alloc(nbytes), self._alloc(self.lib.sb_p2p_flag_bytes())]
+            handles = [bytes(h.bytes) for _, h in own]
+            if self.world > 1:
+                gathered = [None] * self.world
+                self.dist.all_gather_object(gathered, handles, group=group)
+            else:
+                gathered = [handles]
+            g = _native.SbP2PGroup()
+            g.rank, g.world = self.rank, self.world
+            for q in range(self.world):
+                ptrs = [p for p, _ in own] if q == self.rank else [self._open(h) for h in gathered[q]]
+                g.partial[q], g.reduced[q], g.flags[q] = ptrs
+            self.group_struct = g
+            self._partial = torch.as_tensor(_DeviceArray(own[0][0], (rows, cols), "<i2"),
+                                            device=self.device).view(torch.bfloat16)
+            self.stream = torch.cuda.Stream(self.device)
+
+    def _alloc(self, nbytes: int):
+        ptr = ctypes.c_void_p()
+        handle = _native.SbIpcHandle()
+        _native.check(self.lib.sb_p2p_buffer_alloc(nbytes, ctypes.byref(ptr), ctypes.byref(handle)))
+        self._own.append(ptr.value)
+        return ptr.value, handle
+
+    def _open(self, raw: bytes) -> int:
+        handle = _native.SbIpcHandle()
+        ctypes.memmove(handle.bytes, raw, len(raw))
+        ptr = ctypes.c_void_p()
+        _native.check(self.lib.sb_p2p_buffer_open(ctypes.byref(handle), ctypes.byref(ptr)))
+        self._opened.append(ptr.value)
+        return ptr.value
+
+    def partial_rows(self, lo: int, hi: int) -> torch.Tensor:
+        """Rows lo:hi of this rank's partial buffer (the GEMM's ``out``)."""
+        if not 0 <= lo < hi <= self.rows:
+            raise ValueError(f"rows {lo}:{hi} outside the buffer's {self.rows}")
+        return self._partial[lo:hi]
+
+    def reduce(self, part: torch.Tensor, residual: torch.Tensor | None = None,
+               out: torch.Tensor | None = None, async_op: bool = False):
+        """Sum ``part`` (a :meth:`partial_rows` view) over the ranks, plus ``residual``.
+
+        Returns the bf16 result (a new tensor unless ``out`` is given); with
+        ``async_op`` returns ``(result, handle)`` and the caller waits the handle
+        before using the result.
+        """
+        if self._partial is None:
+            raise RuntimeError("PeerReduce is closed")
+        base = self._partial.data_ptr()
+        off_bytes = part.data_ptr() - base
+        if (part.dtype != torch.bfloat16 or not part.is_contiguous() or part.dim() != 2
+                or part.shape[1] != self.cols or off_bytes < 0
+                or off_bytes + part.numel() * 2 > self.rows * self.cols * 2):
+            raise ValueError("part must be a partial_rows() view of this PeerReduce")
+        if residual is not None:
+            if tuple(residual.shape) != tuple(part.shape) or not residual.is_contiguous() \
+                    or residual.dtype not in (torch.bfloat16, torch.float32) or residual.device != self.device:
+                raise ValueError(f"residual must be a contiguous {tuple(part.shape)} bf16/f32 tensor on {self.device}")
+        cur = torch.cuda.current_stream(self.device)
+        if out is None:
+            out = torch.empty_like(part)
+        elif tuple(out.shape) != tuple(part.shape) or out.dtype != torch.bfloat16 or not out.is_contiguous():
+            raise ValueError(f"out must be a contiguous {tuple(part.shape)} bf16 tensor")
+        self.stream.wait_stream(cur)
+        res_ptr = residual.data_ptr() if residual is not None else None
+        res_dt = _native.SB_F32 if residual is not None and residual.dtype == torch.float32 else _native.SB_BF16
+        with torch.cuda.device(self.device):
+            status = self.lib.sb_p2p_reduce(self.stream.cuda_stream, ctypes.byref(self.group_struct),
+                                            off_bytes // 2, part.numel(), res_ptr, res_dt,
+                                            out.data_ptr(), self.blocks)
+        _native.check(status)
+        if residual is not None:
+            residual.record_stream(self.stream)
+        out.record_stream(self.stream)
+        if async_op:
+            done = torch.cuda.Event()
+            done.record(self.stream)
+            return out, _Pending(done)
+        cur.wait_stream(self.stream)
+        return out
+
+    def close(self) -> None:
+        """Unmap the peers' buffers and free this rank's (all ranks call it)."""
+        if self._partial is None:
+            return
+        with torch.cuda.device(self.device):
+            torch.cuda.synchronize(self.device)
+            for ptr in self._opened:
+                _native.check(self.lib.sb_p2p_buffer_close(ptr))
+            if self.world > 1:
+                self.dist.barrier(group=self.group)  # nobody maps our buffers any more
+            for ptr in self._own:
+                _native.check(self.lib.sb_p2p_buffer_free(ptr))
+        self._opened, self._own, self._partial = [], [], None

@@ -71,26 +71,69 @@ class StrassenTiles:
 
 
 class TensorParallel:
-    """Rank, world size and the one collective the decoder needs."""
+    """Rank, world size and the one collective the decoder needs: the sum of the
+    row-parallel projections' partial products plus the residual.
 
-    def __init__(self, group=None):
+    ``collective="nccl"``: rank 0 adds the residual in its GEMM epilogue and an
+    NCCL all-reduce sums the partials in place.  ``collective="p2p"``: the GEMMs
+    write into a symmetric peer buffer and ``sb_p2p_reduce`` sums them with the
+    residual over NVLink peer memory (:mod:`strassen_tpu_b200.p2p`); its
+    buffers are sized by :meth:`ensure_buffers` before the first forward.
+    """
+
+    def __init__(self, group=None, collective: str = "nccl"):
         import torch.distributed as dist
+        if collective not in ("nccl", "p2p"):
+            raise ValueError(f"collective must be 'nccl' or 'p2p', got {collective!r}")
         self.dist = dist if dist.is_available() and dist.is_initialized() else None
         self.group = group
         self.rank = self.dist.get_rank(group) if self.dist else 0
         self.world = self.dist.get_world_size(group) if self.dist else 1
+        self.collective = collective
+        self.peer = None
 
-    def all_reduce(self, x: torch.Tensor) -> torch.Tensor:
+    @property
+    def peer_reduce(self) -> bool:
+        """Whether the row-parallel sums run as sb_p2p_reduce (p2p, more than one rank)."""
+        return self.collective == "p2p" and self.world > 1
+
+    def ensure_buffers(self, rows: int, cols: int, device) -> None:
+        """Size the p2p buffers for `rows` x `cols` partials (every rank calls it)."""
+        if not self.peer_reduce:
+            return
+        if self.peer is None or self.peer.rows < rows or self.peer.cols != cols:
+            from .p2p import PeerReduce
+            if self.peer is not None:
+                self.peer.close()
+            self.peer = PeerReduce(rows, cols, device, group=self.group)
+
+    def partial_out(self, row0: int, rows: int):
+        """Where a row-parallel GEMM writes its partial for token rows row0:row0+rows
+        (a peer-buffer view for p2p; None lets the GEMM allocate)."""
+        return self.peer.partial_rows(row0, row0 + rows) if self.peer_reduce else None
+
+    def all_reduce(self, x: torch.Tensor, residual: torch.Tensor | None = None) -> torch.Tensor:
+        """Sum of x over the ranks (+ residual for p2p; nccl expects it fused on rank 0)."""
+        if self.peer_reduce:
+            return self.peer.reduce(x, residual)
         if self.world > 1:
             self.dist.all_reduce(x, group=self.group)
         return x
 
-    def all_reduce_async(self, x: torch.Tensor):
-        """Start an in-place sum of x over the ranks; returns a handle whose wait()
-        orders the caller's stream after it (None on one rank)."""
+    def all_reduce_async(self, x: torch.Tensor, residual: torch.Tensor | None = None):
+        """Start the sum; returns (result, handle) where handle.wait() orders the
+        caller's stream after it (handle None on one rank)."""
+        if self.peer_reduce:
+            return self.peer.reduce(x, residual, async_op=True)
         if self.world > 1:
-            return self.dist.all_reduce(x, group=self.group, async_op=True)
-        return None
+            return x, self.dist.all_reduce(x, group=self.group, async_op=True)
+        return x, None
+
+    def close(self) -> None:
+        """Free the p2p buffers (every rank calls it, before the process group goes)."""
+        if self.peer is not None:
+            self.peer.close()
+            self.peer = None
 
 
 def _pick_bn(width: int, preferred: int, minimum: int) -> int | None:
@@ -230,22 +273,37 @@ def _qk(layer: Qwen3Layer, name: str, h, heads, norm_w, cos, sin, cos_laid, sin_
     return apply_rope_torch(x, cos, sin)
 
 
-def _plain(layer: Qwen3Layer, name: str, h, residual=None):
+def _plain(layer: Qwen3Layer, name: str, h, residual=None, out=None):
     site = layer.sites[name]
     if site.strassen:
         kw = {}
         if residual is not None:
             kw = dict(epilogue="residual_add", residual=residual)
-        return sp.strassen_matmul(h, site.weight, bm=layer.tiles.bm, bn=site.bn, bk=layer.tiles.bk, **kw)
-    out = sp.native_matmul(h, site.weight)
+        return sp.strassen_matmul(h, site.weight, bm=layer.tiles.bm, bn=site.bn, bk=layer.tiles.bk,
+                                  out=out, **kw)
+    res = sp.native_matmul(h, site.weight)
     if residual is not None:
-        out = (out.float() + residual.float()).to(torch.bfloat16)
-    return out
+        res = (res.float() + residual.float()).to(torch.bfloat16)
+    if out is not None:
+        out.copy_(res)
+        return out
+    return res
 
 
-def _attention_half(layer: Qwen3Layer, x: torch.Tensor, batch: int, seq: int, rope) -> torch.Tensor:
-    """ln1 -> q/k/v (fused qk_norm_rope) -> causal attention -> o projection with the
-    residual on rank 0: this rank's partial sum of the new hidden state."""
+def _row_parallel(layer: Qwen3Layer, name: str, h, residual, row0: int):
+    """A row-parallel projection: (this rank's partial, the residual the sum still
+    needs).  nccl: rank 0 adds the residual in its epilogue; p2p: the partial
+    lands in the peer buffer and the reduce adds the residual."""
+    tp = layer.tp
+    if getattr(tp, "peer_reduce", False):
+        return _plain(layer, name, h, out=tp.partial_out(row0, h.shape[0])), residual
+    return _plain(layer, name, h, residual=residual if tp.rank == 0 else None), None
+
+
+def _attention_half(layer: Qwen3Layer, x: torch.Tensor, batch: int, seq: int, rope, row0: int = 0):
+    """ln1 -> q/k/v (fused qk_norm_rope) -> causal attention -> o projection:
+    this rank's partial sum of the new hidden state and the residual still to
+    add (_row_parallel).  row0: x's first row in the forward's token batch."""
     cfg, tp = layer.cfg, layer.tp
     cos, sin, cos_laid, sin_laid = rope
     norm = sp.rms_norm if layer.backend == "strassen" else (lambda a, b, eps: rms_norm_torch(a, b, eps))
@@ -263,12 +321,12 @@ def _attention_half(layer: Qwen3Layer, x: torch.Tensor, batch: int, seq: int, ro
         v4 = v4.repeat_interleave(rep, dim=1)
     attn = F.scaled_dot_product_attention(q4, k4, v4, is_causal=True)
     attn = attn.transpose(1, 2).reshape(batch * seq, hq * hd)
-    return _plain(layer, "o", attn, residual=x if tp.rank == 0 else None)
+    return _row_parallel(layer, "o", attn, x, row0)
 
 
-def _mlp_half(layer: Qwen3Layer, x1: torch.Tensor) -> torch.Tensor:
-    """ln2 -> gate/up (fused SwiGLU) -> down projection with the residual on rank 0:
-    this rank's partial sum of the block output."""
+def _mlp_half(layer: Qwen3Layer, x1: torch.Tensor, row0: int = 0):
+    """ln2 -> gate/up (fused SwiGLU) -> down projection: this rank's partial sum
+    of the block output and the residual still to add (_row_parallel)."""
     cfg, tp = layer.cfg, layer.tp
     norm = sp.rms_norm if layer.backend == "strassen" else (lambda a, b, eps: rms_norm_torch(a, b, eps))
     h2 = norm(x1, layer.ln2, cfg.rms_eps)
@@ -280,7 +338,7 @@ def _mlp_half(layer: Qwen3Layer, x1: torch.Tensor) -> torch.Tensor:
         gu = sp.native_matmul(h2, up.weight).float()
         gate, upv = gu.chunk(2, dim=-1)
         g = (F.silu(gate) * upv).to(torch.bfloat16)
-    return _plain(layer, "down", g, residual=x1 if tp.rank == 0 else None)
+    return _row_parallel(layer, "down", g, x1, row0)
 
 
 def layer_forward(layer: Qwen3Layer, x: torch.Tensor, batch: int, seq: int, rope) -> torch.Tensor:
@@ -289,8 +347,8 @@ def layer_forward(layer: Qwen3Layer, x: torch.Tensor, batch: int, seq: int, rope
     The composition of benchmark_qwen3_32b_layer.py:344-398 with the row-parallel
     o and down projections each followed by one all-reduce."""
     tp = layer.tp
-    x1 = tp.all_reduce(_attention_half(layer, x, batch, seq, rope))
-    return tp.all_reduce(_mlp_half(layer, x1))
+    x1 = tp.all_reduce(*_attention_half(layer, x, batch, seq, rope))
+    return tp.all_reduce(*_mlp_half(layer, x1))
 
 
 def _chunk_rope(rope, lo: int, hi: int):
@@ -325,13 +383,13 @@ def forward_blocks_chunked(blocks, x: torch.Tensor, batch: int, seq: int, rope, 
         for i in range(chunks):
             if pending[i] is not None:
                 pending[i].wait()
-            part = _attention_half(blk, xs[i], per, seq, ropes[i])
-            mids.append((part, tp.all_reduce_async(part)))
+            part, res = _attention_half(blk, xs[i], per, seq, ropes[i], row0=i * rows)
+            mids.append(tp.all_reduce_async(part, res))
         for i, (x1, work) in enumerate(mids):
             if work is not None:
                 work.wait()
-            xs[i] = _mlp_half(blk, x1)
-            pending[i] = tp.all_reduce_async(xs[i])
+            part, res = _mlp_half(blk, x1, row0=i * rows)
+            xs[i], pending[i] = tp.all_reduce_async(part, res)
     for work in pending:
         if work is not None:
             work.wait()
@@ -374,6 +432,7 @@ class Qwen3Prefill:
         multiple of chunks, else the blocks run unchunked."""
         batch, seq = tokens.shape
         rope = rope if rope is not None else self.rope(batch, seq)
+        self.tp.ensure_buffers(batch * seq, self.cfg.hidden, self.device)
         x = self.embed[tokens.reshape(-1)]
         x = forward_blocks_chunked(self.blocks, x, batch, seq, rope, chunks)
         last = x.view(batch, seq, -1)[:, -1]
