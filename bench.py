@@ -61,6 +61,9 @@ def parse():
     p.add_argument("--chunks", type=int, default=None,
                    help="decoder: token chunks pipelined so all-reduces overlap compute "
                         "(default: 2 with more than one rank, else 1)")
+    p.add_argument("--collective", default="nccl", choices=["nccl", "p2p"],
+                   help="decoder: row-parallel sums by NCCL all-reduce (residual fused on rank 0) "
+                        "or by sb_p2p_reduce over NVLink peer memory")
     return p.parse_args()
 
 
@@ -360,7 +363,7 @@ def run_decoder(args):
         dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=device)
     cfg, (batch, seq) = ({"qwen3-8b": (qwen3.QWEN3_8B, (8, 2048)),
                           "qwen3-32b": (qwen3.QWEN3_32B, (16, 4096))}[args.workload])
-    tp = qwen3.TensorParallel()
+    tp = qwen3.TensorParallel(collective=args.collective)
     model = qwen3.Qwen3Prefill(cfg, tp, device, backend=args.backend, layers=args.layers)
     g = torch.Generator().manual_seed(20260911)
     tokens_host = torch.randint(0, cfg.vocab, (batch, seq), generator=g).pin_memory()
@@ -418,9 +421,12 @@ def run_decoder(args):
     if args.backend == "strassen":
         # two RMSNorm row passes + one GEMM per Strassen site, per block and token chunk
         launches = n_layers * (2 + len(strassen_sites)) * (chunks if batch % chunks == 0 else 1)
+    if tp.peer_reduce:
+        launches += n_layers * 2 * (chunks if batch % chunks == 0 else 1)  # sb_p2p_reduce
     if captured is not None:
         torch.cuda.synchronize(device)
         captured.release()  # a graph holding NCCL calls goes before the process group
+    tp.close()
     if world > 1:
         barrier()
         dist.destroy_process_group()
@@ -436,6 +442,7 @@ def run_decoder(args):
                    "seq_len": seq, "layers": n_layers, "parallelism": f"tp{world}",
                    "backend": args.backend, "strassen_sites": strassen_sites,
                    "token_chunks": chunks, "cuda_graph": not args.eager,
+                   "collective": args.collective if world > 1 else None,
                    "lm_head": "last position per sequence"},
         "achieved_tflops": flops / (ms * 1e-3) / 1e12,
         "e2e": {"value": tok / (e2e_ms * 1e-3), "unit": "tokens/s",

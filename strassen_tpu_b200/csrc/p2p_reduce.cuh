@@ -109,23 +109,36 @@ __global__ void __launch_bounds__(kP2PThreads) p2p_reduce_kernel(const P2PParams
     const int64_t lo = p2p_slice_begin(p.vecs, p.rank, p.world);
     const int64_t hi = p2p_slice_begin(p.vecs, p.rank + 1, p.world);
     uint4* red = reinterpret_cast<uint4*>(p.reduced[p.rank] + p.offset);
-    for (int64_t v = lo + first; v < hi; v += stride) {
-      uint4 u[SB_P2P_MAX_RANKS];
+    // Two vectors per thread per pass (v and v + stride) keep 2 x world peer
+    // loads in flight per thread; remote loads are latency-bound.
+    for (int64_t v = lo + first; v < hi; v += 2 * stride) {
+      const bool second = v + stride < hi;
+      uint4 u[2][SB_P2P_MAX_RANKS];
 #pragma unroll
-      for (int q = 0; q < SB_P2P_MAX_RANKS; ++q)
-        if (q < p.world) u[q] = __ldcg(reinterpret_cast<const uint4*>(p.partial[q] + p.offset) + v);
-      float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-      for (int q = 0; q < SB_P2P_MAX_RANKS; ++q)
-        if (q < p.world) add_bf16x8(u[q], acc);
-      if (p.residual != nullptr) {
-        float r[8];
-        load8(p.residual, v * 8, p.residual_f32, r);
-#pragma unroll
-        for (int e = 0; e < 8; ++e) acc[e] += r[e];
+      for (int q = 0; q < SB_P2P_MAX_RANKS; ++q) {
+        if (q < p.world) {
+          const uint4* src = reinterpret_cast<const uint4*>(p.partial[q] + p.offset);
+          u[0][q] = __ldcg(src + v);
+          if (second) u[1][q] = __ldcg(src + v + stride);
+        }
       }
-      red[v] = make_uint4(pack_bf16x2(acc[0], acc[1]), pack_bf16x2(acc[2], acc[3]),
-                          pack_bf16x2(acc[4], acc[5]), pack_bf16x2(acc[6], acc[7]));
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        if (h == 1 && !second) break;
+        const int64_t w = v + h * stride;
+        float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int q = 0; q < SB_P2P_MAX_RANKS; ++q)
+          if (q < p.world) add_bf16x8(u[h][q], acc);
+        if (p.residual != nullptr) {
+          float r[8];
+          load8(p.residual, w * 8, p.residual_f32, r);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) acc[e] += r[e];
+        }
+        red[w] = make_uint4(pack_bf16x2(acc[0], acc[1]), pack_bf16x2(acc[2], acc[3]),
+                            pack_bf16x2(acc[4], acc[5]), pack_bf16x2(acc[6], acc[7]));
+      }
     }
     if (p2p_barrier(p, 1, epoch)) {
       // Phase 2: every slice from its owner, this CTA's elements of each.
