@@ -111,7 +111,8 @@ class PeerReduce:
         return ptr.value
 
     def partial_rows(self, lo: int, hi: int) -> torch.Tensor:
-        """Rows lo:hi of this rank's partial buffer (the GEMM's ``out``)."""
+        """Rows lo:hi of this rank's partial buffer (the GEMM's ``out``).  The view
+        aliases library-owned memory and is invalid after :meth:`close`."""
         if not 0 <= lo < hi <= self.rows:
             raise ValueError(f"rows {lo}:{hi} outside the buffer's {self.rows}")
         return self._partial[lo:hi]
@@ -139,8 +140,9 @@ class PeerReduce:
         cur = torch.cuda.current_stream(self.device)
         if out is None:
             out = torch.empty_like(part)
-        elif tuple(out.shape) != tuple(part.shape) or out.dtype != torch.bfloat16 or not out.is_contiguous():
-            raise ValueError(f"out must be a contiguous {tuple(part.shape)} bf16 tensor")
+        elif (tuple(out.shape) != tuple(part.shape) or out.dtype != torch.bfloat16
+              or not out.is_contiguous() or out.device != self.device):
+            raise ValueError(f"out must be a contiguous {tuple(part.shape)} bf16 tensor on {self.device}")
         self.stream.wait_stream(cur)
         res_ptr = residual.data_ptr() if residual is not None else None
         res_dt = _native.SB_F32 if residual is not None and residual.dtype == torch.float32 else _native.SB_BF16
@@ -163,6 +165,7 @@ class PeerReduce:
         """Unmap the peers' buffers and free this rank's (all ranks call it)."""
         if self._partial is None:
             return
+        self.group_struct = None
         with torch.cuda.device(self.device):
             torch.cuda.synchronize(self.device)
             for ptr in self._opened:
