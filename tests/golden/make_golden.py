@@ -15,7 +15,7 @@ backend; dots accumulate in fp32).
 
 Usage (needs the reference checkout and ml_dtypes; run in the build container):
 
-    python tests/golden/make_golden.py --reference /root/reference
+    python tests/golden/make_golden.py --reference <path of the reference checkout>
 
 Writes ``tests/golden/golden_cases.json`` (case parameters and input recipes)
 and ``tests/golden/golden_outputs.npz`` (reference outputs as bf16 bit patterns
@@ -293,7 +293,7 @@ def cases():
          rope_head_dim=64)
     gemm("norm_residual_256x512x512", 256, 512, 512, (256, 512, 256), seed=47,
          epilogue="norm_residual_add")
-    # Research options (SURVEY 8(f)): dual formula, block permutation, exact panels.
+    # Research options: dual formula, block permutation, exact panels.
     gemm("dual_512", 512, 512, 512, (256, 256, 256), seed=51, formula_variant="dual")
     gemm("dual_interleaved_512", 512, 512, 512, (256, 256, 256), seed=52, formula_variant="dual",
          interleave_products=True)
@@ -344,7 +344,7 @@ def run_reference(sp, p):
 
 def main():
     parser = argparse.ArgumentParser()
-    parser.add_argument("--reference", default="/root/reference")
+    parser.add_argument("--reference", required=True, help="path of the reference checkout")
     parser.add_argument("--out", default=str(HERE))
     args = parser.parse_args()
     sp = import_reference(Path(args.reference))
