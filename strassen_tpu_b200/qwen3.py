@@ -110,7 +110,12 @@ class TensorParallel:
     def partial_out(self, row0: int, rows: int):
         """Where a row-parallel GEMM writes its partial for token rows row0:row0+rows
         (a peer-buffer view for p2p; None lets the GEMM allocate)."""
-        return self.peer.partial_rows(row0, row0 + rows) if self.peer_reduce else None
+        if not self.peer_reduce:
+            return None
+        if self.peer is None:
+            raise RuntimeError("collective='p2p' needs ensure_buffers(rows, hidden, device) before the "
+                               "first row-parallel projection (Qwen3Prefill.forward calls it)")
+        return self.peer.partial_rows(row0, row0 + rows)
 
     def all_reduce(self, x: torch.Tensor, residual: torch.Tensor | None = None) -> torch.Tensor:
         """Sum of x over the ranks (+ residual for p2p; nccl expects it fused on rank 0)."""

@@ -144,6 +144,13 @@ def test_tensor_parallel_collective_choice():
     assert out is x and handle is None
 
 
+def test_p2p_without_buffers_is_a_clear_error():
+    tp = qwen3.TensorParallel(collective="p2p")
+    tp.world = 2  # as a two-rank group would report, before ensure_buffers
+    with pytest.raises(RuntimeError, match="ensure_buffers"):
+        tp.partial_out(0, 16)
+
+
 def test_single_rank_forward_is_the_same_for_either_collective():
     cfg = qwen3.QWEN3_TINY
     tokens = torch.randint(0, cfg.vocab, (2, 16), generator=torch.Generator().manual_seed(3))
