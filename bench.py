@@ -50,6 +50,8 @@ def parse():
     p.add_argument("--no-cpu-baseline", action="store_true",
                    help="skip the CPU oracle timing (used for ncu captures)")
     p.add_argument("--no-e2e", action="store_true", help="skip the host-buffer end-to-end loop")
+    p.add_argument("--kernel", default="single", choices=["single", "pair"],
+                   help="GEMM workload: the one-CTA Strassen kernel or the two-CTA cluster kernel")
     p.add_argument("--workload", default="gemm", choices=["gemm", "qwen3-8b", "qwen3-32b"],
                    help="gemm: the 8192^3 Strassen GEMM (default, the driver's line); "
                         "qwen3-*: tensor-parallel decoder prefill tokens/s (BASELINE configs 4/5)")
@@ -195,6 +197,8 @@ def run_reference(args):
         "ms_per_step": 1e3 * total_t / args.steps, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
         "config": {"workload": f"strassen_gemm_{M}x{N}x{K}_bf16", "tile": list(TILE),
+                   "kernel": "two-CTA cluster (sb_strassen_gemm_pair)" if args.kernel == "pair"
+                   else "one-CTA (sb_strassen_gemm)",
                    "sample": sample},
         "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port",
                          "sample": sample},
@@ -230,8 +234,10 @@ def run_ours(args):
     stream = torch.cuda.current_stream(device)
     flops = 2.0 * M * N * K
 
+    gemm = sb.pair_matmul if args.kernel == "pair" else sb.strassen_matmul
+
     def step():
-        sb.strassen_matmul(a, b, bm=TILE[0], bn=TILE[1], bk=TILE[2], out=c)
+        gemm(a, b, bm=TILE[0], bn=TILE[1], bk=TILE[2], out=c)
 
     def barrier():
         if world > 1:
@@ -326,6 +332,8 @@ def run_ours(args):
         "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
         "config": {"workload": f"strassen_gemm_{M}x{N}x{K}_bf16", "tile": list(TILE),
+                   "kernel": "two-CTA cluster (sb_strassen_gemm_pair)" if args.kernel == "pair"
+                   else "one-CTA (sb_strassen_gemm)",
                    "l2": "inputs 256 MiB > 126 MiB L2, no flush",
                    "inputs": f"N(0,1) bf16, default_rng({SEED_A}) / ({SEED_B})",
                    "parallelism": f"replicas x{world}" if world > 1 else "single GPU"},

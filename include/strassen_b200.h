@@ -157,6 +157,23 @@ SB_API int sb_classical_gemm(sb_stream_t stream,
                       int32_t bm, int32_t bn, int32_t bk, int32_t out_dtype);
 
 /*
+ * sb_strassen_gemm_pair -- C = A·B, no epilogue, on the two-CTA kernel: a
+ * thread-block cluster of two CTAs shares each 128 x 128 product tile, splits
+ * the seven Strassen products between them (3.5 each, 128-wide tensor-core
+ * products), loads half of the operand quadrants each and forwards the shared
+ * ones to the peer through distributed shared memory.  Same contract as
+ * sb_strassen_gemm with ep == NULL (strassen_pallas.py:882-1221, no epilogue):
+ * same arguments, validation and Strassen block semantics; the fp32 summation
+ * order of the recombination differs, so results agree with sb_strassen_gemm
+ * to fp32 rounding, not bit for bit.
+ */
+SB_API int sb_strassen_gemm_pair(sb_stream_t stream,
+                                 const void* a, const void* b, void* c,
+                                 int64_t m, int64_t n, int64_t k,
+                                 int64_t lda, int64_t ldb, int64_t ldc,
+                                 int32_t bm, int32_t bn, int32_t bk, int32_t out_dtype);
+
+/*
  * sb_strassen_gemm_norm_residual_noalloc -- the norm_residual_add epilogue of
  * sb_strassen_gemm, with its fp32 scratch in a device array built into the
  * library instead of a caller workspace.  No counterpart in the reference.

@@ -89,6 +89,8 @@ SIGNATURES = {
                  _c_int, _c_int, _c_int, ctypes.POINTER(SbEpilogue)]),
     "sb_classical_gemm": (_c_int, [_c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_i64, _c_i64, _c_i64,
                                    _c_i64, _c_i64, _c_i64, _c_int, _c_int, _c_int, _c_int]),
+    "sb_strassen_gemm_pair": (_c_int, [_c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_i64, _c_i64, _c_i64,
+                                       _c_i64, _c_i64, _c_i64, _c_int, _c_int, _c_int, _c_int]),
     "sb_strassen_gemm_lhs_transposed": (_c_int, [_c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_i64, _c_i64,
                                                  _c_i64, _c_i64, _c_i64, _c_i64, _c_int, _c_int,
                                                  _c_int, _c_int]),

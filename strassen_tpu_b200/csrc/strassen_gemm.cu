@@ -1045,6 +1045,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
+// The two-CTA product-split kernel (sb_strassen_gemm_pair).
+#include "strassen_pair.cuh"
+
 // Failure-detection self-test (sb_wait_selftest): warp 0 waits on a barrier
 // nobody arrives on and gives up after the bounded-wait limit, raising the abort
 // flag; warp 1 starts waiting on another such barrier half a limit later, so it
@@ -1440,6 +1443,77 @@ GemmParams base_params(int64_t m, int64_t n, int64_t k, int32_t bm, int32_t bn, 
   return p;
 }
 
+// Tensor maps of the two-CTA kernel (strassen_pair.cuh): each CTA's one copy
+// per operand and K step lands half of the pair's quadrants.
+//   A: dims (k, row in half-block, block, qk, qr) as make_ts_maps; box
+//      {16, rows, blocks, 2, 1} -> quadrants (r, 0), (r, 1) at qr = r.
+//   B: dims (column in a 64-column chunk, k, chunk, qc, qk), strides (1, ldb,
+//      64, half_bn, half_bk*ldb) elements; box {64, 16, 2, 1, 2} -> quadrants
+//      (0, qc), (1, qc), each 16 rows of 128 columns as two 2 KB chunks.
+int make_pair_maps(const void* a, const void* b, int64_t m, int64_t n, int64_t k, int64_t lda, int64_t ldb,
+                   int32_t bm, int32_t bn, int32_t bk, CUtensorMap* ta, CUtensorMap* tb) {
+  EncodeTiledFn enc = encode_fn();
+  if (!enc) return fail(SB_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
+  const int64_t half_bm = bm / 2, half_bn = bn / 2, half_bk = bk / 2;
+  const uint32_t rows = half_bm >= kBlockM ? kBlockM : (uint32_t)half_bm;
+  const uint32_t blocks = half_bm >= kBlockM ? 1 : (uint32_t)(kBlockM / half_bm);
+  {
+    cuuint64_t dims[5] = {(cuuint64_t)k, (cuuint64_t)half_bm, (cuuint64_t)(m / bm), 2, 2};
+    cuuint64_t strides[4] = {(cuuint64_t)(lda * 2), (cuuint64_t)(bm * lda * 2), (cuuint64_t)(half_bk * 2),
+                             (cuuint64_t)(half_bm * lda * 2)};
+    cuuint32_t box[5] = {16, rows, blocks, 2, 1};
+    cuuint32_t estr[5] = {1, 1, 1, 1, 1};
+    CUresult r = enc(ta, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 5, const_cast<void*>(a), dims, strides, box, estr,
+                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_32B, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(SB_ERR_CUDA, "cuTensorMapEncodeTiled(A, pair) failed: " + std::to_string((int)r));
+  }
+  {
+    cuuint64_t dims[5] = {64, (cuuint64_t)k, (cuuint64_t)(n / 64), 2, 2};
+    cuuint64_t strides[4] = {(cuuint64_t)(ldb * 2), 128, (cuuint64_t)(half_bn * 2), (cuuint64_t)(half_bk * ldb * 2)};
+    cuuint32_t box[5] = {64, 16, 2, 1, 2};
+    cuuint32_t estr[5] = {1, 1, 1, 1, 1};
+    CUresult r = enc(tb, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 5, const_cast<void*>(b), dims, strides, box, estr,
+                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(SB_ERR_CUDA, "cuTensorMapEncodeTiled(B, pair) failed: " + std::to_string((int)r));
+  }
+  return SB_OK;
+}
+
+// Launches the two-CTA kernel: clusters of two consecutive CTAs, one cluster
+// per 128 x 128 product tile.
+template <bool kOutF32>
+int launch_pair(cudaStream_t stream, const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p) {
+  auto kernel = strassen_pair_kernel<kOutF32>;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64)
+    return fail(SB_ERR_DEVICE, "no usable current device");
+  static std::once_flag once[64];
+  static cudaError_t attr_err[64];
+  std::call_once(once[dev], [&]() {
+    attr_err[dev] = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, pair::kSmem);
+  });
+  if (attr_err[dev] != cudaSuccess)
+    return fail(SB_ERR_CUDA, std::string("cudaFuncSetAttribute: ") + cudaGetErrorString(attr_err[dev]));
+  cudaLaunchConfig_t cfg;
+  std::memset(&cfg, 0, sizeof(cfg));
+  cfg.gridDim = dim3((unsigned)(2 * p.tiles_m * p.tiles_n), 1, 1);
+  cfg.blockDim = dim3(kThreads, 1, 1);
+  cfg.dynamicSmemBytes = pair::kSmem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, ta, tb, p);
+  if (e != cudaSuccess) return fail(SB_ERR_CUDA, std::string("pair kernel launch: ") + cudaGetErrorString(e));
+  return SB_OK;
+}
+
 void apply_options(GemmParams& p, int formula, int perm, const int32_t* schedule) {
   p.formula = formula == SB_FORMULA_DUAL ? 1 : formula == SB_FORMULA_POWERS ? 2 : 0;
   p.swap_m = perm & 1;
@@ -1678,6 +1752,23 @@ int sb_classical_gemm(sb_stream_t stream_, const void* a, const void* b, void* c
   if (st != SB_OK) return st;
   GemmParams p = base_params(m, n, k, bm, bn, bk, c, ldc, ClassicalPipe::BK);
   return dispatch(false, SB_EPI_NONE, out_dtype == SB_F32, stream, ta, tb, p);
+}
+
+int sb_strassen_gemm_pair(sb_stream_t stream_, const void* a, const void* b, void* c, int64_t m, int64_t n,
+                          int64_t k, int64_t lda, int64_t ldb, int64_t ldc, int32_t bm, int32_t bn, int32_t bk,
+                          int32_t out_dtype) {
+  cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_);
+  int st = validate_core(a, b, c, m, n, k, lda, ldb, ldc, bm, bn, bk, out_dtype);
+  if (st != SB_OK) return st;
+  if (ldc < n) return fail(SB_ERR_ALIGNMENT, "ldc must be >= N");
+  st = check_device();
+  if (st != SB_OK) return st;
+  CUtensorMap ta, tb;
+  st = make_pair_maps(a, b, m, n, k, lda, ldb, bm, bn, bk, &ta, &tb);
+  if (st != SB_OK) return st;
+  GemmParams p = base_params(m, n, k, bm, bn, bk, c, ldc, 16);
+  p.tiles_n = p.Np / pair::kCols;  // bn % 256 == 0, so Np is a multiple of 128
+  return out_dtype == SB_F32 ? launch_pair<true>(stream, ta, tb, p) : launch_pair<false>(stream, ta, tb, p);
 }
 
 int sb_strassen_gemm_lhs_transposed(sb_stream_t stream_, const void* at, const void* b, void* c,

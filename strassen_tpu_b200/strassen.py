@@ -536,6 +536,42 @@ def classical_matmul(a, b, *, bm=TUNED_BM, bn=TUNED_BN, bk=TUNED_BK, output_dtyp
     return out
 
 
+def pair_matmul(a, b, *, bm=TUNED_BM, bn=TUNED_BN, bk=TUNED_BK, output_dtype=None, out=None):
+    """``strassen_matmul(a, b, bm=, bn=, bk=, output_dtype=)`` without an epilogue,
+    on the two-CTA kernel (``sb_strassen_gemm_pair``): a cluster of two CTAs per
+    128 x 128 product tile, 3.5 of the seven products each, operand quadrants
+    shared through distributed shared memory.  Same algorithm and operand
+    pairing as strassen_pallas.py:156-880; the recombination's fp32 order
+    differs from :func:`strassen_matmul`.
+    """
+    if a.ndim != 2 or b.ndim != 2:
+        raise ValueError("pair_matmul expects two rank-2 matrices")
+    m, k = a.shape
+    k2, n = b.shape
+    if k != k2:
+        raise ValueError(f"inner dimensions disagree: {k} vs {k2}")
+    if a.dtype != torch.bfloat16 or b.dtype != torch.bfloat16:
+        raise ValueError("inputs must be BF16")
+    for name, dimension, block in (("M", m, bm), ("N", n, bn), ("K", k, bk)):
+        if dimension % block:
+            raise ValueError(f"{name}={dimension} is not divisible by {block}")
+    check_tiling(bm, bn, bk)
+    if a.device.type != "cuda" or b.device.type != "cuda":
+        raise ValueError("pair_matmul runs on a CUDA device (no CPU fallback)")
+    out_dt = _as_torch_dtype(output_dtype) or torch.bfloat16
+    device = a.device
+    a, b = _rowmajor(a), _rowmajor(b)
+    if out is None:
+        out = torch.empty((m, n), dtype=out_dt, device=device)
+    lib = _native.load()
+    with torch.cuda.device(device):
+        status = lib.sb_strassen_gemm_pair(_stream_handle(device), a.data_ptr(), b.data_ptr(),
+                                           out.data_ptr(), m, n, k, _ld(a), _ld(b), _ld(out),
+                                           bm, bn, bk, SB_F32 if out_dt == torch.float32 else SB_BF16)
+    _native.check(status)
+    return out
+
+
 def rms_norm(x, scale, eps: float = 1e-6, out=None):
     """bf16 RMSNorm with fp32 math on the sm_100a row kernel.
 
