@@ -50,8 +50,9 @@ def parse():
     p.add_argument("--no-cpu-baseline", action="store_true",
                    help="skip the CPU oracle timing (used for ncu captures)")
     p.add_argument("--no-e2e", action="store_true", help="skip the host-buffer end-to-end loop")
-    p.add_argument("--kernel", default="single", choices=["single", "pair"],
-                   help="GEMM workload: the one-CTA Strassen kernel or the two-CTA cluster kernel")
+    p.add_argument("--kernel", default="single", choices=["single", "pair", "pair-planes"],
+                   help="GEMM workload: the one-CTA Strassen kernel, the two-CTA cluster kernel, or the "
+                        "two-CTA kernel on B operand planes formed inside each step")
     p.add_argument("--workload", default="gemm", choices=["gemm", "qwen3-8b", "qwen3-32b"],
                    help="gemm: the 8192^3 Strassen GEMM (default, the driver's line); "
                         "qwen3-*: tensor-parallel decoder prefill tokens/s (BASELINE configs 4/5)")
@@ -197,8 +198,10 @@ def run_reference(args):
         "ms_per_step": 1e3 * total_t / args.steps, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
         "config": {"workload": f"strassen_gemm_{M}x{N}x{K}_bf16", "tile": list(TILE),
-                   "kernel": "two-CTA cluster (sb_strassen_gemm_pair)" if args.kernel == "pair"
-                   else "one-CTA (sb_strassen_gemm)",
+                   "kernel": {"single": "one-CTA (sb_strassen_gemm)",
+                              "pair": "two-CTA cluster (sb_strassen_gemm_pair)",
+                              "pair-planes": "B operand planes + two-CTA cluster (sb_strassen_b_operands, "
+                                             "sb_strassen_gemm_pair_planes), both timed"}[args.kernel],
                    "sample": sample},
         "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port",
                          "sample": sample},
@@ -234,10 +237,20 @@ def run_ours(args):
     stream = torch.cuda.current_stream(device)
     flops = 2.0 * M * N * K
 
-    gemm = sb.pair_matmul if args.kernel == "pair" else sb.strassen_matmul
+    launches_per_step = 1
+    if args.kernel == "pair-planes":
+        planes = torch.empty(7, K // 2, N // 2, dtype=torch.bfloat16, device=device)
+        launches_per_step = 2
 
-    def step():
-        gemm(a, b, bm=TILE[0], bn=TILE[1], bk=TILE[2], out=c)
+        def step():
+            # B's operand planes are formed inside the timed step (B is an input).
+            sb.strassen_b_operands(b, bn=TILE[1], bk=TILE[2], out=planes)
+            sb.pair_matmul(a, None, b_operands=planes, bm=TILE[0], bn=TILE[1], bk=TILE[2], out=c)
+    else:
+        gemm = sb.pair_matmul if args.kernel == "pair" else sb.strassen_matmul
+
+        def step():
+            gemm(a, b, bm=TILE[0], bn=TILE[1], bk=TILE[2], out=c)
 
     def barrier():
         if world > 1:
@@ -332,8 +345,10 @@ def run_ours(args):
         "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
         "config": {"workload": f"strassen_gemm_{M}x{N}x{K}_bf16", "tile": list(TILE),
-                   "kernel": "two-CTA cluster (sb_strassen_gemm_pair)" if args.kernel == "pair"
-                   else "one-CTA (sb_strassen_gemm)",
+                   "kernel": {"single": "one-CTA (sb_strassen_gemm)",
+                              "pair": "two-CTA cluster (sb_strassen_gemm_pair)",
+                              "pair-planes": "B operand planes + two-CTA cluster (sb_strassen_b_operands, "
+                                             "sb_strassen_gemm_pair_planes), both timed"}[args.kernel],
                    "l2": "inputs 256 MiB > 126 MiB L2, no flush",
                    "inputs": f"N(0,1) bf16, default_rng({SEED_A}) / ({SEED_B})",
                    "parallelism": f"replicas x{world}" if world > 1 else "single GPU"},
@@ -344,7 +359,7 @@ def run_ours(args):
         "cpu_baseline": cpu,
         "e2e": e2e,
         "clocks": clock,
-        "gpu_launches": args.steps,
+        "gpu_launches": args.steps * launches_per_step,
         "comparison": {
             "cublas_tflops": flops / (cublas_ms * 1e-3) / 1e12,
             "strassen_vs_cublas": (flops / (ms * 1e-3)) / (flops / (cublas_ms * 1e-3)),

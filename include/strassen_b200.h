@@ -158,20 +158,46 @@ SB_API int sb_classical_gemm(sb_stream_t stream,
 
 /*
  * sb_strassen_gemm_pair -- C = A·B, no epilogue, on the two-CTA kernel: a
- * thread-block cluster of two CTAs shares each 128 x 128 product tile, splits
- * the seven Strassen products between them (3.5 each, 128-wide tensor-core
- * products), loads half of the operand quadrants each and forwards the shared
- * ones to the peer through distributed shared memory.  Same contract as
- * sb_strassen_gemm with ep == NULL (strassen_pallas.py:882-1221, no epilogue):
- * same arguments, validation and Strassen block semantics; the fp32 summation
- * order of the recombination differs, so results agree with sb_strassen_gemm
- * to fp32 rounding, not bit for bit.
+ * thread-block cluster of two CTAs shares each 128 x 128 product tile and
+ * splits the seven Strassen products between them (3.5 each, 128-wide
+ * tensor-core products); the two quadrant halves of every output tile are
+ * finished after one fp32 partial exchange through distributed shared memory.
+ * Same contract as sb_strassen_gemm with ep == NULL (strassen_pallas.py:882-1221,
+ * no epilogue): same arguments, validation and Strassen block semantics; the
+ * fp32 order of the final recombination differs, so results agree with
+ * sb_strassen_gemm to fp32 rounding, not bit for bit.
  */
 SB_API int sb_strassen_gemm_pair(sb_stream_t stream,
                                  const void* a, const void* b, void* c,
                                  int64_t m, int64_t n, int64_t k,
                                  int64_t lda, int64_t ldb, int64_t ldc,
                                  int32_t bm, int32_t bn, int32_t bk, int32_t out_dtype);
+
+/*
+ * sb_strassen_b_operands -- the seven B operands of every Strassen block of
+ * B [K, N] (ldb) for the tile (bn, bk), formed once: the reference's B
+ * pre-adds (strassen_pallas.py:324-379), each rounded once to bf16, written as
+ * planes [7][K/2][N/2] bf16 (contiguous, sb_b_operands_bytes(k, n) bytes) in
+ * the order P3 (b1-b3), P5 (b3), P7 (b2+b3), P1 (b0+b3), P2 (b0),
+ * P4 (b2-b0), P6 (b0+b1).  For a weight used many times this is an offline
+ * relayout, like the reference's swiglu_weight_layout (strassen_pallas.py:1381-1411).
+ */
+SB_API size_t sb_b_operands_bytes(int64_t k, int64_t n);
+SB_API int sb_strassen_b_operands(sb_stream_t stream, const void* b, void* planes,
+                                  int64_t k, int64_t n, int64_t ldb, int32_t bn, int32_t bk);
+
+/*
+ * sb_strassen_gemm_pair_planes -- sb_strassen_gemm_pair with B given as its
+ * operand planes (sb_strassen_b_operands, built for the same bn and bk): the
+ * kernel loads each product's B operand as it is and forms no B sums.  The
+ * operand values are the ones the in-kernel sums produce, so the result
+ * equals sb_strassen_gemm_pair on the raw B bit for bit.
+ */
+SB_API int sb_strassen_gemm_pair_planes(sb_stream_t stream,
+                                        const void* a, const void* b_planes, void* c,
+                                        int64_t m, int64_t n, int64_t k,
+                                        int64_t lda, int64_t ldc,
+                                        int32_t bm, int32_t bn, int32_t bk, int32_t out_dtype);
 
 /*
  * sb_strassen_gemm_norm_residual_noalloc -- the norm_residual_add epilogue of

@@ -91,6 +91,10 @@ SIGNATURES = {
                                    _c_i64, _c_i64, _c_i64, _c_int, _c_int, _c_int, _c_int]),
     "sb_strassen_gemm_pair": (_c_int, [_c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_i64, _c_i64, _c_i64,
                                        _c_i64, _c_i64, _c_i64, _c_int, _c_int, _c_int, _c_int]),
+    "sb_b_operands_bytes": (_c_size, [_c_i64, _c_i64]),
+    "sb_strassen_b_operands": (_c_int, [_c_ptr, _c_ptr, _c_ptr, _c_i64, _c_i64, _c_i64, _c_int, _c_int]),
+    "sb_strassen_gemm_pair_planes": (_c_int, [_c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_i64, _c_i64, _c_i64,
+                                              _c_i64, _c_i64, _c_int, _c_int, _c_int, _c_int]),
     "sb_strassen_gemm_lhs_transposed": (_c_int, [_c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_i64, _c_i64,
                                                  _c_i64, _c_i64, _c_i64, _c_i64, _c_int, _c_int,
                                                  _c_int, _c_int]),

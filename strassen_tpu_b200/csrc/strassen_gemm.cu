@@ -45,6 +45,7 @@
 #include <cuda_runtime.h>
 #include <cuda_bf16.h>
 
+#include <algorithm>
 #include <cmath>
 #include <cstdio>
 #include <cstring>
@@ -1443,56 +1444,91 @@ GemmParams base_params(int64_t m, int64_t n, int64_t k, int32_t bm, int32_t bn, 
   return p;
 }
 
-// Tensor maps of the two-CTA kernel (strassen_pair.cuh): each CTA's one copy
-// per operand and K step lands half of the pair's quadrants.
-//   A: dims (k, row in half-block, block, qk, qr) as make_ts_maps; box
-//      {16, rows, blocks, 2, 1} -> quadrants (r, 0), (r, 1) at qr = r.
-//   B: dims (column in a 64-column chunk, k, chunk, qc, qk), strides (1, ldb,
-//      64, half_bn, half_bk*ldb) elements; box {64, 16, 2, 1, 2} -> quadrants
-//      (0, qc), (1, qc), each 16 rows of 128 columns as two 2 KB chunks.
-int make_pair_maps(const void* a, const void* b, int64_t m, int64_t n, int64_t k, int64_t lda, int64_t ldb,
-                   int32_t bm, int32_t bn, int32_t bk, CUtensorMap* ta, CUtensorMap* tb) {
+// Tensor maps of the two-CTA kernel (strassen_pair.cuh).  Both B modes share
+// the two A maps:
+//   a:  dims (k, row in half-block, block, qk, qr) as make_ts_maps; box
+//       {16, rows, blocks, 2, 1} -> quadrants (r, 0), (r, 1) at qr = r;
+//   a1: the same dims, box {16, rows, blocks, 1, 1} -> one quadrant.
+// Raw B (b_planes == nullptr): dims (column in a 64-column chunk, k, chunk,
+// qc, qk), strides (1, ldb, 64, half_bn, half_bk*ldb) elements;
+//   b:  box {64, 16, 2, 1, 2} -> quadrants (0, qc), (1, qc), 16 x 128 each;
+//   b1: box {64, 16, 2, 1, 1} -> one 16 x 128 quadrant;
+//   bh: box {64, 16, 1, 1, 1} -> one 64-column chunk of a quadrant.
+// B operand planes ([7][K/2][N/2], from b_operand_planes_kernel): dims
+// (column in a chunk, kappa, chunk, plane);
+//   b:  box {64, 16, 2, 3} -> three planes of 16 x 128;  bh: box {64, 16, 1, 1}.
+struct PairMaps {
+  CUtensorMap a, a1, b, b1, bh;
+};
+
+int make_pair_maps(const void* a, const void* b, const void* b_planes, int64_t m, int64_t n, int64_t k,
+                   int64_t lda, int64_t ldb, int32_t bm, int32_t bn, int32_t bk, PairMaps* maps) {
   EncodeTiledFn enc = encode_fn();
   if (!enc) return fail(SB_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
   const int64_t half_bm = bm / 2, half_bn = bn / 2, half_bk = bk / 2;
   const uint32_t rows = half_bm >= kBlockM ? kBlockM : (uint32_t)half_bm;
   const uint32_t blocks = half_bm >= kBlockM ? 1 : (uint32_t)(kBlockM / half_bm);
+  cuuint32_t estr[5] = {1, 1, 1, 1, 1};
+  auto encode = [&](CUtensorMap* map, const void* base, cuuint32_t rank, const cuuint64_t* dims,
+                    const cuuint64_t* strides, const cuuint32_t* box, CUtensorMapSwizzle sw,
+                    const char* what) -> int {
+    CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, rank, const_cast<void*>(base), dims, strides, box,
+                     estr, CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS)
+      return fail(SB_ERR_CUDA, std::string("cuTensorMapEncodeTiled(") + what + ") failed: " + std::to_string((int)r));
+    return SB_OK;
+  };
   {
     cuuint64_t dims[5] = {(cuuint64_t)k, (cuuint64_t)half_bm, (cuuint64_t)(m / bm), 2, 2};
     cuuint64_t strides[4] = {(cuuint64_t)(lda * 2), (cuuint64_t)(bm * lda * 2), (cuuint64_t)(half_bk * 2),
                              (cuuint64_t)(half_bm * lda * 2)};
     cuuint32_t box[5] = {16, rows, blocks, 2, 1};
-    cuuint32_t estr[5] = {1, 1, 1, 1, 1};
-    CUresult r = enc(ta, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 5, const_cast<void*>(a), dims, strides, box, estr,
-                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_32B, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
-                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-    if (r != CUDA_SUCCESS) return fail(SB_ERR_CUDA, "cuTensorMapEncodeTiled(A, pair) failed: " + std::to_string((int)r));
+    int st = encode(&maps->a, a, 5, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_32B, "A, pair");
+    if (st != SB_OK) return st;
+    box[3] = 1;
+    st = encode(&maps->a1, a, 5, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_32B, "A, one quadrant");
+    if (st != SB_OK) return st;
   }
-  {
+  if (b_planes == nullptr) {
     cuuint64_t dims[5] = {64, (cuuint64_t)k, (cuuint64_t)(n / 64), 2, 2};
     cuuint64_t strides[4] = {(cuuint64_t)(ldb * 2), 128, (cuuint64_t)(half_bn * 2), (cuuint64_t)(half_bk * ldb * 2)};
     cuuint32_t box[5] = {64, 16, 2, 1, 2};
-    cuuint32_t estr[5] = {1, 1, 1, 1, 1};
-    CUresult r = enc(tb, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 5, const_cast<void*>(b), dims, strides, box, estr,
-                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
-                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-    if (r != CUDA_SUCCESS) return fail(SB_ERR_CUDA, "cuTensorMapEncodeTiled(B, pair) failed: " + std::to_string((int)r));
+    int st = encode(&maps->b, b, 5, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B, "B, pair");
+    if (st != SB_OK) return st;
+    box[4] = 1;
+    st = encode(&maps->b1, b, 5, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B, "B, one quadrant");
+    if (st != SB_OK) return st;
+    box[2] = 1;
+    return encode(&maps->bh, b, 5, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B, "B, half quadrant");
   }
+  const int64_t kh = k / 2, nh = n / 2;
+  cuuint64_t dims[4] = {64, (cuuint64_t)kh, (cuuint64_t)(nh / 64), 7};
+  cuuint64_t strides[3] = {(cuuint64_t)(nh * 2), 128, (cuuint64_t)(kh * nh * 2)};
+  cuuint32_t box[4] = {64, 16, 2, 3};
+  int st = encode(&maps->b, b_planes, 4, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B, "B planes");
+  if (st != SB_OK) return st;
+  box[2] = 1;
+  box[3] = 1;
+  st = encode(&maps->bh, b_planes, 4, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B, "B plane, half");
+  if (st != SB_OK) return st;
+  maps->b1 = maps->bh;  // unused with planes
   return SB_OK;
 }
 
 // Launches the two-CTA kernel: clusters of two consecutive CTAs, one cluster
 // per 128 x 128 product tile.
-template <bool kOutF32>
-int launch_pair(cudaStream_t stream, const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p) {
-  auto kernel = strassen_pair_kernel<kOutF32>;
+template <bool kOutF32, bool kPreB>
+int launch_pair(cudaStream_t stream, const PairMaps& m, const GemmParams& p) {
+  auto kernel = strassen_pair_kernel<kOutF32, kPreB>;
+  constexpr int kSmem = pair::Geo<kPreB>::SMEM;
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64)
     return fail(SB_ERR_DEVICE, "no usable current device");
   static std::once_flag once[64];
   static cudaError_t attr_err[64];
   std::call_once(once[dev], [&]() {
-    attr_err[dev] = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, pair::kSmem);
+    attr_err[dev] = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
   });
   if (attr_err[dev] != cudaSuccess)
     return fail(SB_ERR_CUDA, std::string("cudaFuncSetAttribute: ") + cudaGetErrorString(attr_err[dev]));
@@ -1500,7 +1536,7 @@ int launch_pair(cudaStream_t stream, const CUtensorMap& ta, const CUtensorMap& t
   std::memset(&cfg, 0, sizeof(cfg));
   cfg.gridDim = dim3((unsigned)(2 * p.tiles_m * p.tiles_n), 1, 1);
   cfg.blockDim = dim3(kThreads, 1, 1);
-  cfg.dynamicSmemBytes = pair::kSmem;
+  cfg.dynamicSmemBytes = kSmem;
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -1509,9 +1545,26 @@ int launch_pair(cudaStream_t stream, const CUtensorMap& ta, const CUtensorMap& t
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  const cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, ta, tb, p);
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, m.a, m.a1, m.b, m.b1, m.bh, p);
   if (e != cudaSuccess) return fail(SB_ERR_CUDA, std::string("pair kernel launch: ") + cudaGetErrorString(e));
   return SB_OK;
+}
+
+// Shared body of sb_strassen_gemm_pair (raw B) and sb_strassen_gemm_pair_planes.
+int run_pair(cudaStream_t stream, const void* a, const void* b, const void* b_planes, void* c, int64_t m,
+             int64_t n, int64_t k, int64_t lda, int64_t ldb, int64_t ldc, int32_t bm, int32_t bn, int32_t bk,
+             int32_t out_dtype) {
+  if (ldc < n) return fail(SB_ERR_ALIGNMENT, "ldc must be >= N");
+  int st = check_device();
+  if (st != SB_OK) return st;
+  PairMaps maps;
+  st = make_pair_maps(a, b, b_planes, m, n, k, lda, ldb, bm, bn, bk, &maps);
+  if (st != SB_OK) return st;
+  GemmParams p = base_params(m, n, k, bm, bn, bk, c, ldc, 16);
+  p.tiles_n = p.Np / pair::kCols;  // bn % 256 == 0, so Np is a multiple of 128
+  if (b_planes)
+    return out_dtype == SB_F32 ? launch_pair<true, true>(stream, maps, p) : launch_pair<false, true>(stream, maps, p);
+  return out_dtype == SB_F32 ? launch_pair<true, false>(stream, maps, p) : launch_pair<false, false>(stream, maps, p);
 }
 
 void apply_options(GemmParams& p, int formula, int perm, const int32_t* schedule) {
@@ -1757,18 +1810,47 @@ int sb_classical_gemm(sb_stream_t stream_, const void* a, const void* b, void* c
 int sb_strassen_gemm_pair(sb_stream_t stream_, const void* a, const void* b, void* c, int64_t m, int64_t n,
                           int64_t k, int64_t lda, int64_t ldb, int64_t ldc, int32_t bm, int32_t bn, int32_t bk,
                           int32_t out_dtype) {
-  cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_);
   int st = validate_core(a, b, c, m, n, k, lda, ldb, ldc, bm, bn, bk, out_dtype);
   if (st != SB_OK) return st;
-  if (ldc < n) return fail(SB_ERR_ALIGNMENT, "ldc must be >= N");
-  st = check_device();
+  return run_pair(reinterpret_cast<cudaStream_t>(stream_), a, b, nullptr, c, m, n, k, lda, ldb, ldc, bm, bn, bk,
+                  out_dtype);
+}
+
+size_t sb_b_operands_bytes(int64_t k, int64_t n) {
+  if (k <= 0 || n <= 0) return 0;
+  return (size_t)7 * (size_t)(k / 2) * (size_t)(n / 2) * 2u;
+}
+
+int sb_strassen_b_operands(sb_stream_t stream_, const void* b, void* planes, int64_t k, int64_t n, int64_t ldb,
+                           int32_t bn, int32_t bk) {
+  if (!b || !planes) return fail(SB_ERR_RANK, "null matrix pointer");
+  if (k <= 0 || n <= 0) return fail(SB_ERR_RANK, "matrix dimensions must be positive");
+  if (bn <= 0 || bk <= 0 || n % bn || k % bk)
+    return fail(SB_ERR_DIVISIBILITY, "K=" + std::to_string(k) + ", N=" + std::to_string(n) +
+                                         " must be divisible by bk=" + std::to_string(bk) + ", bn=" + std::to_string(bn));
+  if (bn % 256 || bk % 256) return fail(SB_ERR_TILING, "bn and bk must be multiples of 256");
+  if (k > (int64_t)INT32_MAX || n > (int64_t)INT32_MAX)
+    return fail(SB_ERR_UNSUPPORTED, "dimensions above 2^31-1 are not supported");
+  if (!aligned16(b) || !aligned16(planes) || ldb % 8 || ldb < n)
+    return fail(SB_ERR_ALIGNMENT, "B and the planes must be 16-byte aligned; ldb a multiple of 8 covering N");
+  const int64_t chunks = (k / 2) * (n / 16);
+  const unsigned grid = (unsigned)std::min<int64_t>((chunks + 255) / 256, 148 * 16);
+  b_operand_planes_kernel<<<grid, 256, 0, reinterpret_cast<cudaStream_t>(stream_)>>>(
+      reinterpret_cast<const __nv_bfloat16*>(b), ldb, (int32_t)k, (int32_t)n, bn, bk,
+      reinterpret_cast<__nv_bfloat16*>(planes));
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return fail(SB_ERR_CUDA, std::string("B operand planes launch: ") + cudaGetErrorString(e));
+  return SB_OK;
+}
+
+int sb_strassen_gemm_pair_planes(sb_stream_t stream_, const void* a, const void* b_planes, void* c, int64_t m,
+                                 int64_t n, int64_t k, int64_t lda, int64_t ldc, int32_t bm, int32_t bn, int32_t bk,
+                                 int32_t out_dtype) {
+  // The planes stand in for B [K, N] (ldb = N) in the shared validation.
+  int st = validate_core(a, b_planes, c, m, n, k, lda, n, ldc, bm, bn, bk, out_dtype);
   if (st != SB_OK) return st;
-  CUtensorMap ta, tb;
-  st = make_pair_maps(a, b, m, n, k, lda, ldb, bm, bn, bk, &ta, &tb);
-  if (st != SB_OK) return st;
-  GemmParams p = base_params(m, n, k, bm, bn, bk, c, ldc, 16);
-  p.tiles_n = p.Np / pair::kCols;  // bn % 256 == 0, so Np is a multiple of 128
-  return out_dtype == SB_F32 ? launch_pair<true>(stream, ta, tb, p) : launch_pair<false>(stream, ta, tb, p);
+  return run_pair(reinterpret_cast<cudaStream_t>(stream_), a, nullptr, b_planes, c, m, n, k, lda, n, ldc, bm, bn,
+                  bk, out_dtype);
 }
 
 int sb_strassen_gemm_lhs_transposed(sb_stream_t stream_, const void* at, const void* b, void* c,

@@ -12,24 +12,25 @@
 //
 // Each CTA accumulates 3 x 128 + 64 = 448 TMEM columns, so three of its four
 // tcgen05.mma per 16-deep K step are 128 x 128 x 16 instead of 128 x 64 x 16:
-// half the instructions per unit of work of the one-CTA kernel.
+// about half the MMA instructions per unit of work of the one-CTA kernel.
 //
-// Operands.  CTA r TMA-loads only half of what the pair needs -- the A
-// quadrants of row half r (a0, a1 or a2, a3) and the B quadrants of column
-// half 1 - r (b1, b3 or b0, b2) -- and forwards the part its peer also needs
-// (CTA 0: a0, b1, b3's right half; CTA 1: a3, b2, b0's left half) from its own
-// shared memory into the peer's with one shared-to-shared bulk copy per tile
-// (one source, one destination CTA per copy).
-// Every operand crosses the L2 once per pair instead of once per CTA.
-//
-// Operand sums, formed by the sum warps with one RNE bf16 rounding each (the
-// reference's pre-add rounding):
-//   A (into a two-step TMEM ring): CTA 0 a0+a1, a1-a3, a0+a3; CTA 1 a2+a3,
-//     a2-a0, a0+a3.
-//   B (shared memory; never over a tile that is forwarded): CTA 0 b1-b3 into
-//     the sum slot, b2+b3 over the received b2, (b0+b3)L over the received
-//     b0L; CTA 1 b2-b0 into the sum slot, b0+b1 over the received b1,
-//     (b0+b3)R over the received b3R.
+// Operands.  Each CTA TMA-loads the three A quadrants its products use (CTA 0:
+// a0, a1, a3; CTA 1: a2, a3, a0) and its B operands, in one of two forms:
+//   * kPreB = false (sb_strassen_gemm_pair): the raw B quadrants it needs
+//     (CTA 0: b1, b3, b2, b0's left half; CTA 1: b0, b2, b1, b3's right
+//     half); the sum warps form the B sums in shared memory -- CTA 0 b1-b3
+//     into the sum slot, b2+b3 over b2, (b0+b3)L over b0L; CTA 1 b2-b0 into
+//     the sum slot, b0+b1 over b1, (b0+b3)R over b3R.
+//   * kPreB = true (sb_strassen_gemm_pair_planes): the seven B operands were
+//     formed once by b_operand_planes_kernel (the same bf16 sums, the same
+//     rounding) and each CTA loads its three and a half operand planes as they
+//     are: no B sums in the K loop, so the step's shared-memory traffic is the
+//     TMA fill, the A-row reads of the sum warps and the MMA operand reads.
+// Two producer threads (warps 0 and 2) issue the copies and arm the stage's
+// barrier together.  The A sums (CTA 0: a0+a1, a1-a3, a0+a3; CTA 1: a2+a3,
+// a2-a0, a0+a3) go to a two-step TMEM ring and feed A-from-TMEM MMAs; the raw
+// a0 (CTA 0) or a3 (CTA 1) is read from shared memory.  Every pre-add is one
+// RNE bf16 rounding, the reference's pre-add rounding.
 //
 // Recombination.  C11 = M1+M4-M5+M7 and C12 = M3+M5 belong to CTA 0 (top
 // rows of each block), C21 = M2+M4 and C22 = M1-M2+M3+M6 to CTA 1 (bottom
@@ -40,65 +41,66 @@
 //   CTA 1: C21 = M2 + M4, C22 = ((Y0 + [0 | M1R]) - M2) + M6.
 //
 // Synchronisation (all waits bounded, as in the one-CTA kernel):
-//   own[s]   own TMA landed (16 KB per step);
-//   full[s]  own data landed (the forwarder's arrival) + the producer's
-//            arrival expecting the peer's 10 KB + those bytes;
+//   full[s]  both producers' arrivals + the stage's TMA bytes;
 //   sums[s]  the four sum warps of the step's set; empty[s] local MMA commit;
-//   pfree[s] the peer's producer: its stage s may be overwritten by our
-//            forward (remote arrival, cluster scope);
-//   xfree / xdata  the epilogue exchange (remote arrivals, cluster scope).
-// Both CTAs end with a cluster barrier, so neither leaves while the other may
-// still touch its shared memory.
+//   xfree / xdata  the epilogue exchange: remote arrivals from the peer, waited
+//            with cluster-scope acquire.
+// The K loop never waits on the peer.  Both CTAs end with a cluster barrier,
+// so neither leaves while the other may still write into its shared memory.
 //
-// Roles: warp 0 TMA producer, warp 1 TMEM allocation + MMA issue, warp 2
-// forwarder, warps 4-11 operand sums then epilogue (as in the one-CTA kernel).
+// Roles: warps 0 and 2 TMA producers, warp 1 TMEM allocation + MMA issue,
+// warps 4-11 operand sums then epilogue (as in the one-CTA kernel).
 //
 // Included by strassen_gemm.cu inside namespace sb, after the one-CTA kernel
 // (it uses its constants, GemmParams and store helpers).
 
 namespace pair {
 
-constexpr int kCols = 128;                         // product columns per CTA pair
-constexpr int kATile = kBlockM * 16 * 2;           // 4 KB: 128 x 16 A quadrant tile (32-byte swizzle)
-constexpr int kBTile = 16 * kCols * 2;             // 4 KB: 16 x 128 B quadrant tile (two 64-column chunks)
-constexpr int kBHalf = kBTile / 2;                 // 2 KB: one 64-column chunk
-// Stage layout (byte offsets), the same in both CTAs.
-constexpr int kAOwn = 0;                           // A quadrants (r, 0), (r, 1)
-constexpr int kARecv = 2 * kATile;                 // A quadrant from the peer (CTA 0: a3, CTA 1: a0)
-constexpr int kBOwn = 3 * kATile;                  // B quadrants (0, 1-r), (1, 1-r)
-constexpr int kBRecvF = kBOwn + 2 * kBTile;        // full B tile from the peer (CTA 0: b2, CTA 1: b1)
-constexpr int kBRecvH = kBRecvF + kBTile;          // half B tile from the peer (CTA 0: b0L, CTA 1: b3R)
-constexpr int kBSum = kBRecvH + kBHalf;            // B sum slot (CTA 0: b1-b3, CTA 1: b2-b0)
-constexpr int kStageBytes = kBSum + kBTile;        // 30 KB
-constexpr int kOwnTx = 2 * kATile + 2 * kBTile;    // bytes landed by the CTA's own TMA per step
-constexpr int kRecvTx = kATile + kBTile + kBHalf;  // bytes forwarded by the peer per step
-#ifndef SB_PAIR_STAGES
-#define SB_PAIR_STAGES 7
-#endif
-constexpr int kStages = SB_PAIR_STAGES;
-constexpr int kBarBytes = 512;
-constexpr int kDataBytes = kStages * kStageBytes;
-constexpr int kSmem = kDataBytes + kBarBytes + 1024;  // + alignment slack
-constexpr int kXRowBytes = kCols * 4 + 16;            // exchange row: 128 fp32 + 16 B (bank spread)
+constexpr int kCols = 128;              // product columns per CTA pair
+constexpr int kATile = kBlockM * 16 * 2;  // 4 KB: 128 x 16 A quadrant tile (32-byte swizzle)
+constexpr int kBTile = 16 * kCols * 2;    // 4 KB: 16 x 128 B tile (two 64-column chunks)
+constexpr int kBHalf = kBTile / 2;        // 2 KB: one 64-column chunk
+// Stage layout (byte offsets), the same in both CTAs and both B modes up to
+// the half slot:
+constexpr int kAOwn = 0;                 // A quadrants (r, 0), (r, 1)
+constexpr int kARecv = 2 * kATile;       // the third A quadrant (CTA 0: a3, CTA 1: a0)
+constexpr int kB0 = 3 * kATile;          // three 4 KB B tiles at kB0, kB1, kB2
+constexpr int kB1 = kB0 + kBTile;
+constexpr int kB2 = kB1 + kBTile;
+constexpr int kBH = kB2 + kBTile;        // the 64-column half tile for P1
+constexpr int kBSum = kBH + kBHalf;      // in-kernel B sums only: the sum slot
+// kPreB = false: kB0/kB1 own quadrants (0, 1-r), (1, 1-r); kB2 the other full
+// quadrant; kBH the P1 half.  kPreB = true: kB0..kB2 the operand planes of the
+// CTA's three full products (CTA 0: P3, P5, P7; CTA 1: P2, P4, P6), kBH P1's.
+template <bool kPreB>
+struct Geo {
+  static constexpr int STAGE = kPreB ? kBSum : kBSum + kBTile;  // 26 KB or 30 KB
+  static constexpr int STAGES = kPreB ? 8 : 7;
+  static constexpr int DATA = STAGES * STAGE;
+  static constexpr int BAR_BYTES = 512;
+  static constexpr int SMEM = DATA + BAR_BYTES + 1024;  // + alignment slack
+  static constexpr int TX0 = 2 * kATile + (kPreB ? 3 : 2) * kBTile;    // producer 0 (warp 0)
+  static constexpr int TX1 = kATile + (kPreB ? 0 : kBTile) + kBHalf;   // producer 1 (warp 2)
+  // Barrier slots (8 bytes each) after the stages.
+  static constexpr int FULL = 0, SUMS = STAGES, EMPTY = 2 * STAGES, ACC = 3 * STAGES, XFREE = ACC + 1,
+                       XDATA = ACC + 2, WORDS = ACC + 3;
+  static_assert(STAGE % 1024 == 0, "128-byte swizzle atoms need 1024-byte aligned tiles");
+  static_assert(WORDS * 8 + 16 <= BAR_BYTES, "barrier area");
+  static_assert(SMEM <= 227 * 1024, "shared memory budget");
+};
+static_assert(kB0 % 1024 == 0 && kBH % 1024 == 0 && kBSum % 1024 == 0, "1024-byte aligned B tiles");
+constexpr int kXRowBytes = kCols * 4 + 16;  // exchange row: 128 fp32 + 16 B (bank spread)
+static_assert(kBlockM * kXRowBytes <= Geo<true>::DATA, "exchange buffer fits in the idle stages");
 constexpr uint32_t kIdesc128 = umma_idesc_bf16_f32(kBlockM, 128, false, true);
 constexpr uint32_t kIdesc64 = umma_idesc_bf16_f32(kBlockM, 64, false, true);
 constexpr uint32_t kBLbo = 2048;  // MN-major 128-byte swizzle: offset of the next 64-column chunk
 constexpr uint32_t kBSbo = 1024;  // next 8 k-rows
 constexpr uint32_t kALbo = 16, kASbo = 256;  // K-major 32-byte swizzle rows (LBO unused)
-// Barrier slots (8 bytes each) after the stages.
-constexpr int kBarFull = 0, kBarOwn = kStages, kBarSums = 2 * kStages, kBarEmpty = 3 * kStages,
-              kBarPfree = 4 * kStages, kBarAcc = 5 * kStages, kBarXfree = kBarAcc + 1,
-              kBarXdata = kBarAcc + 2, kBarWords = kBarAcc + 3;
-static_assert(kStageBytes % 1024 == 0 && kBOwn % 1024 == 0 && kBRecvF % 1024 == 0 && kBRecvH % 1024 == 0 &&
-                  kBSum % 1024 == 0,
-              "128-byte swizzle atoms need 1024-byte aligned tiles");
-static_assert(kBarWords * 8 + 16 <= kBarBytes, "barrier area");
-static_assert(kBlockM * kXRowBytes <= kDataBytes, "exchange buffer fits in the idle stages");
-static_assert(kSmem <= 227 * 1024, "shared memory budget");
 static_assert(kRingCol0 + 32 + 24 <= kTmemCols, "two-step ring of three A operands");
+// Operand planes of the B side, in the order the CTAs load them.
+constexpr int kPlaneP3 = 0, kPlaneP5 = 1, kPlaneP7 = 2, kPlaneP1 = 3, kPlaneP2 = 4, kPlaneP4 = 5, kPlaneP6 = 6;
 
 enum : int {
-  kErrPairForward = 5,   // forwarder: own TMA or the peer's stage release never came
   kErrPairExchange = 6,  // epilogue exchange with the peer timed out
 };
 
@@ -111,19 +113,56 @@ __device__ __forceinline__ bool warp_wait_cluster(uint32_t bar, uint32_t parity,
 
 }  // namespace pair
 
-template <bool kOutF32>
+// The seven B operands of every Strassen block, formed once (the reference's
+// B pre-adds, strassen_pallas.py:324-379, each rounded once to bf16):
+//   planes[i][kappa][u] = operand i at product depth kappa = P*bk/2 + k' and
+//   product column u = J*bn/2 + c', in the order P3 (b1-b3), P5 (b3),
+//   P7 (b2+b3), P1 (b0+b3), P2 (b0), P4 (b2-b0), P6 (b0+b1).
+// planes is [7][K/2][N/2] bf16, contiguous.  One thread per 8 columns.
+__global__ void __launch_bounds__(256) b_operand_planes_kernel(const __nv_bfloat16* __restrict__ b, int64_t ldb,
+                                                               int32_t k, int32_t n, int32_t bn, int32_t bk,
+                                                               __nv_bfloat16* __restrict__ planes) {
+  const int64_t kh = k / 2, nh = n / 2, hbn = bn / 2, hbk = bk / 2;
+  const int64_t chunks = kh * (nh / 8);
+  const int64_t plane = kh * nh;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < chunks; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t kappa = i / (nh / 8);
+    const int64_t u = (i - kappa * (nh / 8)) * 8;
+    const int64_t pnl = kappa / hbk, blk = u / hbn;
+    const int64_t row0 = pnl * bk + (kappa - pnl * hbk);
+    const int64_t col0 = blk * bn + (u - blk * hbn);
+    const uint4 b0 = *reinterpret_cast<const uint4*>(b + row0 * ldb + col0);
+    const uint4 b1 = *reinterpret_cast<const uint4*>(b + row0 * ldb + col0 + hbn);
+    const uint4 b2 = *reinterpret_cast<const uint4*>(b + (row0 + hbk) * ldb + col0);
+    const uint4 b3 = *reinterpret_cast<const uint4*>(b + (row0 + hbk) * ldb + col0 + hbn);
+    uint4* out = reinterpret_cast<uint4*>(planes + kappa * nh + u);
+    const int64_t step = plane / 8;  // one plane, in uint4 units
+    out[pair::kPlaneP3 * step] = sub4(b1, b3);
+    out[pair::kPlaneP5 * step] = b3;
+    out[pair::kPlaneP7 * step] = add4(b2, b3);
+    out[pair::kPlaneP1 * step] = add4(b0, b3);
+    out[pair::kPlaneP2 * step] = b0;
+    out[pair::kPlaneP4 * step] = sub4(b2, b0);
+    out[pair::kPlaneP6 * step] = add4(b0, b1);
+  }
+}
+
+template <bool kOutF32, bool kPreB>
 __global__ void __launch_bounds__(kThreads, 1)
-    strassen_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
-                         const GemmParams p) {
+    strassen_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_a1,
+                         const __grid_constant__ CUtensorMap tmap_b, const __grid_constant__ CUtensorMap tmap_b1,
+                         const __grid_constant__ CUtensorMap tmap_bh, const GemmParams p) {
   using namespace pair;
+  using G = Geo<kPreB>;
+  constexpr int kStages = G::STAGES;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_addr = smem_addr(smem_raw);
   uint8_t* smem = smem_raw + ((1024u - (raw_addr & 1023u)) & 1023u);
   const uint32_t smem_base = smem_addr(smem);
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kDataBytes);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + G::DATA);
   const uint32_t bar0 = smem_addr(bars);
   auto bar = [&](int slot) -> uint32_t { return bar0 + 8u * (uint32_t)slot; };
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + kBarWords);
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + G::WORDS);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
 
   const int warp = threadIdx.x >> 5;
@@ -143,121 +182,115 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
-      mbar_init(bar(kBarFull + s), 2);
-      mbar_init(bar(kBarOwn + s), 1);
-      mbar_init(bar(kBarSums + s), 4);
-      mbar_init(bar(kBarEmpty + s), 1);
-      mbar_init(bar(kBarPfree + s), 1);
+      mbar_init(bar(G::FULL + s), 2);
+      mbar_init(bar(G::SUMS + s), 4);
+      mbar_init(bar(G::EMPTY + s), 1);
     }
-    mbar_init(bar(kBarAcc), 1);
-    mbar_init(bar(kBarXfree), kSumWarps);
-    mbar_init(bar(kBarXdata), kSumThreads);
+    mbar_init(bar(G::ACC), 1);
+    mbar_init(bar(G::XFREE), kSumWarps);
+    mbar_init(bar(G::XDATA), kSumThreads);
     *abort_flag = 0;
     fence_mbar_init();
     fence_proxy_async_smem();
   }
-  if (warp == 0 && lane == 0) {
-    tma_prefetch_desc(&tmap_a);
-    tma_prefetch_desc(&tmap_b);
+  if ((warp == 0 || warp == 2) && lane == 0) {
+    tma_prefetch_desc(warp == 0 ? &tmap_a : &tmap_a1);
+    tma_prefetch_desc(warp == 0 ? &tmap_b : &tmap_bh);
   }
   if (warp == 1) tmem_alloc<kTmemCols>(smem_addr(tmem_holder));
   tc_fence_before();
-  // The peer's barriers must be initialised before the first remote arrival
-  // or forwarded byte reaches them.
+  // The peer's barriers must be initialised before its epilogue exchange can
+  // reach them.
   cluster_sync_all();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_holder;
 
   bool ok = true;
-  if (warp == 0) {
-    // ------------------------------------------------------------ TMA producer
+  if (warp == 0 || warp == 2) {
+    // ------------------------------------------------------------ TMA producers
     if (lane == 0) {
+      const bool first = warp == 0;
       int last_armed[kStages];
 #pragma unroll
       for (int s = 0; s < kStages; ++s) last_armed[s] = -1;
       const int a_row_base = t0 % p.half_bm;
       const int a_block = t0 / p.half_bm;
       const int j_block = u0 / p.half_bn;
-      const int b_chunk0 = (j_block * p.bn + (u0 - j_block * p.half_bn)) / 64;
+      const int b_chunk0 = (j_block * p.bn + (u0 - j_block * p.half_bn)) / 64;  // raw-B column chunk
       for (int c = 0; c < p.num_chunks; ++c) {
         const int s = c % kStages;
-        if (!mbar_wait(bar(kBarEmpty + s), ((c / kStages) & 1u) ^ 1u, abort_flag, p.err, kErrWaitEmpty)) break;
-        // Our stage s is free: the peer may forward this phase's tiles into it.
-        mbar_remote_arrive(mapa_shared(bar(kBarPfree + s), peer));
+        if (!mbar_wait(bar(G::EMPTY + s), ((c / kStages) & 1u) ^ 1u, abort_flag, p.err, kErrWaitEmpty)) break;
+        const uint32_t stage = smem_base + s * G::STAGE;
+        const uint32_t fb = bar(G::FULL + s);
         const int kap = c * 16;
         const int panel = kap / p.half_bk;
         const int kcol = panel * p.bk + (kap - panel * p.half_bk);
-        const uint32_t stage = smem_base + s * kStageBytes;
-        mbar_arrive_expect_tx(bar(kBarOwn + s), kOwnTx);
-        tma_load_5d(stage + kAOwn, &tmap_a, bar(kBarOwn + s), kcol, a_row_base, a_block, 0, (int)rank);
-        tma_load_5d(stage + kBOwn, &tmap_b, bar(kBarOwn + s), 0, kcol, b_chunk0, (int)peer, 0);
-        mbar_arrive_expect_tx(bar(kBarFull + s), kRecvTx);
+        if (first) {
+          mbar_arrive_expect_tx(fb, G::TX0);
+          tma_load_5d(stage + kAOwn, &tmap_a, fb, kcol, a_row_base, a_block, 0, (int)rank);
+          if constexpr (kPreB) {
+            tma_load_4d(stage + kB0, &tmap_b, fb, 0, kap, u0 / 64, rank ? kPlaneP2 : kPlaneP3);
+          } else {
+            tma_load_5d(stage + kB0, &tmap_b, fb, 0, kcol, b_chunk0, (int)peer, 0);
+          }
+        } else {
+          mbar_arrive_expect_tx(fb, G::TX1);
+          tma_load_5d(stage + kARecv, &tmap_a1, fb, kcol, a_row_base, a_block, (int)peer, (int)peer);
+          if constexpr (kPreB) {
+            tma_load_4d(stage + kBH, &tmap_bh, fb, 0, kap, u0 / 64 + (int)rank, kPlaneP1);
+          } else {
+            tma_load_5d(stage + kB2, &tmap_b1, fb, 0, kcol, b_chunk0, (int)rank, (int)peer);
+            tma_load_5d(stage + kBH, &tmap_bh, fb, 0, kcol, b_chunk0 + (int)rank, (int)rank, (int)rank);
+          }
+        }
         last_armed[s] = c;
       }
-      // Drain: no TMA write may land after teardown.
+      // Drain: no TMA write may land after teardown (bounded: a phase the
+      // other producer never armed gives up after the wait limit).
 #pragma unroll
       for (int s = 0; s < kStages; ++s)
-        if (last_armed[s] >= 0) mbar_wait_drain(bar(kBarOwn + s), (last_armed[s] / kStages) & 1u);
-      // After a failure, give the peer's forwards into our stages time to land
-      // (a phase we armed and never consumed; bounded).
-      if (*abort_flag) {
-#pragma unroll
-        for (int s = 0; s < kStages; ++s)
-          if (last_armed[s] >= 0) mbar_wait_drain(bar(kBarFull + s), (last_armed[s] / kStages) & 1u);
-      }
+        if (last_armed[s] >= 0) mbar_wait_drain(bar(G::FULL + s), (last_armed[s] / kStages) & 1u);
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
       const uint64_t a_d0 = umma_smem_desc(smem_base, kALbo, kASbo, kLayoutSwizzle32B);
       const uint64_t b_d0 = umma_smem_desc(smem_base, kBLbo, kBSbo, kLayoutSwizzle128B);
-      // Per rank: accumulator 0 and 1 -- one from the A ring, one with A in
-      // shared memory (CTA 0: P3 ss, P5 ts; CTA 1: P2 ts, P4 ss).
-      const uint64_t ss_a = (uint64_t)((kAOwn + (rank ? kATile : 0)) >> 4);    // a0 or a3
-      const uint64_t ss_b = (uint64_t)(kBSum >> 4);
-      const uint64_t ts_b = (uint64_t)((kBOwn + (rank ? 0 : kBTile)) >> 4);     // b3 or b0
+      // Accumulators 0 and 1: one with A in shared memory, one from the A ring
+      // (CTA 0: M3 = a0 x B0 ss, M5 = ring0 x B1; CTA 1: M2 = ring0 x B0,
+      // M4 = a3 x B1 ss).  B tile of each accumulator per mode (see Geo).
+      const uint64_t ss_a = (uint64_t)((kAOwn + (rank ? kATile : 0)) >> 4);  // a0 or a3
+      int ss_bo, ts_bo;
+      if (kPreB) {
+        ss_bo = rank ? kB1 : kB0;
+        ts_bo = rank ? kB0 : kB1;
+      } else {
+        ss_bo = kBSum;               // b1-b3 or b2-b0
+        ts_bo = rank ? kB0 : kB1;    // b0 (own quadrant 0 of CTA 1) or b3 (own quadrant 1 of CTA 0)
+      }
+      const uint64_t ss_b = (uint64_t)(ss_bo >> 4), ts_b = (uint64_t)(ts_bo >> 4);
       const uint32_t ss_d = tmem_base + (rank ? 128u : 0u);
       const uint32_t ts_d = tmem_base + (rank ? 0u : 128u);
       int s = 0;
       uint32_t ph = 0;
       for (int c = 0; c < p.num_chunks; ++c) {
-        if (!mbar_wait(bar(kBarSums + s), ph, abort_flag, p.err, kErrWaitSums)) break;
+        if (!mbar_wait(bar(G::SUMS + s), ph, abort_flag, p.err, kErrWaitSums)) break;
         tc_fence_after();
-        const uint64_t so = (uint64_t)((s * kStageBytes) >> 4);
+        const uint64_t so = (uint64_t)((s * G::STAGE) >> 4);
         const uint32_t acc = c != 0 ? 1u : 0u;
         const uint32_t ring = tmem_base + kRingCol0 + 32u * (uint32_t)(c & 1);
         umma_bf16_ss(ss_d, a_d0 + so + ss_a, b_d0 + so + ss_b, kIdesc128, acc);
         umma_bf16_ts(ts_d, ring + 0, b_d0 + so + ts_b, kIdesc128, acc);
-        umma_bf16_ts(tmem_base + 256, ring + 8, b_d0 + so + (uint64_t)(kBRecvF >> 4), kIdesc128, acc);
-        umma_bf16_ts(tmem_base + 384, ring + 16, b_d0 + so + (uint64_t)(kBRecvH >> 4), kIdesc64, acc);
-        umma_commit(bar(kBarEmpty + s));
+        umma_bf16_ts(tmem_base + 256, ring + 8, b_d0 + so + (uint64_t)(kB2 >> 4), kIdesc128, acc);
+        umma_bf16_ts(tmem_base + 384, ring + 16, b_d0 + so + (uint64_t)(kBH >> 4), kIdesc64, acc);
+        umma_commit(bar(G::EMPTY + s));
         if (++s == kStages) {
           s = 0;
           ph ^= 1u;
         }
       }
       // Always commit: the epilogue (or the teardown drain) waits on it.
-      umma_commit(bar(kBarAcc));
-    }
-  } else if (warp == 2) {
-    // ------------------------------------------------------------ forwarder
-    if (lane == 0) {
-      const uint32_t a_src = kAOwn + (rank ? kATile : 0);                 // CTA 0: a0, CTA 1: a3
-      const uint32_t f_src = kBOwn + (rank ? kBTile : 0);                 // CTA 0: b1, CTA 1: b2
-      const uint32_t h_src = kBOwn + (rank ? 0 : kBTile + kBHalf);        // CTA 0: b3R, CTA 1: b0L
-      for (int c = 0; c < p.num_chunks; ++c) {
-        const int s = c % kStages;
-        const uint32_t ph = (c / kStages) & 1u;
-        if (!mbar_wait(bar(kBarOwn + s), ph, abort_flag, p.err, kErrPairForward)) break;
-        if (!mbar_wait_cluster(bar(kBarPfree + s), ph, abort_flag, p.err, kErrPairForward)) break;
-        const uint32_t so = (uint32_t)(s * kStageBytes);
-        const uint32_t peer_full = mapa_shared(bar(kBarFull + s), peer);
-        const uint32_t local = smem_base + so;
-        bulk_copy_to_peer(mapa_shared(local + kARecv, peer), local + a_src, kATile, peer_full);
-        bulk_copy_to_peer(mapa_shared(local + kBRecvF, peer), local + f_src, kBTile, peer_full);
-        bulk_copy_to_peer(mapa_shared(local + kBRecvH, peer), local + h_src, kBHalf, peer_full);
-        mbar_arrive(bar(kBarFull + s));  // our own half of stage s has landed
-      }
+      umma_commit(bar(G::ACC));
     }
   } else if (warp >= kFirstSumWarp) {
     // ------------------------------------------------------------ operand sums
@@ -272,12 +305,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int c = set; c < p.num_chunks; c += 2) {
       const int s = c % kStages;
       if (!__all_sync(0xffffffffu,
-                      mbar_wait(bar(kBarFull + s), (c / kStages) & 1u, abort_flag, p.err, kErrWaitRaw))) {
+                      mbar_wait(bar(G::FULL + s), (c / kStages) & 1u, abort_flag, p.err, kErrWaitRaw))) {
         ok = false;
         break;
       }
-      const uint32_t st = smem_base + s * kStageBytes;
-      // A: x0, x1 own (quadrants (r,0), (r,1)), x2 received.
+      const uint32_t st = smem_base + s * G::STAGE;
+      // A: x0, x1 = quadrants (r, 0), (r, 1); x2 = the third quadrant.
       const uint4 x0l = lds128(st + kAOwn + lo_off), x0h = lds128(st + kAOwn + hi_off);
       const uint4 x1l = lds128(st + kAOwn + kATile + lo_off), x1h = lds128(st + kAOwn + kATile + hi_off);
       const uint4 x2l = lds128(st + kARecv + lo_off), x2h = lds128(st + kARecv + hi_off);
@@ -291,29 +324,30 @@ __global__ void __launch_bounds__(kThreads, 1)
         r1l = sub4(x0l, x2l); r1h = sub4(x0h, x2h);  // a2-a0
         r2l = add4(x1l, x2l); r2h = add4(x1h, x2h);  // a3+a0
       }
-      // B: d = own quadrant (0, 1-r), e = own (1, 1-r), f = received full, h = received half.
-      const uint32_t bo = st + kBOwn;
-      const uint4 d1 = lds128(bo + o1), d2 = lds128(bo + o2);
-      const uint4 e1 = lds128(bo + kBTile + o1), e2 = lds128(bo + kBTile + o2);
-      const uint4 f1 = lds128(st + kBRecvF + o1), f2 = lds128(st + kBRecvF + o2);
-      const uint4 h1 = lds128(st + kBRecvH + o1);
-      if (rank == 0) {
-        sts128(st + kBSum + o1, sub4(d1, e1));    // b1 - b3
-        sts128(st + kBSum + o2, sub4(d2, e2));
-        sts128(st + kBRecvF + o1, add4(f1, e1));  // b2 + b3
-        sts128(st + kBRecvF + o2, add4(f2, e2));
-        sts128(st + kBRecvH + o1, add4(h1, e1));  // (b0 + b3) left chunk
-      } else {
-        sts128(st + kBSum + o1, sub4(e1, d1));    // b2 - b0
-        sts128(st + kBSum + o2, sub4(e2, d2));
-        sts128(st + kBRecvF + o1, add4(d1, f1));  // b0 + b1
-        sts128(st + kBRecvF + o2, add4(d2, f2));
-        sts128(st + kBRecvH + o1, add4(d2, h1));  // (b0 + b3) right chunk
+      if constexpr (!kPreB) {
+        // B: d, e = own quadrants (0, 1-r), (1, 1-r); f = the other full quadrant, h = P1's half.
+        const uint4 d1 = lds128(st + kB0 + o1), d2 = lds128(st + kB0 + o2);
+        const uint4 e1 = lds128(st + kB1 + o1), e2 = lds128(st + kB1 + o2);
+        const uint4 f1 = lds128(st + kB2 + o1), f2 = lds128(st + kB2 + o2);
+        const uint4 h1 = lds128(st + kBH + o1);
+        if (rank == 0) {
+          sts128(st + kBSum + o1, sub4(d1, e1));  // b1 - b3
+          sts128(st + kBSum + o2, sub4(d2, e2));
+          sts128(st + kB2 + o1, add4(f1, e1));    // b2 + b3
+          sts128(st + kB2 + o2, add4(f2, e2));
+          sts128(st + kBH + o1, add4(h1, e1));    // (b0 + b3) left chunk
+        } else {
+          sts128(st + kBSum + o1, sub4(e1, d1));  // b2 - b0
+          sts128(st + kBSum + o2, sub4(e2, d2));
+          sts128(st + kB2 + o1, add4(d1, f1));    // b0 + b1
+          sts128(st + kB2 + o2, add4(d2, f2));
+          sts128(st + kBH + o1, add4(d2, h1));    // (b0 + b3) right chunk
+        }
+        fence_proxy_async_smem();
       }
-      fence_proxy_async_smem();
       // Ring half c & 1 is free once the MMAs of step c - 2 completed.
       if (c >= 2) {
-        const bool waited = mbar_wait(bar(kBarEmpty + (c - 2) % kStages), ((c - 2) / kStages) & 1u, abort_flag,
+        const bool waited = mbar_wait(bar(G::EMPTY + (c - 2) % kStages), ((c - 2) / kStages) & 1u, abort_flag,
                                       p.err, kErrWaitEmpty);
         if (!__all_sync(0xffffffffu, waited)) {
           ok = false;
@@ -328,19 +362,20 @@ __global__ void __launch_bounds__(kThreads, 1)
       tmem_store_wait();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(bar(kBarSums + s));
+      if (lane == 0) mbar_arrive(bar(G::SUMS + s));
     }
 
     // ------------------------------------------------------------ epilogue
-    if (ok && warp_wait(bar(kBarAcc), 0, abort_flag, p.err, kErrWaitAcc)) {
+    if (ok && warp_wait(bar(G::ACC), 0, abort_flag, p.err, kErrWaitAcc)) {
       tc_fence_after();
-      // Our stages are idle now: let the peer write its partial into them.
-      if (lane == 0) mbar_remote_arrive(mapa_shared(bar(kBarXfree), peer));
+      // Our stages are idle now (every MMA retired, every copy consumed): let
+      // the peer write its partial into them.
+      if (lane == 0) mbar_remote_arrive(mapa_shared(bar(G::XFREE), peer));
       const int h = set;                        // columns [64h, 64h + 64) of the product tile
       const bool mine = (uint32_t)h == rank;    // this half holds our 64 columns of P1
       const uint32_t tmem_row = tmem_base + ((uint32_t)(32 * q) << 16);
       const uint32_t xrow = smem_base + row * kXRowBytes;
-      if (warp_wait_cluster(bar(kBarXfree), 0, abort_flag, p.err, kErrPairExchange)) {
+      if (warp_wait_cluster(bar(G::XFREE), 0, abort_flag, p.err, kErrPairExchange)) {
 #pragma unroll 1
         for (int j = 0; j < 8; ++j) {
           const int col = 64 * h + 8 * j;
@@ -354,8 +389,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           st_cluster_f32x4(mapa_shared(xrow + col * 4, peer), y[0], y[1], y[2], y[3]);
           st_cluster_f32x4(mapa_shared(xrow + col * 4 + 16, peer), y[4], y[5], y[6], y[7]);
         }
-        mbar_remote_arrive(mapa_shared(bar(kBarXdata), peer));
-        if (warp_wait_cluster(bar(kBarXdata), 0, abort_flag, p.err, kErrPairExchange)) {
+        mbar_remote_arrive(mapa_shared(bar(G::XDATA), peer));
+        if (warp_wait_cluster(bar(G::XDATA), 0, abort_flag, p.err, kErrPairExchange)) {
           const int t = t0 + (int)row;
           const bool row_ok = t < p.Mp;
           const int blk_i = t / p.half_bm;
@@ -401,7 +436,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   cluster_sync_all();
   if (warp == 1) {
     tc_fence_after();
-    if (lane == 0) mbar_wait_drain(bar(kBarAcc), 0);  // every issued MMA has retired
+    if (lane == 0) mbar_wait_drain(bar(G::ACC), 0);  // every issued MMA has retired
     __syncwarp();
     tmem_dealloc<kTmemCols>(tmem_base);
   }

@@ -536,38 +536,83 @@ def classical_matmul(a, b, *, bm=TUNED_BM, bn=TUNED_BN, bk=TUNED_BK, output_dtyp
     return out
 
 
-def pair_matmul(a, b, *, bm=TUNED_BM, bn=TUNED_BN, bk=TUNED_BK, output_dtype=None, out=None):
+def strassen_b_operands(b, *, bn=TUNED_BN, bk=TUNED_BK, out=None):
+    """The seven B operands of every Strassen block of ``b`` for the tile (bn, bk).
+
+    Returns ``[7, K/2, N/2]`` bf16 planes in the order P3 (b1-b3), P5 (b3),
+    P7 (b2+b3), P1 (b0+b3), P2 (b0), P4 (b2-b0), P6 (b0+b1): the reference's B
+    pre-adds (strassen_pallas.py:324-379), each rounded once to bf16.  Pass them
+    to :func:`pair_matmul` as ``b_operands=`` with the same ``bn`` and ``bk``.
+    For a weight reused across calls this is an offline relayout, like
+    :func:`swiglu_weight_layout`.
+    """
+    if b.ndim != 2 or b.dtype != torch.bfloat16:
+        raise ValueError("strassen_b_operands expects a rank-2 BF16 matrix")
+    if b.device.type != "cuda":
+        raise ValueError("strassen_b_operands runs on a CUDA device (no CPU fallback)")
+    k, n = b.shape
+    b = _rowmajor(b)
+    shape = (7, k // 2, n // 2)
+    if out is None:
+        out = torch.empty(shape, dtype=torch.bfloat16, device=b.device)
+    elif tuple(out.shape) != shape or out.dtype != torch.bfloat16 or not out.is_contiguous():
+        raise ValueError(f"out must be a contiguous bf16 tensor of shape {shape}")
+    lib = _native.load()
+    with torch.cuda.device(b.device):
+        status = lib.sb_strassen_b_operands(_stream_handle(b.device), b.data_ptr(), out.data_ptr(), k, n,
+                                            _ld(b), bn, bk)
+    _native.check(status)
+    return out
+
+
+def pair_matmul(a, b, *, bm=TUNED_BM, bn=TUNED_BN, bk=TUNED_BK, output_dtype=None, out=None,
+                b_operands=None):
     """``strassen_matmul(a, b, bm=, bn=, bk=, output_dtype=)`` without an epilogue,
     on the two-CTA kernel (``sb_strassen_gemm_pair``): a cluster of two CTAs per
-    128 x 128 product tile, 3.5 of the seven products each, operand quadrants
-    shared through distributed shared memory.  Same algorithm and operand
-    pairing as strassen_pallas.py:156-880; the recombination's fp32 order
-    differs from :func:`strassen_matmul`.
+    128 x 128 product tile, 3.5 of the seven products each.  Same algorithm and
+    operand pairing as strassen_pallas.py:156-880; the recombination's fp32
+    order differs from :func:`strassen_matmul`.
+
+    ``b_operands``: B's operand planes from :func:`strassen_b_operands` (built
+    with the same bn, bk); then ``b`` may be None and the kernel forms no B sums
+    (``sb_strassen_gemm_pair_planes``; bit-identical to the raw-B call).
     """
-    if a.ndim != 2 or b.ndim != 2:
+    if b_operands is not None:
+        if b_operands.ndim != 3 or b_operands.shape[0] != 7 or b_operands.dtype != torch.bfloat16 \
+                or not b_operands.is_contiguous():
+            raise ValueError("b_operands must be the contiguous [7, K/2, N/2] bf16 planes of strassen_b_operands")
+        kb, nb = 2 * b_operands.shape[1], 2 * b_operands.shape[2]
+        if b is not None and tuple(b.shape) != (kb, nb):
+            raise ValueError(f"b_operands describe a {kb}x{nb} B, b is {tuple(b.shape)}")
+    if a.ndim != 2 or (b is not None and b.ndim != 2):
         raise ValueError("pair_matmul expects two rank-2 matrices")
     m, k = a.shape
-    k2, n = b.shape
+    k2, n = (kb, nb) if b_operands is not None else b.shape
     if k != k2:
         raise ValueError(f"inner dimensions disagree: {k} vs {k2}")
-    if a.dtype != torch.bfloat16 or b.dtype != torch.bfloat16:
+    if a.dtype != torch.bfloat16 or (b is not None and b.dtype != torch.bfloat16):
         raise ValueError("inputs must be BF16")
     for name, dimension, block in (("M", m, bm), ("N", n, bn), ("K", k, bk)):
         if dimension % block:
             raise ValueError(f"{name}={dimension} is not divisible by {block}")
     check_tiling(bm, bn, bk)
-    if a.device.type != "cuda" or b.device.type != "cuda":
+    if a.device.type != "cuda" or (b is not None and b.device.type != "cuda"):
         raise ValueError("pair_matmul runs on a CUDA device (no CPU fallback)")
     out_dt = _as_torch_dtype(output_dtype) or torch.bfloat16
     device = a.device
-    a, b = _rowmajor(a), _rowmajor(b)
+    a = _rowmajor(a)
     if out is None:
         out = torch.empty((m, n), dtype=out_dt, device=device)
     lib = _native.load()
+    od = SB_F32 if out_dt == torch.float32 else SB_BF16
     with torch.cuda.device(device):
-        status = lib.sb_strassen_gemm_pair(_stream_handle(device), a.data_ptr(), b.data_ptr(),
-                                           out.data_ptr(), m, n, k, _ld(a), _ld(b), _ld(out),
-                                           bm, bn, bk, SB_F32 if out_dt == torch.float32 else SB_BF16)
+        if b_operands is not None:
+            status = lib.sb_strassen_gemm_pair_planes(_stream_handle(device), a.data_ptr(), b_operands.data_ptr(),
+                                                      out.data_ptr(), m, n, k, _ld(a), _ld(out), bm, bn, bk, od)
+        else:
+            b = _rowmajor(b)
+            status = lib.sb_strassen_gemm_pair(_stream_handle(device), a.data_ptr(), b.data_ptr(),
+                                               out.data_ptr(), m, n, k, _ld(a), _ld(b), _ld(out), bm, bn, bk, od)
     _native.check(status)
     return out
 

@@ -1,12 +1,14 @@
-"""Parity of the two-CTA Strassen kernel (``sb_strassen_gemm_pair``, needs a B200).
+"""Parity of the two-CTA Strassen kernel (``sb_strassen_gemm_pair`` and
+``sb_strassen_gemm_pair_planes``, needs a B200).
 
 The kernel computes the same products as ``sb_strassen_gemm`` (the reference's
 strassen_pallas.py:156-880 without an epilogue) with the seven products split
-over a cluster of two CTAs and the operand quadrants shared through distributed
-shared memory.  Bar: the parity rule of test_gpu_parity.assert_parity against
-the reference's own golden vectors, bit-exact integer and constant known
-answers, and agreement with the one-CTA kernel to fp32 rounding (the two
-recombine the products in a different fp32 order).
+over a cluster of two CTAs.  "raw" forms the B operand sums in the kernel;
+"planes" reads them from ``strassen_b_operands``.  Bar: the parity rule of
+test_gpu_parity.assert_parity against the reference's own golden vectors,
+bit-exact integer and constant known answers, bit-exact agreement between the
+two B modes, and agreement with the one-CTA kernel to fp32 rounding (the two
+kernels recombine the products in a different fp32 order).
 """
 
 from __future__ import annotations
@@ -31,16 +33,28 @@ PLAIN = [c for c in GOLDEN_CASES if c in {
     "normal_256x512x768_f32", "normal_512x512x512_tile512", "sentinel_256x512x256"}]
 
 
-@pytest.mark.parametrize("case", PLAIN)
-def test_pair_golden_case(golden, case):
+MODES = ["raw", "planes"]
+
+
+def pair(a, b, mode, **kw):
+    """pair_matmul on device tensors, with B raw or as its operand planes."""
     import strassen_tpu_b200 as sb
+    if mode == "planes":
+        planes = sb.strassen_b_operands(b, bn=kw["bn"], bk=kw["bk"])
+        return sb.pair_matmul(a, None, b_operands=planes, **kw)
+    return sb.pair_matmul(a, b, **kw)
+
+
+@pytest.mark.parametrize("mode", MODES)
+@pytest.mark.parametrize("case", PLAIN)
+def test_pair_golden_case(golden, case, mode):
     manifest, arrays = golden
     p = manifest[case]
     a, b, extra = make_inputs(p)
     assert not extra
     od = p["kwargs"].get("output_dtype")
-    out = sb.pair_matmul(dev_bf16(a), dev_bf16(b), bm=p["bm"], bn=p["bn"], bk=p["bk"],
-                         output_dtype=torch.float32 if od == "float32" else None)
+    out = pair(dev_bf16(a), dev_bf16(b), mode, bm=p["bm"], bn=p["bn"], bk=p["bk"],
+               output_dtype=torch.float32 if od == "float32" else None)
     torch.cuda.synchronize()
     got = host(out)
     assert list(got.shape) == p["shape"]
@@ -60,13 +74,13 @@ def test_pair_golden_case(golden, case):
     ((384, 768, 1024), (128, 512, 256)),    # 64-row blocks, two column tiles per block
     ((2048, 1024, 768), (1024, 256, 512)),  # large blocks, several row tiles per block
 ])
-def test_pair_exact_integer_products(shape, tile):
-    import strassen_tpu_b200 as sb
+@pytest.mark.parametrize("mode", MODES)
+def test_pair_exact_integer_products(shape, tile, mode):
     m, k, n = shape
     a = ref.integers_bf16((m, k), -2, 2, 11)
     b = ref.integers_bf16((k, n), -2, 2, 12)
-    got = host(sb.pair_matmul(dev_bf16(a), dev_bf16(b), bm=tile[0], bn=tile[1], bk=tile[2],
-                              output_dtype=torch.float32))
+    got = host(pair(dev_bf16(a), dev_bf16(b), mode, bm=tile[0], bn=tile[1], bk=tile[2],
+                    output_dtype=torch.float32))
     np.testing.assert_array_equal(got, a @ b)
 
 
@@ -85,6 +99,9 @@ def test_pair_matches_one_cta_kernel(m, n, k):
     assert (two - one).abs().max().item() <= 1e-4 * rms
     bf = sb.pair_matmul(a, b, **tile)
     assert torch.equal(bf, two.to(torch.bfloat16))
+    # The planes carry exactly the operand values the in-kernel sums form.
+    planes = sb.strassen_b_operands(b, bn=tile["bn"], bk=tile["bk"])
+    assert torch.equal(sb.pair_matmul(a, None, b_operands=planes, output_dtype=torch.float32, **tile), two)
     from strassen_tpu_b200 import _native
     assert _native.device_status() == 0
 
@@ -105,3 +122,30 @@ def test_pair_validation_matches_the_reference_messages():
         sb.pair_matmul(a, a, bm=256, bn=512, bk=256)
     with pytest.raises(ValueError, match="multiple of 256"):
         sb.pair_matmul(a, a, bm=256, bn=128, bk=256)
+
+
+def test_b_operand_planes_are_the_reference_pre_adds():
+    """Plane i at (kappa, u) is operand i of block (kappa // (bk/2), u // (bn/2)),
+    each sum rounded once to bf16 (strassen_pallas.py:324-379)."""
+    import strassen_tpu_b200 as sb
+    k, n, bn, bk = 1024, 1536, 512, 512
+    b = ref.normal_bf16((k, n), 31)
+    got = sb.strassen_b_operands(dev_bf16(b), bn=bn, bk=bk).float().cpu().numpy()
+    hbn, hbk = bn // 2, bk // 2
+    blocks = b.reshape(k // bk, 2, hbk, n // bn, 2, hbn)  # [P, qk, k', J, qc, c']
+    q = lambda qk, qc: blocks[:, qk, :, :, qc, :].reshape(k // 2, n // 2)
+    b0, b1, b2, b3 = q(0, 0), q(0, 1), q(1, 0), q(1, 1)
+    r = ref.bf16_round
+    want = np.stack([r(b1 - b3), b3, r(b2 + b3), r(b0 + b3), b0, r(b2 - b0), r(b0 + b1)])
+    np.testing.assert_array_equal(got, want)
+
+
+def test_b_operand_planes_validation():
+    import strassen_tpu_b200 as sb
+    b = torch.zeros(512, 512, dtype=torch.bfloat16, device="cuda")
+    with pytest.raises(ValueError, match="divisible"):
+        sb.strassen_b_operands(b, bn=1024, bk=256)
+    planes = sb.strassen_b_operands(b, bn=256, bk=256)
+    a = torch.zeros(256, 256, dtype=torch.bfloat16, device="cuda")
+    with pytest.raises(ValueError, match="inner dimensions"):
+        sb.pair_matmul(a, None, b_operands=planes, bm=256, bn=256, bk=256)
