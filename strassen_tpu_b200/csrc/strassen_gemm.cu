@@ -1273,21 +1273,34 @@ int dispatch(bool strassen, int epi, bool out_f32, cudaStream_t stream, const CU
   }
 }
 
+// Device address of g_device_error per device, resolved by check_device().
+int* g_error_word_addr[64];
+
+// Checks that the current device is an sm_100 part and, once per device with
+// that device current, resolves the address of the bounded-wait error word the
+// kernels write to (base_params hands it to every launch).
 int check_device() {
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return fail(SB_ERR_CUDA, std::string("cudaGetDevice: ") + cudaGetErrorString(e));
   static int cached_major[64];
   static int cached_minor[64];
+  static cudaError_t symbol_err[64];
   static std::once_flag flags[64];
   if (dev < 0 || dev >= 64) return fail(SB_ERR_DEVICE, "device ordinal out of range");
   std::call_once(flags[dev], [&]() {
     cudaDeviceGetAttribute(&cached_major[dev], cudaDevAttrComputeCapabilityMajor, dev);
     cudaDeviceGetAttribute(&cached_minor[dev], cudaDevAttrComputeCapabilityMinor, dev);
+    void* addr = nullptr;
+    symbol_err[dev] = cudaGetSymbolAddress(&addr, g_device_error);
+    g_error_word_addr[dev] = symbol_err[dev] == cudaSuccess ? static_cast<int*>(addr) : nullptr;
   });
   if (cached_major[dev] != 10 || cached_minor[dev] != 0)
     return fail(SB_ERR_DEVICE, "the Strassen kernel is built for sm_100a (B200); device is sm_" +
                                    std::to_string(cached_major[dev]) + std::to_string(cached_minor[dev]));
+  if (g_error_word_addr[dev] == nullptr)
+    return fail(SB_ERR_CUDA, std::string("cudaGetSymbolAddress(device error word): ") +
+                                 cudaGetErrorString(symbol_err[dev]));
   return SB_OK;
 }
 
@@ -1438,9 +1451,10 @@ GemmParams base_params(int64_t m, int64_t n, int64_t k, int32_t bm, int32_t bn, 
   p.eps = 1e-6f;
   p.half_head = 64;
   p.inv_head_dim = 1.0f / 128.0f;
-  int* err = nullptr;
-  cudaGetSymbolAddress(reinterpret_cast<void**>(&err), g_device_error);
-  p.err = err;
+  // check_device() has resolved the error word of the current device.
+  int dev = 0;
+  cudaGetDevice(&dev);
+  p.err = (dev >= 0 && dev < 64) ? g_error_word_addr[dev] : nullptr;
   return p;
 }
 
