@@ -143,3 +143,42 @@ def test_streamed_validates_before_touching_the_device():
         sb.strassen_matmul_streamed(a, b.t(), bm=1024, bn=1024, bk=512)
     with pytest.raises(ValueError, match="is not divisible by"):
         sb.strassen_matmul_streamed(a[:1536], b, bm=1024, bn=1024, bk=512)
+
+
+# --- the two-CTA kernel's host API (pair_matmul, strassen_b_operands) ---------
+
+@pytest.mark.parametrize("kw, match", [
+    (dict(a=torch.zeros(2, 2, 2, dtype=BF)), "two rank-2 matrices"),
+    (dict(a=torch.zeros(256, 512, dtype=BF)), "inner dimensions disagree: 512 vs 256"),
+    (dict(a=torch.zeros(256, 256, dtype=torch.float32)), "inputs must be BF16"),
+    (dict(bm=48), "M=256 is not divisible by 48"),
+    (dict(bn=128), "bn=128 must be a multiple of 256"),
+    (dict(), "runs on a CUDA device"),  # valid arguments, but CPU tensors: no CPU fallback
+])
+def test_pair_matmul_value_errors(kw, match):
+    a = kw.pop("a", torch.zeros(256, 256, dtype=BF))
+    b = torch.zeros(256, 256, dtype=BF)
+    kw.setdefault("bm", 256)
+    kw.setdefault("bn", 256)
+    kw.setdefault("bk", 256)
+    with pytest.raises(ValueError, match=match):
+        sb.pair_matmul(a, b, **kw)
+
+
+def test_pair_matmul_checks_the_operand_planes():
+    a = torch.zeros(256, 512, dtype=BF)
+    with pytest.raises(ValueError, match=r"\[7, K/2, N/2\] bf16 planes"):
+        sb.pair_matmul(a, None, b_operands=torch.zeros(6, 256, 128, dtype=BF), bm=256, bn=256, bk=256)
+    with pytest.raises(ValueError, match="describe a 512x256 B, b is"):
+        sb.pair_matmul(a, torch.zeros(512, 512, dtype=BF), b_operands=torch.zeros(7, 256, 128, dtype=BF),
+                       bm=256, bn=256, bk=256)
+    # Planes of a 512x256 B: shapes agree, so only the device check is left.
+    with pytest.raises(ValueError, match="runs on a CUDA device"):
+        sb.pair_matmul(a, None, b_operands=torch.zeros(7, 256, 128, dtype=BF), bm=256, bn=256, bk=256)
+
+
+def test_strassen_b_operands_refuses_host_tensors_and_other_dtypes():
+    with pytest.raises(ValueError, match="rank-2 BF16"):
+        sb.strassen_b_operands(torch.zeros(512, 512, dtype=torch.float32), bn=256, bk=256)
+    with pytest.raises(ValueError, match="CUDA device"):
+        sb.strassen_b_operands(torch.zeros(512, 512, dtype=BF), bn=256, bk=256)
