@@ -1458,11 +1458,13 @@ GemmParams base_params(int64_t m, int64_t n, int64_t k, int32_t bm, int32_t bn, 
   return p;
 }
 
-// Tensor maps of the two-CTA kernel (strassen_pair.cuh).  Both B modes share
-// the two A maps:
+// Tensor maps of the two-CTA kernel (strassen_pair.cuh); KD = the stage depth
+// of the mode (16 for raw B, pair::Geo<true>::KD for the planes).  Both B
+// modes share the two A maps:
 //   a:  dims (k, row in half-block, block, qk, qr) as make_ts_maps; box
-//       {16, rows, blocks, 2, 1} -> quadrants (r, 0), (r, 1) at qr = r;
-//   a1: the same dims, box {16, rows, blocks, 1, 1} -> one quadrant.
+//       {KD, rows, blocks, 2, 1} -> quadrants (r, 0), (r, 1) at qr = r
+//       (KD = 16: 32-byte rows, 32-byte swizzle; KD = 32: 64-byte rows and swizzle);
+//   a1: the same dims, box {KD, rows, blocks, 1, 1} -> one quadrant.
 // Raw B (b_planes == nullptr): dims (column in a 64-column chunk, k, chunk,
 // qc, qk), strides (1, ldb, 64, half_bn, half_bk*ldb) elements;
 //   b:  box {64, 16, 2, 1, 2} -> quadrants (0, qc), (1, qc), 16 x 128 each;
@@ -1470,7 +1472,7 @@ GemmParams base_params(int64_t m, int64_t n, int64_t k, int32_t bm, int32_t bn, 
 //   bh: box {64, 16, 1, 1, 1} -> one 64-column chunk of a quadrant.
 // B operand planes ([7][K/2][N/2], from b_operand_planes_kernel): dims
 // (column in a chunk, kappa, chunk, plane);
-//   b:  box {64, 16, 2, 3} -> three planes of 16 x 128;  bh: box {64, 16, 1, 1}.
+//   b:  box {64, KD, 2, 3} -> three planes of KD x 128;  bh: box {64, KD, 1, 1}.
 struct PairMaps {
   CUtensorMap a, a1, b, b1, bh;
 };
@@ -1483,6 +1485,8 @@ int make_pair_maps(const void* a, const void* b, const void* b_planes, int64_t m
   const uint32_t rows = half_bm >= kBlockM ? kBlockM : (uint32_t)half_bm;
   const uint32_t blocks = half_bm >= kBlockM ? 1 : (uint32_t)(kBlockM / half_bm);
   cuuint32_t estr[5] = {1, 1, 1, 1, 1};
+  const uint32_t kd = b_planes ? (uint32_t)pair::Geo<true>::KD : 16u;
+  const CUtensorMapSwizzle a_sw = kd == 32 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_32B;
   auto encode = [&](CUtensorMap* map, const void* base, cuuint32_t rank, const cuuint64_t* dims,
                     const cuuint64_t* strides, const cuuint32_t* box, CUtensorMapSwizzle sw,
                     const char* what) -> int {
@@ -1497,11 +1501,11 @@ int make_pair_maps(const void* a, const void* b, const void* b_planes, int64_t m
     cuuint64_t dims[5] = {(cuuint64_t)k, (cuuint64_t)half_bm, (cuuint64_t)(m / bm), 2, 2};
     cuuint64_t strides[4] = {(cuuint64_t)(lda * 2), (cuuint64_t)(bm * lda * 2), (cuuint64_t)(half_bk * 2),
                              (cuuint64_t)(half_bm * lda * 2)};
-    cuuint32_t box[5] = {16, rows, blocks, 2, 1};
-    int st = encode(&maps->a, a, 5, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_32B, "A, pair");
+    cuuint32_t box[5] = {kd, rows, blocks, 2, 1};
+    int st = encode(&maps->a, a, 5, dims, strides, box, a_sw, "A, pair");
     if (st != SB_OK) return st;
     box[3] = 1;
-    st = encode(&maps->a1, a, 5, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_32B, "A, one quadrant");
+    st = encode(&maps->a1, a, 5, dims, strides, box, a_sw, "A, one quadrant");
     if (st != SB_OK) return st;
   }
   if (b_planes == nullptr) {
@@ -1519,7 +1523,7 @@ int make_pair_maps(const void* a, const void* b, const void* b_planes, int64_t m
   const int64_t kh = k / 2, nh = n / 2;
   cuuint64_t dims[4] = {64, (cuuint64_t)kh, (cuuint64_t)(nh / 64), 7};
   cuuint64_t strides[3] = {(cuuint64_t)(nh * 2), 128, (cuuint64_t)(kh * nh * 2)};
-  cuuint32_t box[4] = {64, 16, 2, 3};
+  cuuint32_t box[4] = {64, kd, 2, 3};
   int st = encode(&maps->b, b_planes, 4, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B, "B planes");
   if (st != SB_OK) return st;
   box[2] = 1;

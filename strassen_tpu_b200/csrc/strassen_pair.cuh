@@ -56,46 +56,60 @@
 
 namespace pair {
 
-constexpr int kCols = 128;              // product columns per CTA pair
-constexpr int kATile = kBlockM * 16 * 2;  // 4 KB: 128 x 16 A quadrant tile (32-byte swizzle)
-constexpr int kBTile = 16 * kCols * 2;    // 4 KB: 16 x 128 B tile (two 64-column chunks)
-constexpr int kBHalf = kBTile / 2;        // 2 KB: one 64-column chunk
-// Stage layout (byte offsets), the same in both CTAs and both B modes up to
-// the half slot:
-constexpr int kAOwn = 0;                 // A quadrants (r, 0), (r, 1)
-constexpr int kARecv = 2 * kATile;       // the third A quadrant (CTA 0: a3, CTA 1: a0)
-constexpr int kB0 = 3 * kATile;          // three 4 KB B tiles at kB0, kB1, kB2
-constexpr int kB1 = kB0 + kBTile;
-constexpr int kB2 = kB1 + kBTile;
-constexpr int kBH = kB2 + kBTile;        // the 64-column half tile for P1
-constexpr int kBSum = kBH + kBHalf;      // in-kernel B sums only: the sum slot
-// kPreB = false: kB0/kB1 own quadrants (0, 1-r), (1, 1-r); kB2 the other full
-// quadrant; kBH the P1 half.  kPreB = true: kB0..kB2 the operand planes of the
-// CTA's three full products (CTA 0: P3, P5, P7; CTA 1: P2, P4, P6), kBH P1's.
+constexpr int kCols = 128;  // product columns per CTA pair
+// Stage depth of the planes mode: 16 (eight 26 KB stages, the default) or 32
+// (four 52 KB stages with 64-byte A rows: half the TMA requests per byte,
+// measured 2-6 % slower at 8192^3 -- depth in stages matters more).
+#ifndef SB_PAIR_PLANES_KD
+#define SB_PAIR_PLANES_KD 16
+#endif
+// Stage geometry.  A stage holds KD (16 or 32) product-depth columns of every
+// operand; the MMAs and the A-sum ring work in 16-deep sub-steps (two per stage
+// when KD = 32).  Byte offsets, the same in both CTAs:
+//   AOWN  A quadrants (r, 0), (r, 1)           ARECV the third A quadrant
+//   B0..B2 three B tiles (128 columns)          BH    the 64-column half tile for P1
+//   BSUM  (raw B only) the B sum slot
+// Raw B (kPreB = false, KD = 16): B0/B1 own quadrants (0, 1-r), (1, 1-r), B2 the
+// other full quadrant.  Planes (kPreB = true): B0..B2 the operand planes of the
+// CTA's three full products (CTA 0: P3, P5, P7; CTA 1: P2, P4, P6), BH P1's.
+// KD = 32 gives the A tiles 64-byte rows (half the TMA requests of 32-byte rows).
 template <bool kPreB>
 struct Geo {
-  static constexpr int STAGE = kPreB ? kBSum : kBSum + kBTile;  // 26 KB or 30 KB
-  static constexpr int STAGES = kPreB ? 8 : 7;
+  static constexpr int KD = kPreB ? SB_PAIR_PLANES_KD : 16;
+  static constexpr int SUB = KD / 16;                    // 16-deep sub-steps per stage
+  static constexpr int ATILE = kBlockM * KD * 2;         // 128 rows x KD, K-major
+  static constexpr int BTILE = KD * kCols * 2;           // KD rows x 128 columns, two 64-column chunks
+  static constexpr int BHALF = BTILE / 2;
+  static constexpr int AOWN = 0, ARECV = 2 * ATILE, B0 = 3 * ATILE, B1 = B0 + BTILE, B2 = B1 + BTILE,
+                       BH = B2 + BTILE, BSUM = BH + BHALF;
+  static constexpr int STAGE = kPreB ? BSUM : BSUM + BTILE;  // 26 or 52 KB (planes), 30 KB (raw)
+  static constexpr int STAGES = kPreB ? (KD == 32 ? 4 : 8) : 7;
   static constexpr int DATA = STAGES * STAGE;
   static constexpr int BAR_BYTES = 512;
   static constexpr int SMEM = DATA + BAR_BYTES + 1024;  // + alignment slack
-  static constexpr int TX0 = 2 * kATile + (kPreB ? 3 : 2) * kBTile;    // producer 0 (warp 0)
-  static constexpr int TX1 = kATile + (kPreB ? 0 : kBTile) + kBHalf;   // producer 1 (warp 2)
-  // Barrier slots (8 bytes each) after the stages.
-  static constexpr int FULL = 0, SUMS = STAGES, EMPTY = 2 * STAGES, ACC = 3 * STAGES, XFREE = ACC + 1,
-                       XDATA = ACC + 2, WORDS = ACC + 3;
-  static_assert(STAGE % 1024 == 0, "128-byte swizzle atoms need 1024-byte aligned tiles");
+  static constexpr int TX0 = 2 * ATILE + (kPreB ? 3 : 2) * BTILE;   // producer 0 (warp 0)
+  static constexpr int TX1 = ATILE + (kPreB ? 0 : BTILE) + BHALF;   // producer 1 (warp 2)
+  // A tiles: 32- or 64-byte rows (swizzle span); 8-row core groups.
+  static constexpr uint32_t A_LAYOUT = KD == 32 ? kLayoutSwizzle64B : kLayoutSwizzle32B;
+  static constexpr uint32_t A_SBO = 8 * KD * 2;
+  static constexpr uint32_t B_LBO = KD * 128;  // MN-major 128-byte swizzle: next 64-column chunk
+  // Barrier slots (8 bytes each) after the stages.  RING0: the commit after a
+  // stage's first sub-step (KD = 32), which frees ring half 0.
+  static constexpr int FULL = 0, SUMS = STAGES, EMPTY = STAGES * (1 + SUB), RING0 = EMPTY + STAGES,
+                       ACC = RING0 + STAGES, XFREE = ACC + 1, XDATA = ACC + 2, WORDS = ACC + 3;
+  static_assert(KD == 16 || (KD == 32 && kPreB), "32-deep stages need the B operand planes");
+  static_assert(STAGE % 1024 == 0 && B0 % 1024 == 0 && BH % 1024 == 0 && BSUM % 1024 == 0,
+                "128-byte swizzle atoms need 1024-byte aligned tiles");
   static_assert(WORDS * 8 + 16 <= BAR_BYTES, "barrier area");
   static_assert(SMEM <= 227 * 1024, "shared memory budget");
 };
-static_assert(kB0 % 1024 == 0 && kBH % 1024 == 0 && kBSum % 1024 == 0, "1024-byte aligned B tiles");
 constexpr int kXRowBytes = kCols * 4 + 16;  // exchange row: 128 fp32 + 16 B (bank spread)
-static_assert(kBlockM * kXRowBytes <= Geo<true>::DATA, "exchange buffer fits in the idle stages");
+static_assert(kBlockM * kXRowBytes <= Geo<true>::DATA && kBlockM * kXRowBytes <= Geo<false>::DATA,
+              "exchange buffer fits in the idle stages");
 constexpr uint32_t kIdesc128 = umma_idesc_bf16_f32(kBlockM, 128, false, true);
 constexpr uint32_t kIdesc64 = umma_idesc_bf16_f32(kBlockM, 64, false, true);
-constexpr uint32_t kBLbo = 2048;  // MN-major 128-byte swizzle: offset of the next 64-column chunk
-constexpr uint32_t kBSbo = 1024;  // next 8 k-rows
-constexpr uint32_t kALbo = 16, kASbo = 256;  // K-major 32-byte swizzle rows (LBO unused)
+constexpr uint32_t kBSbo = 1024;  // next 8 k-rows of a 128-byte-swizzled B tile
+constexpr uint32_t kALbo = 16;    // unused for swizzled K-major A
 static_assert(kRingCol0 + 32 + 24 <= kTmemCols, "two-step ring of three A operands");
 // Operand planes of the B side, in the order the CTAs load them.
 constexpr int kPlaneP3 = 0, kPlaneP5 = 1, kPlaneP7 = 2, kPlaneP1 = 3, kPlaneP2 = 4, kPlaneP4 = 5, kPlaneP6 = 6;
@@ -183,8 +197,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
       mbar_init(bar(G::FULL + s), 2);
-      mbar_init(bar(G::SUMS + s), 4);
+      for (int h = 0; h < G::SUB; ++h) mbar_init(bar(G::SUMS + s * G::SUB + h), 4);
       mbar_init(bar(G::EMPTY + s), 1);
+      mbar_init(bar(G::RING0 + s), 1);
     }
     mbar_init(bar(G::ACC), 1);
     mbar_init(bar(G::XFREE), kSumWarps);
@@ -217,30 +232,31 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int a_block = t0 / p.half_bm;
       const int j_block = u0 / p.half_bn;
       const int b_chunk0 = (j_block * p.bn + (u0 - j_block * p.half_bn)) / 64;  // raw-B column chunk
-      for (int c = 0; c < p.num_chunks; ++c) {
+      const int num_stages = p.num_chunks / G::SUB;  // num_chunks counts 16-deep steps
+      for (int c = 0; c < num_stages; ++c) {
         const int s = c % kStages;
         if (!mbar_wait(bar(G::EMPTY + s), ((c / kStages) & 1u) ^ 1u, abort_flag, p.err, kErrWaitEmpty)) break;
         const uint32_t stage = smem_base + s * G::STAGE;
         const uint32_t fb = bar(G::FULL + s);
-        const int kap = c * 16;
+        const int kap = c * G::KD;  // a stage never straddles a K panel: half_bk is a multiple of 128
         const int panel = kap / p.half_bk;
         const int kcol = panel * p.bk + (kap - panel * p.half_bk);
         if (first) {
           mbar_arrive_expect_tx(fb, G::TX0);
-          tma_load_5d(stage + kAOwn, &tmap_a, fb, kcol, a_row_base, a_block, 0, (int)rank);
+          tma_load_5d(stage + G::AOWN, &tmap_a, fb, kcol, a_row_base, a_block, 0, (int)rank);
           if constexpr (kPreB) {
-            tma_load_4d(stage + kB0, &tmap_b, fb, 0, kap, u0 / 64, rank ? kPlaneP2 : kPlaneP3);
+            tma_load_4d(stage + G::B0, &tmap_b, fb, 0, kap, u0 / 64, rank ? kPlaneP2 : kPlaneP3);
           } else {
-            tma_load_5d(stage + kB0, &tmap_b, fb, 0, kcol, b_chunk0, (int)peer, 0);
+            tma_load_5d(stage + G::B0, &tmap_b, fb, 0, kcol, b_chunk0, (int)peer, 0);
           }
         } else {
           mbar_arrive_expect_tx(fb, G::TX1);
-          tma_load_5d(stage + kARecv, &tmap_a1, fb, kcol, a_row_base, a_block, (int)peer, (int)peer);
+          tma_load_5d(stage + G::ARECV, &tmap_a1, fb, kcol, a_row_base, a_block, (int)peer, (int)peer);
           if constexpr (kPreB) {
-            tma_load_4d(stage + kBH, &tmap_bh, fb, 0, kap, u0 / 64 + (int)rank, kPlaneP1);
+            tma_load_4d(stage + G::BH, &tmap_bh, fb, 0, kap, u0 / 64 + (int)rank, kPlaneP1);
           } else {
-            tma_load_5d(stage + kB2, &tmap_b1, fb, 0, kcol, b_chunk0, (int)rank, (int)peer);
-            tma_load_5d(stage + kBH, &tmap_bh, fb, 0, kcol, b_chunk0 + (int)rank, (int)rank, (int)rank);
+            tma_load_5d(stage + G::B2, &tmap_b1, fb, 0, kcol, b_chunk0, (int)rank, (int)peer);
+            tma_load_5d(stage + G::BH, &tmap_bh, fb, 0, kcol, b_chunk0 + (int)rank, (int)rank, (int)rank);
           }
         }
         last_armed[s] = c;
@@ -254,39 +270,53 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
-      const uint64_t a_d0 = umma_smem_desc(smem_base, kALbo, kASbo, kLayoutSwizzle32B);
-      const uint64_t b_d0 = umma_smem_desc(smem_base, kBLbo, kBSbo, kLayoutSwizzle128B);
+      const uint64_t a_d0 = umma_smem_desc(smem_base, kALbo, G::A_SBO, G::A_LAYOUT);
+      const uint64_t b_d0 = umma_smem_desc(smem_base, G::B_LBO, kBSbo, kLayoutSwizzle128B);
       // Accumulators 0 and 1: one with A in shared memory, one from the A ring
       // (CTA 0: M3 = a0 x B0 ss, M5 = ring0 x B1; CTA 1: M2 = ring0 x B0,
       // M4 = a3 x B1 ss).  B tile of each accumulator per mode (see Geo).
-      const uint64_t ss_a = (uint64_t)((kAOwn + (rank ? kATile : 0)) >> 4);  // a0 or a3
+      const uint64_t ss_a = (uint64_t)((G::AOWN + (rank ? G::ATILE : 0)) >> 4);  // a0 or a3
       int ss_bo, ts_bo;
       if (kPreB) {
-        ss_bo = rank ? kB1 : kB0;
-        ts_bo = rank ? kB0 : kB1;
+        ss_bo = rank ? G::B1 : G::B0;
+        ts_bo = rank ? G::B0 : G::B1;
       } else {
-        ss_bo = kBSum;               // b1-b3 or b2-b0
-        ts_bo = rank ? kB0 : kB1;    // b0 (own quadrant 0 of CTA 1) or b3 (own quadrant 1 of CTA 0)
+        ss_bo = G::BSUM;               // b1-b3 or b2-b0
+        ts_bo = rank ? G::B0 : G::B1;  // b0 (own quadrant 0 of CTA 1) or b3 (own quadrant 1 of CTA 0)
       }
       const uint64_t ss_b = (uint64_t)(ss_bo >> 4), ts_b = (uint64_t)(ts_bo >> 4);
+      const uint64_t b2_b = (uint64_t)(G::B2 >> 4), bh_b = (uint64_t)(G::BH >> 4);
       const uint32_t ss_d = tmem_base + (rank ? 128u : 0u);
       const uint32_t ts_d = tmem_base + (rank ? 0u : 128u);
-      int s = 0;
+      // One pass per 16-deep sub-step g: stage g / SUB, half h = g % SUB.  Within
+      // a stage, sub-step h starts 16 K columns in: +32 bytes along a K-major A
+      // row, +16 rows (2048 bytes) of an MN-major B tile.
+      int s = 0, h = 0;
       uint32_t ph = 0;
-      for (int c = 0; c < p.num_chunks; ++c) {
-        if (!mbar_wait(bar(G::SUMS + s), ph, abort_flag, p.err, kErrWaitSums)) break;
+      for (int g = 0; g < p.num_chunks; ++g) {
+        if (!mbar_wait(bar(G::SUMS + s * G::SUB + h), ph, abort_flag, p.err, kErrWaitSums)) break;
         tc_fence_after();
         const uint64_t so = (uint64_t)((s * G::STAGE) >> 4);
-        const uint32_t acc = c != 0 ? 1u : 0u;
-        const uint32_t ring = tmem_base + kRingCol0 + 32u * (uint32_t)(c & 1);
-        umma_bf16_ss(ss_d, a_d0 + so + ss_a, b_d0 + so + ss_b, kIdesc128, acc);
-        umma_bf16_ts(ts_d, ring + 0, b_d0 + so + ts_b, kIdesc128, acc);
-        umma_bf16_ts(tmem_base + 256, ring + 8, b_d0 + so + (uint64_t)(kB2 >> 4), kIdesc128, acc);
-        umma_bf16_ts(tmem_base + 384, ring + 16, b_d0 + so + (uint64_t)(kBH >> 4), kIdesc64, acc);
-        umma_commit(bar(G::EMPTY + s));
-        if (++s == kStages) {
-          s = 0;
-          ph ^= 1u;
+        const uint64_t ka = (uint64_t)(h * 2), kb = (uint64_t)(h * 128);
+        const uint32_t acc = g != 0 ? 1u : 0u;
+        const uint32_t ring = tmem_base + kRingCol0 + 32u * (uint32_t)(g & 1);
+        umma_bf16_ss(ss_d, a_d0 + so + ss_a + ka, b_d0 + so + ss_b + kb, kIdesc128, acc);
+        umma_bf16_ts(ts_d, ring + 0, b_d0 + so + ts_b + kb, kIdesc128, acc);
+        umma_bf16_ts(tmem_base + 256, ring + 8, b_d0 + so + b2_b + kb, kIdesc128, acc);
+        umma_bf16_ts(tmem_base + 384, ring + 16, b_d0 + so + bh_b + kb, kIdesc64, acc);
+        // The last sub-step of a stage frees the stage (and its ring half); an
+        // earlier one frees ring half 0 only.
+        if (h == G::SUB - 1) {
+          umma_commit(bar(G::EMPTY + s));
+        } else {
+          umma_commit(bar(G::RING0 + s));
+        }
+        if (++h == G::SUB) {
+          h = 0;
+          if (++s == kStages) {
+            s = 0;
+            ph ^= 1u;
+          }
         }
       }
       // Always commit: the epilogue (or the teardown drain) waits on it.
@@ -297,23 +327,36 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int set = (warp - kFirstSumWarp) >> 2;
     const int q = warp & 3;
     const uint32_t row = 32 * q + lane;  // product row = TMEM lane; also the B chunk index
-    const uint32_t sw = (row >> 2) & 1u;  // 32-byte swizzle: the row's two chunks swap on bit 2
-    const uint32_t lo_off = 32 * row + 16 * sw;
-    const uint32_t hi_off = 32 * row + 16 * (sw ^ 1u);
+    // The two 16-byte chunks of this row's 16-deep slice in a swizzled A tile.
+    // 32-byte rows (KD = 16): the chunks swap on row bit 2.  64-byte rows
+    // (KD = 32): chunk j sits at j ^ ((row >> 1) & 3); a set always takes the
+    // same half h = set of a stage, so its offsets are fixed.
+    uint32_t lo_off, hi_off;
+    if constexpr (G::KD == 32) {
+      const uint32_t sw = (row >> 1) & 3u;
+      lo_off = 64 * row + 16 * ((2u * set) ^ sw);
+      hi_off = 64 * row + 16 * ((2u * set + 1u) ^ sw);
+    } else {
+      const uint32_t sw = (row >> 2) & 1u;
+      lo_off = 32 * row + 16 * sw;
+      hi_off = 32 * row + 16 * (sw ^ 1u);
+    }
     const uint32_t tmem_lane = tmem_base + ((uint32_t)(32 * q) << 16) + kRingCol0;
-    const uint32_t o1 = 16 * row, o2 = o1 + kBHalf;
-    for (int c = set; c < p.num_chunks; c += 2) {
-      const int s = c % kStages;
+    const uint32_t o1 = 16 * row, o2 = o1 + G::BHALF;
+    // Sub-steps g = set, set + 2, ...: stage g / SUB, half g % SUB.
+    for (int g = set; g < p.num_chunks; g += 2) {
+      const int stage_i = g / G::SUB, h = g % G::SUB;
+      const int s = stage_i % kStages;
       if (!__all_sync(0xffffffffu,
-                      mbar_wait(bar(G::FULL + s), (c / kStages) & 1u, abort_flag, p.err, kErrWaitRaw))) {
+                      mbar_wait(bar(G::FULL + s), (stage_i / kStages) & 1u, abort_flag, p.err, kErrWaitRaw))) {
         ok = false;
         break;
       }
       const uint32_t st = smem_base + s * G::STAGE;
       // A: x0, x1 = quadrants (r, 0), (r, 1); x2 = the third quadrant.
-      const uint4 x0l = lds128(st + kAOwn + lo_off), x0h = lds128(st + kAOwn + hi_off);
-      const uint4 x1l = lds128(st + kAOwn + kATile + lo_off), x1h = lds128(st + kAOwn + kATile + hi_off);
-      const uint4 x2l = lds128(st + kARecv + lo_off), x2h = lds128(st + kARecv + hi_off);
+      const uint4 x0l = lds128(st + G::AOWN + lo_off), x0h = lds128(st + G::AOWN + hi_off);
+      const uint4 x1l = lds128(st + G::AOWN + G::ATILE + lo_off), x1h = lds128(st + G::AOWN + G::ATILE + hi_off);
+      const uint4 x2l = lds128(st + G::ARECV + lo_off), x2h = lds128(st + G::ARECV + hi_off);
       uint4 r0l, r0h, r1l, r1h, r2l, r2h;
       r0l = add4(x0l, x1l);  // CTA 0: a0+a1   CTA 1: a2+a3
       r0h = add4(x0h, x1h);
@@ -326,43 +369,45 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       if constexpr (!kPreB) {
         // B: d, e = own quadrants (0, 1-r), (1, 1-r); f = the other full quadrant, h = P1's half.
-        const uint4 d1 = lds128(st + kB0 + o1), d2 = lds128(st + kB0 + o2);
-        const uint4 e1 = lds128(st + kB1 + o1), e2 = lds128(st + kB1 + o2);
-        const uint4 f1 = lds128(st + kB2 + o1), f2 = lds128(st + kB2 + o2);
-        const uint4 h1 = lds128(st + kBH + o1);
+        const uint4 d1 = lds128(st + G::B0 + o1), d2 = lds128(st + G::B0 + o2);
+        const uint4 e1 = lds128(st + G::B1 + o1), e2 = lds128(st + G::B1 + o2);
+        const uint4 f1 = lds128(st + G::B2 + o1), f2 = lds128(st + G::B2 + o2);
+        const uint4 h1 = lds128(st + G::BH + o1);
         if (rank == 0) {
-          sts128(st + kBSum + o1, sub4(d1, e1));  // b1 - b3
-          sts128(st + kBSum + o2, sub4(d2, e2));
-          sts128(st + kB2 + o1, add4(f1, e1));    // b2 + b3
-          sts128(st + kB2 + o2, add4(f2, e2));
-          sts128(st + kBH + o1, add4(h1, e1));    // (b0 + b3) left chunk
+          sts128(st + G::BSUM + o1, sub4(d1, e1));  // b1 - b3
+          sts128(st + G::BSUM + o2, sub4(d2, e2));
+          sts128(st + G::B2 + o1, add4(f1, e1));    // b2 + b3
+          sts128(st + G::B2 + o2, add4(f2, e2));
+          sts128(st + G::BH + o1, add4(h1, e1));    // (b0 + b3) left chunk
         } else {
-          sts128(st + kBSum + o1, sub4(e1, d1));  // b2 - b0
-          sts128(st + kBSum + o2, sub4(e2, d2));
-          sts128(st + kB2 + o1, add4(d1, f1));    // b0 + b1
-          sts128(st + kB2 + o2, add4(d2, f2));
-          sts128(st + kBH + o1, add4(d2, h1));    // (b0 + b3) right chunk
+          sts128(st + G::BSUM + o1, sub4(e1, d1));  // b2 - b0
+          sts128(st + G::BSUM + o2, sub4(e2, d2));
+          sts128(st + G::B2 + o1, add4(d1, f1));    // b0 + b1
+          sts128(st + G::B2 + o2, add4(d2, f2));
+          sts128(st + G::BH + o1, add4(d2, h1));    // (b0 + b3) right chunk
         }
         fence_proxy_async_smem();
       }
-      // Ring half c & 1 is free once the MMAs of step c - 2 completed.
-      if (c >= 2) {
-        const bool waited = mbar_wait(bar(G::EMPTY + (c - 2) % kStages), ((c - 2) / kStages) & 1u, abort_flag,
-                                      p.err, kErrWaitEmpty);
+      // Ring half g & 1 is free once the MMAs of sub-step g - 2 completed: the
+      // stage commit if that was its stage's last sub-step, else RING0.
+      if (g >= 2) {
+        const int ps = (g - 2) / G::SUB, ph_ = (g - 2) % G::SUB;
+        const uint32_t free_bar = bar((ph_ == G::SUB - 1 ? G::EMPTY : G::RING0) + ps % kStages);
+        const bool waited = mbar_wait(free_bar, (ps / kStages) & 1u, abort_flag, p.err, kErrWaitEmpty);
         if (!__all_sync(0xffffffffu, waited)) {
           ok = false;
           break;
         }
       }
       tc_fence_after();
-      const uint32_t ring = tmem_lane + 32u * (uint32_t)(c & 1);
+      const uint32_t ring = tmem_lane + 32u * (uint32_t)(g & 1);
       tmem_store_8(ring + 0, r0l, r0h);
       tmem_store_8(ring + 8, r1l, r1h);
       tmem_store_8(ring + 16, r2l, r2h);
       tmem_store_wait();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(bar(G::SUMS + s));
+      if (lane == 0) mbar_arrive(bar(G::SUMS + s * G::SUB + h));
     }
 
     // ------------------------------------------------------------ epilogue
