@@ -198,10 +198,6 @@ def run_reference(args):
         "ms_per_step": 1e3 * total_t / args.steps, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
         "config": {"workload": f"strassen_gemm_{M}x{N}x{K}_bf16", "tile": list(TILE),
-                   "kernel": {"single": "one-CTA (sb_strassen_gemm)",
-                              "pair": "two-CTA cluster (sb_strassen_gemm_pair)",
-                              "pair-planes": "B operand planes + two-CTA cluster (sb_strassen_b_operands, "
-                                             "sb_strassen_gemm_pair_planes), both timed"}[args.kernel],
                    "sample": sample},
         "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port",
                          "sample": sample},
