@@ -240,8 +240,8 @@ def run_ours(args):
 
         def step():
             # B's operand planes are formed inside the timed step (B is an input).
-            sb.strassen_b_operands(b, bn=TILE[1], bk=TILE[2], out=planes)
-            sb.pair_matmul(a, None, b_operands=planes, bm=TILE[0], bn=TILE[1], bk=TILE[2], out=c)
+            ops = sb.strassen_b_operands(b, bn=TILE[1], bk=TILE[2], out=planes)
+            sb.pair_matmul(a, None, b_operands=ops, bm=TILE[0], bn=TILE[1], bk=TILE[2], out=c)
     else:
         gemm = sb.pair_matmul if args.kernel == "pair" else sb.strassen_matmul
 

@@ -7,7 +7,9 @@
  * buffer: the library allocates device memory only in sb_p2p_buffer_alloc,
  * whose job that is.  Scratch space that an epilogue needs
  * (norm_residual_add) is passed in as `workspace`, sized by
- * sb_workspace_bytes().
+ * sb_workspace_bytes(); the one exception is
+ * sb_strassen_gemm_norm_residual_noalloc, whose scratch is a fixed 32 MiB
+ * device array built into the library (see its declaration).
  *
  * The single operator mirrors strassen_pallas.strassen_matmul
  * (reference: strassen_pallas.py:882-1221).  Matrix semantics follow the
@@ -209,9 +211,10 @@ SB_API int sb_strassen_gemm_pair_planes(sb_stream_t stream,
  * its allocator and synchronise the device), or a service with a fixed memory
  * budget.  It allocates nothing.  Limit: M*N <= 8,388,608 (32 MiB of fp32),
  * else SB_ERR_WORKSPACE.  Every GPU that loads the library holds the 32 MiB
- * until exit; all calls share it, so calls that overlap on the GPU race.  The
- * first call on a device looks up the array's address (make it before any
- * stream capture).  `ep->kind` must be SB_EPI_NORM_RESIDUAL_ADD and bn == n.
+ * until exit; all calls share it, so calls that overlap on the GPU race.  Every
+ * call looks up the array's address in the current context (the first call on
+ * a device also loads the module there: make it before any stream capture).
+ * `ep->kind` must be SB_EPI_NORM_RESIDUAL_ADD and bn == n.
  */
 SB_API int sb_strassen_gemm_norm_residual_noalloc(sb_stream_t stream,
                                                   const void* a, const void* b, void* c,

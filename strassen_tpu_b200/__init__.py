@@ -22,6 +22,7 @@ from .strassen import (
     native_matmul,
     pair_matmul,
     rms_norm,
+    StrassenBOperands,
     strassen_b_operands,
     strassen_matmul,
     strassen_matmul_lhs_transposed,

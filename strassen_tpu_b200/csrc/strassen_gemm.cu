@@ -1273,34 +1273,37 @@ int dispatch(bool strassen, int epi, bool out_f32, cudaStream_t stream, const CU
   }
 }
 
-// Device address of g_device_error per device, resolved by check_device().
-int* g_error_word_addr[64];
+// Device address of g_device_error in the current context, resolved by
+// check_device() on every call (so a cudaDeviceReset or a new primary context
+// never leaves a stale pointer) and read by base_params() on the same host
+// thread.
+thread_local int* t_error_word = nullptr;
 
-// Checks that the current device is an sm_100 part and, once per device with
-// that device current, resolves the address of the bounded-wait error word the
-// kernels write to (base_params hands it to every launch).
+// Checks that the current device is an sm_100 part (the compute capability is
+// cached per device) and resolves the address of the bounded-wait error word
+// the kernels write to.
 int check_device() {
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return fail(SB_ERR_CUDA, std::string("cudaGetDevice: ") + cudaGetErrorString(e));
   static int cached_major[64];
   static int cached_minor[64];
-  static cudaError_t symbol_err[64];
   static std::once_flag flags[64];
   if (dev < 0 || dev >= 64) return fail(SB_ERR_DEVICE, "device ordinal out of range");
   std::call_once(flags[dev], [&]() {
     cudaDeviceGetAttribute(&cached_major[dev], cudaDevAttrComputeCapabilityMajor, dev);
     cudaDeviceGetAttribute(&cached_minor[dev], cudaDevAttrComputeCapabilityMinor, dev);
-    void* addr = nullptr;
-    symbol_err[dev] = cudaGetSymbolAddress(&addr, g_device_error);
-    g_error_word_addr[dev] = symbol_err[dev] == cudaSuccess ? static_cast<int*>(addr) : nullptr;
   });
   if (cached_major[dev] != 10 || cached_minor[dev] != 0)
     return fail(SB_ERR_DEVICE, "the Strassen kernel is built for sm_100a (B200); device is sm_" +
                                    std::to_string(cached_major[dev]) + std::to_string(cached_minor[dev]));
-  if (g_error_word_addr[dev] == nullptr)
-    return fail(SB_ERR_CUDA, std::string("cudaGetSymbolAddress(device error word): ") +
-                                 cudaGetErrorString(symbol_err[dev]));
+  void* addr = nullptr;
+  e = cudaGetSymbolAddress(&addr, g_device_error);
+  if (e != cudaSuccess || addr == nullptr) {
+    t_error_word = nullptr;
+    return fail(SB_ERR_CUDA, std::string("cudaGetSymbolAddress(device error word): ") + cudaGetErrorString(e));
+  }
+  t_error_word = static_cast<int*>(addr);
   return SB_OK;
 }
 
@@ -1451,10 +1454,9 @@ GemmParams base_params(int64_t m, int64_t n, int64_t k, int32_t bm, int32_t bn, 
   p.eps = 1e-6f;
   p.half_head = 64;
   p.inv_head_dim = 1.0f / 128.0f;
-  // check_device() has resolved the error word of the current device.
-  int dev = 0;
-  cudaGetDevice(&dev);
-  p.err = (dev >= 0 && dev < 64) ? g_error_word_addr[dev] : nullptr;
+  // check_device(), called first by every entry point on this thread, has
+  // resolved the error word of the current context.
+  p.err = t_error_word;
   return p;
 }
 
@@ -1553,7 +1555,7 @@ int launch_pair(cudaStream_t stream, const PairMaps& m, const GemmParams& p) {
   cudaLaunchConfig_t cfg;
   std::memset(&cfg, 0, sizeof(cfg));
   cfg.gridDim = dim3((unsigned)(2 * p.tiles_m * p.tiles_n), 1, 1);
-  cfg.blockDim = dim3(kThreads, 1, 1);
+  cfg.blockDim = dim3(pair::kPairThreads, 1, 1);
   cfg.dynamicSmemBytes = kSmem;
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];
@@ -1737,32 +1739,24 @@ int sb_strassen_gemm_ex(sb_stream_t stream_, const void* a, const void* b, void*
 //     M * N values before the row pass reads them;
 //   * calls whose kernels overlap on the GPU (different streams, or several
 //     host threads) race on the array -- serialise them;
-//   * the first call on a device resolves the array's device address with
-//     cudaGetSymbolAddress (once per device, with that device current); make
-//     that first call before any stream capture.
+//   * every call resolves the array's device address in the current context
+//     with cudaGetSymbolAddress (the first call on a device also loads the
+//     module there); make that first call before any stream capture.
 // ---------------------------------------------------------------------------
 namespace sb {
 namespace {
 constexpr size_t kNoAllocScratchFloats = size_t(32) << 20 >> 2;  // 32 MiB of fp32
 static __device__ __align__(256) float g_noalloc_scratch[kNoAllocScratchFloats];
 
+// The array's device address in the current context, looked up on every call
+// (cheap next to a GEMM) so that it stays valid after a cudaDeviceReset or in a
+// new primary context.
 int noalloc_scratch_address(float** out) {
-  int dev = 0;
-  cudaError_t e = cudaGetDevice(&dev);
-  if (e != cudaSuccess) return fail(SB_ERR_CUDA, std::string("cudaGetDevice: ") + cudaGetErrorString(e));
-  if (dev < 0 || dev >= 64) return fail(SB_ERR_DEVICE, "device ordinal out of range");
-  static float* addr[64];
-  static cudaError_t status[64];
-  static std::once_flag once[64];
-  std::call_once(once[dev], [&]() {
-    void* p = nullptr;
-    status[dev] = cudaGetSymbolAddress(&p, g_noalloc_scratch);
-    addr[dev] = static_cast<float*>(p);
-  });
-  if (status[dev] != cudaSuccess || addr[dev] == nullptr)
-    return fail(SB_ERR_CUDA, std::string("cudaGetSymbolAddress(no-alloc scratch): ") +
-                                 cudaGetErrorString(status[dev]));
-  *out = addr[dev];
+  void* p = nullptr;
+  const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+  if (e != cudaSuccess || p == nullptr)
+    return fail(SB_ERR_CUDA, std::string("cudaGetSymbolAddress(no-alloc scratch): ") + cudaGetErrorString(e));
+  *out = static_cast<float*>(p);
   return SB_OK;
 }
 }  // namespace

@@ -26,11 +26,14 @@
 //     rounding) and each CTA loads its three and a half operand planes as they
 //     are: no B sums in the K loop, so the step's shared-memory traffic is the
 //     TMA fill, the A-row reads of the sum warps and the MMA operand reads.
-// Two producer threads (warps 0 and 2) issue the copies and arm the stage's
-// barrier together.  The A sums (CTA 0: a0+a1, a1-a3, a0+a3; CTA 1: a2+a3,
-// a2-a0, a0+a3) go to a two-step TMEM ring and feed A-from-TMEM MMAs; the raw
-// a0 (CTA 0) or a3 (CTA 1) is read from shared memory.  Every pre-add is one
-// RNE bf16 rounding, the reference's pre-add rounding.
+// Four producer warps (0, 2, 12, 13) take the steps round robin; four lanes of
+// the step's warp issue its copies.  The A sums (CTA 0: a0+a1, a1-a3, a0+a3; CTA 1: a2+a3,
+// a2-a0, a0+a3) are written back into the stage (two over raw quadrants that
+// are no longer needed, one into a fourth A slot), so every MMA reads both
+// operands from shared memory and a stage is recycled only through the stage
+// ring: no operand ring in TMEM, whose two-step depth made every step wait on
+// the MMAs of the step before last.  Every pre-add is one RNE bf16 rounding,
+// the reference's pre-add rounding.
 //
 // Recombination.  C11 = M1+M4-M5+M7 and C12 = M3+M5 belong to CTA 0 (top
 // rows of each block), C21 = M2+M4 and C22 = M1-M2+M3+M6 to CTA 1 (bottom
@@ -41,15 +44,19 @@
 //   CTA 1: C21 = M2 + M4, C22 = ((Y0 + [0 | M1R]) - M2) + M6.
 //
 // Synchronisation (all waits bounded, as in the one-CTA kernel):
-//   full[s]  both producers' arrivals + the stage's TMA bytes;
+//   full[s]  the producer's arrival + the stage's TMA bytes;
 //   sums[s]  the four sum warps of the step's set; empty[s] local MMA commit;
+//   named barrier 1: warp 3 waits on sums[] for a group of kGroup steps and
+//            meets the MMA warp there, so the issuing thread never polls an
+//            mbarrier (that stalls it behind its queued MMAs on B200);
 //   xfree / xdata  the epilogue exchange: remote arrivals from the peer, waited
 //            with cluster-scope acquire.
 // The K loop never waits on the peer.  Both CTAs end with a cluster barrier,
 // so neither leaves while the other may still write into its shared memory.
 //
-// Roles: warps 0 and 2 TMA producers, warp 1 TMEM allocation + MMA issue,
-// warps 4-11 operand sums then epilogue (as in the one-CTA kernel).
+// Roles: warps 0, 2, 12, 13 TMA producers, warp 1 TMEM allocation + MMA issue,
+// warp 3 hands each sub-step to the MMA warp (named barrier), warps 4-11
+// operand sums then epilogue (as in the one-CTA kernel).
 //
 // Included by strassen_gemm.cu inside namespace sb, after the one-CTA kernel
 // (it uses its constants, GemmParams and store helpers).
@@ -57,52 +64,55 @@
 namespace pair {
 
 constexpr int kCols = 128;  // product columns per CTA pair
-// Stage depth of the planes mode: 16 (eight 26 KB stages, the default) or 32
-// (four 52 KB stages with 64-byte A rows: half the TMA requests per byte,
-// measured 2-6 % slower at 8192^3 -- depth in stages matters more).
-#ifndef SB_PAIR_PLANES_KD
-#define SB_PAIR_PLANES_KD 16
+// Steps handed from warp 3 to the MMA warp per named-barrier meeting.
+#ifndef SB_PAIR_GROUP
+#define SB_PAIR_GROUP 2
 #endif
-// Stage geometry.  A stage holds KD (16 or 32) product-depth columns of every
-// operand; the MMAs and the A-sum ring work in 16-deep sub-steps (two per stage
-// when KD = 32).  Byte offsets, the same in both CTAs:
+constexpr int kGroup = SB_PAIR_GROUP;
+// Stage geometry: one 16-deep K step of every operand.  Byte offsets, the same
+// in both CTAs:
 //   AOWN  A quadrants (r, 0), (r, 1)           ARECV the third A quadrant
-//   B0..B2 three B tiles (128 columns)          BH    the 64-column half tile for P1
-//   BSUM  (raw B only) the B sum slot
-// Raw B (kPreB = false, KD = 16): B0/B1 own quadrants (0, 1-r), (1, 1-r), B2 the
-// other full quadrant.  Planes (kPreB = true): B0..B2 the operand planes of the
-// CTA's three full products (CTA 0: P3, P5, P7; CTA 1: P2, P4, P6), BH P1's.
-// KD = 32 gives the A tiles 64-byte rows (half the TMA requests of 32-byte rows).
+//   ASUM  the third A operand sum              B0..B2 three B tiles (128 columns)
+//   BH    the 64-column half tile for P1       BSUM  (raw B only) the B sum slot
+// Raw B (kPreB = false): B0/B1 own quadrants (0, 1-r), (1, 1-r), B2 the other
+// full quadrant.  Planes (kPreB = true): B0..B2 the operand planes of the CTA's
+// three full products (CTA 0: P3, P5, P7; CTA 1: P2, P4, P6), BH P1's.
 template <bool kPreB>
 struct Geo {
-  static constexpr int KD = kPreB ? SB_PAIR_PLANES_KD : 16;
-  static constexpr int SUB = KD / 16;                    // 16-deep sub-steps per stage
-  static constexpr int ATILE = kBlockM * KD * 2;         // 128 rows x KD, K-major
-  static constexpr int BTILE = KD * kCols * 2;           // KD rows x 128 columns, two 64-column chunks
+  static constexpr int KD = 16;
+  static constexpr int ATILE = kBlockM * KD * 2;         // 128 rows x 16, K-major, 32-byte rows
+  static constexpr int BTILE = KD * kCols * 2;           // 16 rows x 128 columns, two 64-column chunks
   static constexpr int BHALF = BTILE / 2;
-  static constexpr int AOWN = 0, ARECV = 2 * ATILE, B0 = 3 * ATILE, B1 = B0 + BTILE, B2 = B1 + BTILE,
-                       BH = B2 + BTILE, BSUM = BH + BHALF;
-  static constexpr int STAGE = kPreB ? BSUM : BSUM + BTILE;  // 26 or 52 KB (planes), 30 KB (raw)
-  static constexpr int STAGES = kPreB ? (KD == 32 ? 4 : 8) : 7;
+  static constexpr int AOWN = 0, ARECV = 2 * ATILE, ASUM = 3 * ATILE, B0 = 4 * ATILE, B1 = B0 + BTILE,
+                       B2 = B1 + BTILE, BH = B2 + BTILE, BSUM = BH + BHALF;
+  static constexpr int STAGE = kPreB ? BSUM : BSUM + BTILE;  // 30 KB (planes), 34 KB (raw)
+  static constexpr int STAGES = kPreB ? 7 : 6;
   static constexpr int DATA = STAGES * STAGE;
   static constexpr int BAR_BYTES = 512;
   static constexpr int SMEM = DATA + BAR_BYTES + 1024;  // + alignment slack
-  static constexpr int TX0 = 2 * ATILE + (kPreB ? 3 : 2) * BTILE;   // producer 0 (warp 0)
-  static constexpr int TX1 = ATILE + (kPreB ? 0 : BTILE) + BHALF;   // producer 1 (warp 2)
-  // A tiles: 32- or 64-byte rows (swizzle span); 8-row core groups.
-  static constexpr uint32_t A_LAYOUT = KD == 32 ? kLayoutSwizzle64B : kLayoutSwizzle32B;
+  // Bytes each producer warp lands per stage (roles, see the kernel).
+  static constexpr int TX_A_OWN = 2 * ATILE, TX_A_RECV = ATILE;  // per stage, all four copies together
+  static constexpr int TX_B = (kPreB ? 3 : 2) * BTILE, TX_BH = (kPreB ? 0 : BTILE) + BHALF;
+  static constexpr uint32_t A_LAYOUT = kLayoutSwizzle32B;
   static constexpr uint32_t A_SBO = 8 * KD * 2;
   static constexpr uint32_t B_LBO = KD * 128;  // MN-major 128-byte swizzle: next 64-column chunk
-  // Barrier slots (8 bytes each) after the stages.  RING0: the commit after a
-  // stage's first sub-step (KD = 32), which frees ring half 0.
-  static constexpr int FULL = 0, SUMS = STAGES, EMPTY = STAGES * (1 + SUB), RING0 = EMPTY + STAGES,
-                       ACC = RING0 + STAGES, XFREE = ACC + 1, XDATA = ACC + 2, WORDS = ACC + 3;
-  static_assert(KD == 16 || (KD == 32 && kPreB), "32-deep stages need the B operand planes");
+  // Barrier slots (8 bytes each) after the stages.
+  static constexpr int FULL = 0, SUMS = STAGES, EMPTY = 2 * STAGES, ACC = 3 * STAGES, XFREE = ACC + 1,
+                       XDATA = ACC + 2, WORDS = ACC + 3;
   static_assert(STAGE % 1024 == 0 && B0 % 1024 == 0 && BH % 1024 == 0 && BSUM % 1024 == 0,
                 "128-byte swizzle atoms need 1024-byte aligned tiles");
   static_assert(WORDS * 8 + 16 <= BAR_BYTES, "barrier area");
   static_assert(SMEM <= 227 * 1024, "shared memory budget");
 };
+// Four producer warps take the K steps round robin (warp i: steps i, i + 4,
+// ...); within a step lanes 0-3 issue its four TMA copies.  A B200 thread that
+// streams copies through a ring sustains only about one copy per 500-800
+// cycles however deep the ring or large the copy (measured), so each thread
+// issues one copy per four steps.
+constexpr int kProducers = 4;
+constexpr int kProducerWarp[kProducers] = {0, 2, 12, 13};
+constexpr int kCopies = 4;  // TMA copies per stage (lanes 0..3 of the step's producer warp)
+constexpr int kPairThreads = 14 * 32;  // warps 0-13
 constexpr int kXRowBytes = kCols * 4 + 16;  // exchange row: 128 fp32 + 16 B (bank spread)
 static_assert(kBlockM * kXRowBytes <= Geo<true>::DATA && kBlockM * kXRowBytes <= Geo<false>::DATA,
               "exchange buffer fits in the idle stages");
@@ -110,7 +120,6 @@ constexpr uint32_t kIdesc128 = umma_idesc_bf16_f32(kBlockM, 128, false, true);
 constexpr uint32_t kIdesc64 = umma_idesc_bf16_f32(kBlockM, 64, false, true);
 constexpr uint32_t kBSbo = 1024;  // next 8 k-rows of a 128-byte-swizzled B tile
 constexpr uint32_t kALbo = 16;    // unused for swizzled K-major A
-static_assert(kRingCol0 + 32 + 24 <= kTmemCols, "two-step ring of three A operands");
 // Operand planes of the B side, in the order the CTAs load them.
 constexpr int kPlaneP3 = 0, kPlaneP5 = 1, kPlaneP7 = 2, kPlaneP1 = 3, kPlaneP2 = 4, kPlaneP4 = 5, kPlaneP6 = 6;
 
@@ -162,7 +171,7 @@ __global__ void __launch_bounds__(256) b_operand_planes_kernel(const __nv_bfloat
 }
 
 template <bool kOutF32, bool kPreB>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(pair::kPairThreads, 1)
     strassen_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_a1,
                          const __grid_constant__ CUtensorMap tmap_b, const __grid_constant__ CUtensorMap tmap_b1,
                          const __grid_constant__ CUtensorMap tmap_bh, const GemmParams p) {
@@ -196,10 +205,9 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
-      mbar_init(bar(G::FULL + s), 2);
-      for (int h = 0; h < G::SUB; ++h) mbar_init(bar(G::SUMS + s * G::SUB + h), 4);
+      mbar_init(bar(G::FULL + s), 1);
+      mbar_init(bar(G::SUMS + s), 4);
       mbar_init(bar(G::EMPTY + s), 1);
-      mbar_init(bar(G::RING0 + s), 1);
     }
     mbar_init(bar(G::ACC), 1);
     mbar_init(bar(G::XFREE), kSumWarps);
@@ -208,9 +216,15 @@ __global__ void __launch_bounds__(kThreads, 1)
     fence_mbar_init();
     fence_proxy_async_smem();
   }
-  if ((warp == 0 || warp == 2) && lane == 0) {
-    tma_prefetch_desc(warp == 0 ? &tmap_a : &tmap_a1);
-    tma_prefetch_desc(warp == 0 ? &tmap_b : &tmap_bh);
+  // Index of this producer warp (-1: not a producer); lane `role` < kCopies
+  // issues one copy of each of the warp's steps: 0 A own quadrants, 1 the third
+  // A quadrant, 2 the B tiles, 3 P1's half tile (raw B: also the third B tile).
+  const int producer = warp == kProducerWarp[0] ? 0 : warp == kProducerWarp[1] ? 1
+                     : warp == kProducerWarp[2] ? 2 : warp == kProducerWarp[3] ? 3 : -1;
+  const int role = lane;
+  if (producer >= 0 && role < kCopies) {
+    tma_prefetch_desc(role == 0 ? &tmap_a : role == 1 ? &tmap_a1 : role == 2 ? &tmap_b : &tmap_bh);
+    if (!kPreB && role == 3) tma_prefetch_desc(&tmap_b1);
   }
   if (warp == 1) tmem_alloc<kTmemCols>(smem_addr(tmem_holder));
   tc_fence_before();
@@ -221,151 +235,146 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t tmem_base = *tmem_holder;
 
   bool ok = true;
-  if (warp == 0 || warp == 2) {
+  if (producer >= 0) {
     // ------------------------------------------------------------ TMA producers
-    if (lane == 0) {
-      const bool first = warp == 0;
-      int last_armed[kStages];
-#pragma unroll
-      for (int s = 0; s < kStages; ++s) last_armed[s] = -1;
-      const int a_row_base = t0 % p.half_bm;
-      const int a_block = t0 / p.half_bm;
-      const int j_block = u0 / p.half_bn;
-      const int b_chunk0 = (j_block * p.bn + (u0 - j_block * p.half_bn)) / 64;  // raw-B column chunk
-      const int num_stages = p.num_chunks / G::SUB;  // num_chunks counts 16-deep steps
-      for (int c = 0; c < num_stages; ++c) {
-        const int s = c % kStages;
-        if (!mbar_wait(bar(G::EMPTY + s), ((c / kStages) & 1u) ^ 1u, abort_flag, p.err, kErrWaitEmpty)) break;
-        const uint32_t stage = smem_base + s * G::STAGE;
-        const uint32_t fb = bar(G::FULL + s);
-        const int kap = c * G::KD;  // a stage never straddles a K panel: half_bk is a multiple of 128
-        const int panel = kap / p.half_bk;
-        const int kcol = panel * p.bk + (kap - panel * p.half_bk);
-        if (first) {
-          mbar_arrive_expect_tx(fb, G::TX0);
-          tma_load_5d(stage + G::AOWN, &tmap_a, fb, kcol, a_row_base, a_block, 0, (int)rank);
-          if constexpr (kPreB) {
-            tma_load_4d(stage + G::B0, &tmap_b, fb, 0, kap, u0 / 64, rank ? kPlaneP2 : kPlaneP3);
-          } else {
-            tma_load_5d(stage + G::B0, &tmap_b, fb, 0, kcol, b_chunk0, (int)peer, 0);
-          }
+    const int a_row_base = t0 % p.half_bm;
+    const int a_block = t0 / p.half_bm;
+    const int j_block = u0 / p.half_bn;
+    const int b_chunk0 = (j_block * p.bn + (u0 - j_block * p.half_bn)) / 64;  // raw-B column chunk
+    for (int c = producer; c < p.num_chunks; c += kProducers) {
+      const int s = c % kStages;
+      const bool freed = mbar_wait_hint(bar(G::EMPTY + s), ((c / kStages) & 1u) ^ 1u, abort_flag, p.err,
+                                        kErrWaitEmpty);
+      if (!__all_sync(0xffffffffu, freed)) break;
+      const uint32_t stage = smem_base + s * G::STAGE;
+      const uint32_t fb = bar(G::FULL + s);
+      const int kap = c * G::KD;
+      const int panel = kap / p.half_bk;
+      const int kcol = panel * p.bk + (kap - panel * p.half_bk);
+      if (lane == 0) mbar_arrive_expect_tx(fb, G::TX_A_OWN + G::TX_A_RECV + G::TX_B + G::TX_BH);
+      __syncwarp();
+      if (role == 0) {
+        tma_load_5d(stage + G::AOWN, &tmap_a, fb, kcol, a_row_base, a_block, 0, (int)rank);
+      } else if (role == 1) {
+        tma_load_5d(stage + G::ARECV, &tmap_a1, fb, kcol, a_row_base, a_block, (int)peer, (int)peer);
+      } else if (role == 2) {
+        if constexpr (kPreB) {
+          tma_load_4d(stage + G::B0, &tmap_b, fb, 0, kap, u0 / 64, rank ? kPlaneP2 : kPlaneP3);
         } else {
-          mbar_arrive_expect_tx(fb, G::TX1);
-          tma_load_5d(stage + G::ARECV, &tmap_a1, fb, kcol, a_row_base, a_block, (int)peer, (int)peer);
-          if constexpr (kPreB) {
-            tma_load_4d(stage + G::BH, &tmap_bh, fb, 0, kap, u0 / 64 + (int)rank, kPlaneP1);
-          } else {
-            tma_load_5d(stage + G::B2, &tmap_b1, fb, 0, kcol, b_chunk0, (int)rank, (int)peer);
-            tma_load_5d(stage + G::BH, &tmap_bh, fb, 0, kcol, b_chunk0 + (int)rank, (int)rank, (int)rank);
-          }
+          tma_load_5d(stage + G::B0, &tmap_b, fb, 0, kcol, b_chunk0, (int)peer, 0);
         }
-        last_armed[s] = c;
+      } else if (role == 3) {
+        if constexpr (kPreB) {
+          tma_load_4d(stage + G::BH, &tmap_bh, fb, 0, kap, u0 / 64 + (int)rank, kPlaneP1);
+        } else {
+          tma_load_5d(stage + G::B2, &tmap_b1, fb, 0, kcol, b_chunk0, (int)rank, (int)peer);
+          tma_load_5d(stage + G::BH, &tmap_bh, fb, 0, kcol, b_chunk0 + (int)rank, (int)rank, (int)rank);
+        }
       }
-      // Drain: no TMA write may land after teardown (bounded: a phase the
-      // other producer never armed gives up after the wait limit).
-#pragma unroll
-      for (int s = 0; s < kStages; ++s)
-        if (last_armed[s] >= 0) mbar_wait_drain(bar(G::FULL + s), (last_armed[s] / kStages) & 1u);
+      __syncwarp();
+    }
+    // Drain: no TMA write may land after teardown.  Every step this warp armed
+    // in the last kStages steps is waited for (bounded: a phase that never
+    // completes gives up after the wait limit).
+    if (lane == 0) {
+      const int first = p.num_chunks > kStages ? p.num_chunks - kStages : 0;
+      for (int c = producer; c < p.num_chunks; c += kProducers)
+        if (c >= first) mbar_wait_drain(bar(G::FULL + c % kStages), (c / kStages) & 1u);
+    }
+  } else if (warp == 3) {
+    // ------------------------------------------------------------ step hand-off
+    // Waits on the sums barriers of a group of kGroup steps and meets the MMA
+    // warp at named barrier 1 (ORing in the abort verdict), so the issuing
+    // thread itself never polls an mbarrier: that would stall it behind its
+    // queued MMAs and idle the tensor pipe.
+    for (int g0 = 0; g0 < p.num_chunks; g0 += kGroup) {
+      const int cnt = min(kGroup, p.num_chunks - g0);
+      bool waited = true;
+      for (int i = 0; i < cnt && waited; ++i) {
+        const int g = g0 + i;
+        waited = mbar_wait_hint(bar(G::SUMS + g % kStages), (g / kStages) & 1u, abort_flag, p.err, kErrWaitSums);
+      }
+      __syncwarp();  // bar.red is warp-aligned
+      if (named_bar_red_or(1, 64, !waited)) break;
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
-    if (lane == 0) {
-      const uint64_t a_d0 = umma_smem_desc(smem_base, kALbo, G::A_SBO, G::A_LAYOUT);
-      const uint64_t b_d0 = umma_smem_desc(smem_base, G::B_LBO, kBSbo, kLayoutSwizzle128B);
-      // Accumulators 0 and 1: one with A in shared memory, one from the A ring
-      // (CTA 0: M3 = a0 x B0 ss, M5 = ring0 x B1; CTA 1: M2 = ring0 x B0,
-      // M4 = a3 x B1 ss).  B tile of each accumulator per mode (see Geo).
-      const uint64_t ss_a = (uint64_t)((G::AOWN + (rank ? G::ATILE : 0)) >> 4);  // a0 or a3
-      int ss_bo, ts_bo;
-      if (kPreB) {
-        ss_bo = rank ? G::B1 : G::B0;
-        ts_bo = rank ? G::B0 : G::B1;
-      } else {
-        ss_bo = G::BSUM;               // b1-b3 or b2-b0
-        ts_bo = rank ? G::B0 : G::B1;  // b0 (own quadrant 0 of CTA 1) or b3 (own quadrant 1 of CTA 0)
-      }
-      const uint64_t ss_b = (uint64_t)(ss_bo >> 4), ts_b = (uint64_t)(ts_bo >> 4);
-      const uint64_t b2_b = (uint64_t)(G::B2 >> 4), bh_b = (uint64_t)(G::BH >> 4);
-      const uint32_t ss_d = tmem_base + (rank ? 128u : 0u);
-      const uint32_t ts_d = tmem_base + (rank ? 0u : 128u);
-      // One pass per 16-deep sub-step g: stage g / SUB, half h = g % SUB.  Within
-      // a stage, sub-step h starts 16 K columns in: +32 bytes along a K-major A
-      // row, +16 rows (2048 bytes) of an MN-major B tile.
-      int s = 0, h = 0;
-      uint32_t ph = 0;
-      for (int g = 0; g < p.num_chunks; ++g) {
-        if (!mbar_wait(bar(G::SUMS + s * G::SUB + h), ph, abort_flag, p.err, kErrWaitSums)) break;
+    // Accumulators (TMEM columns): 0 and 128 two full products, 256 the third,
+    // 384 the 64-column half of P1 (CTA 0: M3, M5, M7, M1L; CTA 1: M2, M4, M6,
+    // M1R).  A operand of each, by slot (after the sum warps): x0, x1, ARECV,
+    // ASUM -- CTA 0: a0, a0+a1, a1-a3, a0+a3; CTA 1: a2+a3, a3, a2-a0, a0+a3.
+    // B tiles: planes B0, B1, B2, BH; raw B: CTA 0 BSUM (b1-b3), B1 (b3),
+    // B2 (b2+b3), BH; CTA 1 B0 (b0), BSUM (b2-b0), B2 (b0+b1), BH.
+    const uint64_t a_d0 = umma_smem_desc(smem_base, kALbo, G::A_SBO, G::A_LAYOUT);
+    const uint64_t b_d0 = umma_smem_desc(smem_base, G::B_LBO, kBSbo, kLayoutSwizzle128B);
+    const uint64_t a0_o = (uint64_t)(G::AOWN >> 4), a1_o = (uint64_t)((G::AOWN + G::ATILE) >> 4);
+    const uint64_t a2_o = (uint64_t)(G::ARECV >> 4), a3_o = (uint64_t)(G::ASUM >> 4);
+    const int b0_bo = kPreB ? G::B0 : (rank ? G::B0 : G::BSUM);
+    const int b1_bo = kPreB ? G::B1 : (rank ? G::BSUM : G::B1);
+    const uint64_t b0_o = (uint64_t)(b0_bo >> 4), b1_o = (uint64_t)(b1_bo >> 4);
+    const uint64_t b2_o = (uint64_t)(G::B2 >> 4), bh_o = (uint64_t)(G::BH >> 4);
+    for (int g0 = 0; g0 < p.num_chunks; g0 += kGroup) {
+      __syncwarp();  // bar.red is warp-aligned
+      if (named_bar_red_or(1, 64, false)) break;
+      if (lane == 0) {
         tc_fence_after();
-        const uint64_t so = (uint64_t)((s * G::STAGE) >> 4);
-        const uint64_t ka = (uint64_t)(h * 2), kb = (uint64_t)(h * 128);
-        const uint32_t acc = g != 0 ? 1u : 0u;
-        const uint32_t ring = tmem_base + kRingCol0 + 32u * (uint32_t)(g & 1);
-        umma_bf16_ss(ss_d, a_d0 + so + ss_a + ka, b_d0 + so + ss_b + kb, kIdesc128, acc);
-        umma_bf16_ts(ts_d, ring + 0, b_d0 + so + ts_b + kb, kIdesc128, acc);
-        umma_bf16_ts(tmem_base + 256, ring + 8, b_d0 + so + b2_b + kb, kIdesc128, acc);
-        umma_bf16_ts(tmem_base + 384, ring + 16, b_d0 + so + bh_b + kb, kIdesc64, acc);
-        // The last sub-step of a stage frees the stage (and its ring half); an
-        // earlier one frees ring half 0 only.
-        if (h == G::SUB - 1) {
-          umma_commit(bar(G::EMPTY + s));
-        } else {
-          umma_commit(bar(G::RING0 + s));
-        }
-        if (++h == G::SUB) {
-          h = 0;
-          if (++s == kStages) {
-            s = 0;
-            ph ^= 1u;
-          }
+        const int cnt = min(kGroup, p.num_chunks - g0);
+        for (int i = 0; i < cnt; ++i) {
+          const int g = g0 + i;
+          const int s = g % kStages;
+          const uint64_t so = (uint64_t)((s * G::STAGE) >> 4);
+          const uint32_t acc = g != 0 ? 1u : 0u;
+          umma_bf16_ss(tmem_base + 0, a_d0 + so + a0_o, b_d0 + so + b0_o, kIdesc128, acc);
+          umma_bf16_ss(tmem_base + 128, a_d0 + so + a1_o, b_d0 + so + b1_o, kIdesc128, acc);
+          umma_bf16_ss(tmem_base + 256, a_d0 + so + a2_o, b_d0 + so + b2_o, kIdesc128, acc);
+          umma_bf16_ss(tmem_base + 384, a_d0 + so + a3_o, b_d0 + so + bh_o, kIdesc64, acc);
+          umma_commit(bar(G::EMPTY + s));  // frees the stage once these MMAs have read it
         }
       }
-      // Always commit: the epilogue (or the teardown drain) waits on it.
-      umma_commit(bar(G::ACC));
     }
-  } else if (warp >= kFirstSumWarp) {
+    // Always commit: the epilogue (or the teardown drain) waits on it.
+    if (lane == 0) umma_commit(bar(G::ACC));
+    __syncwarp();
+  } else if (warp >= kFirstSumWarp && warp < kFirstSumWarp + kSumWarps) {
     // ------------------------------------------------------------ operand sums
     const int set = (warp - kFirstSumWarp) >> 2;
     const int q = warp & 3;
-    const uint32_t row = 32 * q + lane;  // product row = TMEM lane; also the B chunk index
-    // The two 16-byte chunks of this row's 16-deep slice in a swizzled A tile.
-    // 32-byte rows (KD = 16): the chunks swap on row bit 2.  64-byte rows
-    // (KD = 32): chunk j sits at j ^ ((row >> 1) & 3); a set always takes the
-    // same half h = set of a stage, so its offsets are fixed.
-    uint32_t lo_off, hi_off;
-    if constexpr (G::KD == 32) {
-      const uint32_t sw = (row >> 1) & 3u;
-      lo_off = 64 * row + 16 * ((2u * set) ^ sw);
-      hi_off = 64 * row + 16 * ((2u * set + 1u) ^ sw);
-    } else {
-      const uint32_t sw = (row >> 2) & 1u;
-      lo_off = 32 * row + 16 * sw;
-      hi_off = 32 * row + 16 * (sw ^ 1u);
-    }
-    const uint32_t tmem_lane = tmem_base + ((uint32_t)(32 * q) << 16) + kRingCol0;
+    const uint32_t row = 32 * q + lane;  // 0..127 within the set
+    // The A operand tiles of a stage share one layout (same swizzle, same row
+    // order), so the sums are elementwise over byte offsets: thread `row` takes
+    // the 16-byte chunks row and row + 128 of each tile, a warp reading 512
+    // contiguous bytes per load (no bank conflicts).
+    const uint32_t lo_off = 16 * row;
+    const uint32_t hi_off = 16 * row + 2048;
     const uint32_t o1 = 16 * row, o2 = o1 + G::BHALF;
-    // Sub-steps g = set, set + 2, ...: stage g / SUB, half g % SUB.
+    // Steps g = set, set + 2, ...
     for (int g = set; g < p.num_chunks; g += 2) {
-      const int stage_i = g / G::SUB, h = g % G::SUB;
-      const int s = stage_i % kStages;
+      const int s = g % kStages;
       if (!__all_sync(0xffffffffu,
-                      mbar_wait(bar(G::FULL + s), (stage_i / kStages) & 1u, abort_flag, p.err, kErrWaitRaw))) {
+                      mbar_wait_hint(bar(G::FULL + s), (g / kStages) & 1u, abort_flag, p.err, kErrWaitRaw))) {
         ok = false;
         break;
       }
       const uint32_t st = smem_base + s * G::STAGE;
       // A: x0, x1 = quadrants (r, 0), (r, 1); x2 = the third quadrant.
-      const uint4 x0l = lds128(st + G::AOWN + lo_off), x0h = lds128(st + G::AOWN + hi_off);
-      const uint4 x1l = lds128(st + G::AOWN + G::ATILE + lo_off), x1h = lds128(st + G::AOWN + G::ATILE + hi_off);
-      const uint4 x2l = lds128(st + G::ARECV + lo_off), x2h = lds128(st + G::ARECV + hi_off);
-      uint4 r0l, r0h, r1l, r1h, r2l, r2h;
-      r0l = add4(x0l, x1l);  // CTA 0: a0+a1   CTA 1: a2+a3
-      r0h = add4(x0h, x1h);
+      const uint32_t x0a = st + G::AOWN, x1a = st + G::AOWN + G::ATILE, x2a = st + G::ARECV, xsa = st + G::ASUM;
+      const uint4 x0l = lds128(x0a + lo_off), x0h = lds128(x0a + hi_off);
+      const uint4 x1l = lds128(x1a + lo_off), x1h = lds128(x1a + hi_off);
+      const uint4 x2l = lds128(x2a + lo_off), x2h = lds128(x2a + hi_off);
       if (rank == 0) {
-        r1l = sub4(x1l, x2l); r1h = sub4(x1h, x2h);  // a1-a3
-        r2l = add4(x0l, x2l); r2h = add4(x0h, x2h);  // a0+a3
+        sts128(x1a + lo_off, add4(x0l, x1l));  // a0+a1 over a1
+        sts128(x1a + hi_off, add4(x0h, x1h));
+        sts128(x2a + lo_off, sub4(x1l, x2l));  // a1-a3 over a3
+        sts128(x2a + hi_off, sub4(x1h, x2h));
+        sts128(xsa + lo_off, add4(x0l, x2l));  // a0+a3
+        sts128(xsa + hi_off, add4(x0h, x2h));
       } else {
-        r1l = sub4(x0l, x2l); r1h = sub4(x0h, x2h);  // a2-a0
-        r2l = add4(x1l, x2l); r2h = add4(x1h, x2h);  // a3+a0
+        sts128(x0a + lo_off, add4(x0l, x1l));  // a2+a3 over a2
+        sts128(x0a + hi_off, add4(x0h, x1h));
+        sts128(x2a + lo_off, sub4(x0l, x2l));  // a2-a0 over a0
+        sts128(x2a + hi_off, sub4(x0h, x2h));
+        sts128(xsa + lo_off, add4(x1l, x2l));  // a3+a0
+        sts128(xsa + hi_off, add4(x1h, x2h));
       }
       if constexpr (!kPreB) {
         // B: d, e = own quadrants (0, 1-r), (1, 1-r); f = the other full quadrant, h = P1's half.
@@ -386,28 +395,11 @@ __global__ void __launch_bounds__(kThreads, 1)
           sts128(st + G::B2 + o2, add4(d2, f2));
           sts128(st + G::BH + o1, add4(d2, h1));    // (b0 + b3) right chunk
         }
-        fence_proxy_async_smem();
       }
-      // Ring half g & 1 is free once the MMAs of sub-step g - 2 completed: the
-      // stage commit if that was its stage's last sub-step, else RING0.
-      if (g >= 2) {
-        const int ps = (g - 2) / G::SUB, ph_ = (g - 2) % G::SUB;
-        const uint32_t free_bar = bar((ph_ == G::SUB - 1 ? G::EMPTY : G::RING0) + ps % kStages);
-        const bool waited = mbar_wait(free_bar, (ps / kStages) & 1u, abort_flag, p.err, kErrWaitEmpty);
-        if (!__all_sync(0xffffffffu, waited)) {
-          ok = false;
-          break;
-        }
-      }
-      tc_fence_after();
-      const uint32_t ring = tmem_lane + 32u * (uint32_t)(g & 1);
-      tmem_store_8(ring + 0, r0l, r0h);
-      tmem_store_8(ring + 8, r1l, r1h);
-      tmem_store_8(ring + 16, r2l, r2h);
-      tmem_store_wait();
-      tc_fence_before();
+      // Make the generic-proxy writes visible to the tensor core, then signal.
+      fence_proxy_async_smem();
       __syncwarp();
-      if (lane == 0) mbar_arrive(bar(G::SUMS + s * G::SUB + h));
+      if (lane == 0) mbar_arrive(bar(G::SUMS + s));
     }
 
     // ------------------------------------------------------------ epilogue

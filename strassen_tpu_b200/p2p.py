@@ -73,6 +73,15 @@ class PeerReduce:
             raise ValueError(f"at most {_native.P2P_MAX_RANKS} ranks, got {self.world}")
         self.device = torch.device(device)
         self.rows, self.cols, self.blocks = rows, cols, blocks
+        if self.world > 1:
+            # CTA b of one rank meets CTA b of every other rank at the flag
+            # barriers, so the ranks must launch the same grid over the same
+            # bounds; a mismatch would surface only as 2 s barrier timeouts.
+            config = (rows, cols, blocks)
+            configs = [None] * self.world
+            self.dist.all_gather_object(configs, config, group=group)
+            if any(tuple(c) != config for c in configs):
+                raise ValueError(f"PeerReduce (rows, cols, blocks) differ across ranks: {configs}")
         self.lib = _native.load()
         self._own: list[int] = []
         self._opened: list[int] = []

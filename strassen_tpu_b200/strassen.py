@@ -21,6 +21,8 @@ Tensors are ``torch.Tensor`` on a CUDA B200 device.  There is no CPU path:
 
 from __future__ import annotations
 
+from typing import NamedTuple
+
 import ctypes
 
 import torch
@@ -536,15 +538,28 @@ def classical_matmul(a, b, *, bm=TUNED_BM, bn=TUNED_BN, bk=TUNED_BK, output_dtyp
     return out
 
 
+class StrassenBOperands(NamedTuple):
+    """B operand planes and the tile they were formed for.
+
+    ``planes`` is ``[7, K/2, N/2]`` bf16; plane i at (kappa, u) belongs to block
+    (kappa // (bk/2), u // (bn/2)), so the planes are only valid for a GEMM with
+    the same ``bn`` and ``bk`` -- :func:`pair_matmul` checks this.
+    """
+    planes: torch.Tensor
+    bn: int
+    bk: int
+
+
 def strassen_b_operands(b, *, bn=TUNED_BN, bk=TUNED_BK, out=None):
     """The seven B operands of every Strassen block of ``b`` for the tile (bn, bk).
 
-    Returns ``[7, K/2, N/2]`` bf16 planes in the order P3 (b1-b3), P5 (b3),
-    P7 (b2+b3), P1 (b0+b3), P2 (b0), P4 (b2-b0), P6 (b0+b1): the reference's B
-    pre-adds (strassen_pallas.py:324-379), each rounded once to bf16.  Pass them
-    to :func:`pair_matmul` as ``b_operands=`` with the same ``bn`` and ``bk``.
-    For a weight reused across calls this is an offline relayout, like
-    :func:`swiglu_weight_layout`.
+    Returns a :class:`StrassenBOperands` whose ``planes`` are ``[7, K/2, N/2]``
+    bf16 in the order P3 (b1-b3), P5 (b3), P7 (b2+b3), P1 (b0+b3), P2 (b0),
+    P4 (b2-b0), P6 (b0+b1): the reference's B pre-adds
+    (strassen_pallas.py:324-379), each rounded once to bf16.  Pass it to
+    :func:`pair_matmul` as ``b_operands=``; the tile must match.  For a weight
+    reused across calls this is an offline relayout, like
+    :func:`swiglu_weight_layout`.  ``out``: a preallocated planes tensor.
     """
     if b.ndim != 2 or b.dtype != torch.bfloat16:
         raise ValueError("strassen_b_operands expects a rank-2 BF16 matrix")
@@ -562,7 +577,7 @@ def strassen_b_operands(b, *, bn=TUNED_BN, bk=TUNED_BK, out=None):
         status = lib.sb_strassen_b_operands(_stream_handle(b.device), b.data_ptr(), out.data_ptr(), k, n,
                                             _ld(b), bn, bk)
     _native.check(status)
-    return out
+    return StrassenBOperands(out, int(bn), int(bk))
 
 
 def pair_matmul(a, b, *, bm=TUNED_BM, bn=TUNED_BN, bk=TUNED_BK, output_dtype=None, out=None,
@@ -573,15 +588,22 @@ def pair_matmul(a, b, *, bm=TUNED_BM, bn=TUNED_BN, bk=TUNED_BK, output_dtype=Non
     operand pairing as strassen_pallas.py:156-880; the recombination's fp32
     order differs from :func:`strassen_matmul`.
 
-    ``b_operands``: B's operand planes from :func:`strassen_b_operands` (built
-    with the same bn, bk); then ``b`` may be None and the kernel forms no B sums
-    (``sb_strassen_gemm_pair_planes``; bit-identical to the raw-B call).
+    ``b_operands``: B's :class:`StrassenBOperands` from :func:`strassen_b_operands`,
+    formed for the same bn, bk; then ``b`` may be None and the kernel forms no B
+    sums (``sb_strassen_gemm_pair_planes``; bit-identical to the raw-B call).
     """
     if b_operands is not None:
-        if b_operands.ndim != 3 or b_operands.shape[0] != 7 or b_operands.dtype != torch.bfloat16 \
-                or not b_operands.is_contiguous():
-            raise ValueError("b_operands must be the contiguous [7, K/2, N/2] bf16 planes of strassen_b_operands")
-        kb, nb = 2 * b_operands.shape[1], 2 * b_operands.shape[2]
+        if not isinstance(b_operands, StrassenBOperands):
+            raise ValueError("b_operands must be the StrassenBOperands returned by strassen_b_operands "
+                             "(the planes' layout depends on the tile they were formed for)")
+        if (b_operands.bn, b_operands.bk) != (bn, bk):
+            raise ValueError(f"b_operands were formed for bn={b_operands.bn}, bk={b_operands.bk}; "
+                             f"this call uses bn={bn}, bk={bk}")
+        planes = b_operands.planes
+        if planes.ndim != 3 or planes.shape[0] != 7 or planes.dtype != torch.bfloat16 \
+                or not planes.is_contiguous():
+            raise ValueError("b_operands must hold the contiguous [7, K/2, N/2] bf16 planes of strassen_b_operands")
+        kb, nb = 2 * planes.shape[1], 2 * planes.shape[2]
         if b is not None and tuple(b.shape) != (kb, nb):
             raise ValueError(f"b_operands describe a {kb}x{nb} B, b is {tuple(b.shape)}")
     if a.ndim != 2 or (b is not None and b.ndim != 2):
@@ -607,7 +629,7 @@ def pair_matmul(a, b, *, bm=TUNED_BM, bn=TUNED_BN, bk=TUNED_BK, output_dtype=Non
     od = SB_F32 if out_dt == torch.float32 else SB_BF16
     with torch.cuda.device(device):
         if b_operands is not None:
-            status = lib.sb_strassen_gemm_pair_planes(_stream_handle(device), a.data_ptr(), b_operands.data_ptr(),
+            status = lib.sb_strassen_gemm_pair_planes(_stream_handle(device), a.data_ptr(), planes.data_ptr(),
                                                       out.data_ptr(), m, n, k, _ld(a), _ld(out), bm, bn, bk, od)
         else:
             b = _rowmajor(b)

@@ -167,14 +167,21 @@ def test_pair_matmul_value_errors(kw, match):
 
 def test_pair_matmul_checks_the_operand_planes():
     a = torch.zeros(256, 512, dtype=BF)
+    ops = lambda t, bn=256, bk=256: sb.StrassenBOperands(t, bn, bk)
+    with pytest.raises(ValueError, match="StrassenBOperands returned by strassen_b_operands"):
+        sb.pair_matmul(a, None, b_operands=torch.zeros(7, 256, 128, dtype=BF), bm=256, bn=256, bk=256)
     with pytest.raises(ValueError, match=r"\[7, K/2, N/2\] bf16 planes"):
-        sb.pair_matmul(a, None, b_operands=torch.zeros(6, 256, 128, dtype=BF), bm=256, bn=256, bk=256)
+        sb.pair_matmul(a, None, b_operands=ops(torch.zeros(6, 256, 128, dtype=BF)), bm=256, bn=256, bk=256)
     with pytest.raises(ValueError, match="describe a 512x256 B, b is"):
-        sb.pair_matmul(a, torch.zeros(512, 512, dtype=BF), b_operands=torch.zeros(7, 256, 128, dtype=BF),
+        sb.pair_matmul(a, torch.zeros(512, 512, dtype=BF), b_operands=ops(torch.zeros(7, 256, 128, dtype=BF)),
+                       bm=256, bn=256, bk=256)
+    # Planes formed for another tile are refused: their layout would silently give a wrong product.
+    with pytest.raises(ValueError, match="formed for bn=256, bk=512; this call uses bn=256, bk=256"):
+        sb.pair_matmul(a, None, b_operands=ops(torch.zeros(7, 256, 128, dtype=BF), 256, 512),
                        bm=256, bn=256, bk=256)
     # Planes of a 512x256 B: shapes agree, so only the device check is left.
     with pytest.raises(ValueError, match="runs on a CUDA device"):
-        sb.pair_matmul(a, None, b_operands=torch.zeros(7, 256, 128, dtype=BF), bm=256, bn=256, bk=256)
+        sb.pair_matmul(a, None, b_operands=ops(torch.zeros(7, 256, 128, dtype=BF)), bm=256, bn=256, bk=256)
 
 
 def test_strassen_b_operands_refuses_host_tensors_and_other_dtypes():

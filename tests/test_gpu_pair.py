@@ -130,7 +130,7 @@ def test_b_operand_planes_are_the_reference_pre_adds():
     import strassen_tpu_b200 as sb
     k, n, bn, bk = 1024, 1536, 512, 512
     b = ref.normal_bf16((k, n), 31)
-    got = sb.strassen_b_operands(dev_bf16(b), bn=bn, bk=bk).float().cpu().numpy()
+    got = sb.strassen_b_operands(dev_bf16(b), bn=bn, bk=bk).planes.float().cpu().numpy()
     hbn, hbk = bn // 2, bk // 2
     blocks = b.reshape(k // bk, 2, hbk, n // bn, 2, hbn)  # [P, qk, k', J, qc, c']
     q = lambda qk, qc: blocks[:, qk, :, :, qc, :].reshape(k // 2, n // 2)

@@ -155,3 +155,16 @@ def test_lhs_transposed_oracle_matches_reference(golden_lhs_t):
                                               else "bfloat16", **c["kwargs"])
         want = golden_output(c, arrays[name])
         np.testing.assert_array_equal(got[::c["row_stride"]], want, err_msg=name)
+
+
+def test_row_sampling_reproduces_block_rows():
+    """Output row I*bm + r' pairs only with row I*bm + bm/2 + r' (the A quadrant
+    split), so running the oracle on just those A rows with bm = 2 * rows gives
+    the same values: the basis of the full-size sweep parity tests."""
+    m, k, n, bm, bn, bk = 1024, 512, 512, 512, 256, 256
+    a = ref.normal_bf16((m, k), 71)
+    b = ref.normal_bf16((k, n), 72)
+    full = ref.strassen_matmul_ref(a, b, bm=bm, bn=bn, bk=bk, output_dtype="float32")
+    rows = np.concatenate([np.arange(base, base + 16) for base in (0, bm // 2, 512, 512 + bm // 2)])
+    sub = ref.strassen_matmul_ref(a[rows], b, bm=32, bn=bn, bk=bk, output_dtype="float32")
+    np.testing.assert_allclose(sub, full[rows], rtol=1e-6, atol=1e-6)

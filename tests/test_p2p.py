@@ -157,3 +157,35 @@ def test_single_rank_forward_is_the_same_for_either_collective():
     a = qwen3.Qwen3Prefill(cfg, qwen3.TensorParallel(), "cpu", backend="native", layers=2)
     b = qwen3.Qwen3Prefill(cfg, qwen3.TensorParallel(collective="p2p"), "cpu", backend="native", layers=2)
     assert torch.equal(a.forward(tokens), b.forward(tokens))
+
+
+def _mismatch_worker(rank, world, port, out_dir):
+    import os
+    from datetime import timedelta
+    import torch.distributed as dist
+    from strassen_tpu_b200.p2p import PeerReduce
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=30))
+    try:
+        try:
+            PeerReduce(64, 64, "cpu", blocks=16 * (rank + 1))  # ranks disagree on the grid
+            msg = "no error"
+        except ValueError as exc:
+            msg = str(exc)
+        with open(os.path.join(out_dir, f"rank{rank}.txt"), "w") as f:
+            f.write(msg)
+    finally:
+        dist.destroy_process_group()
+
+
+def test_peer_reduce_ranks_must_agree_on_grid(tmp_path):
+    """Every rank learns of a (rows, cols, blocks) mismatch and raises before any
+    buffer is allocated (world size 2, gloo, CPU)."""
+    import socket
+    import torch.multiprocessing as mp
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    mp.spawn(_mismatch_worker, args=(2, port, str(tmp_path)), nprocs=2, join=True)
+    for r in range(2):
+        assert "differ across ranks" in (tmp_path / f"rank{r}.txt").read_text()

@@ -89,3 +89,31 @@ def test_noalloc_refuses_problems_beyond_its_scratch():
     scale = torch.ones(n, dtype=torch.bfloat16, device="cuda")
     with pytest.raises(_native.StrassenError, match="exceeds the no-allocation scratch capacity"):
         _noalloc(a, b, residual, scale)
+
+
+def test_noalloc_at_exact_capacity_and_one_row_tile_over():
+    """M*N equal to the array's 8,388,608 fp32 values uses its last rows and is
+    accepted (matching the workspace entry point); one more 256-row tile is
+    refused before any launch."""
+    import strassen_tpu_b200 as sb
+    from strassen_tpu_b200 import _native
+    m, k, n = 2048, 256, 4096  # m * n == 8,388,608
+    a = _dev(ref.normal_bf16((m, k), 906))
+    b = _dev(ref.normal_bf16((k, n), 907))
+    residual = _dev(ref.normal_bf16((m, n), 908))
+    scale = _dev(ref.bf16_round(1.0 + 0.02 * ref.normal_bf16((n,), 909)))
+    got = _noalloc(a, b, residual, scale)
+    want = sb.strassen_matmul(a, b, bm=256, bn=n, bk=256, epilogue="norm_residual_add",
+                              residual=residual, norm_scale=scale)
+    torch.cuda.synchronize()
+    g = got.float().cpu().numpy().astype(np.float64)
+    w = want.float().cpu().numpy().astype(np.float64)
+    rms = np.sqrt(np.mean(w ** 2))
+    assert np.isfinite(g).all()
+    assert np.abs(g - w).max() <= MAX_ABS_REL_RMS * rms
+    assert _native.device_status() == 0
+    m_over = m + 256
+    a2 = torch.zeros(m_over, k, dtype=torch.bfloat16, device="cuda")
+    r2 = torch.zeros(m_over, n, dtype=torch.bfloat16, device="cuda")
+    with pytest.raises(_native.StrassenError, match="exceeds the no-allocation scratch capacity"):
+        _noalloc(a2, b, r2, scale)
