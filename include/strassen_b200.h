@@ -202,6 +202,26 @@ SB_API int sb_strassen_gemm_pair_planes(sb_stream_t stream,
                                         int32_t bm, int32_t bn, int32_t bk, int32_t out_dtype);
 
 /*
+ * sb_strassen_gemm_quad -- C = A·B, no epilogue, on the four-CTA kernel:
+ * clusters of two CTA pairs (tcgen05 cta_group::2, M = 256) per 256 x 128
+ * product tile, each pair 3.5 of the seven products.  Replaces
+ * strassen_pallas.strassen_matmul(a, b, bm=, bn=, bk=, output_dtype=) without
+ * an epilogue (strassen_pallas.py:882-1221); same operand pairing and
+ * rounding, recombination in a different fp32 order.  The call forms A's
+ * operands (a pass over A) and B's operand planes (sb_strassen_b_operands) in
+ * `workspace` (sb_quad_workspace_bytes(m, n, k) bytes, 16-byte aligned) and
+ * then runs the GEMM, all on `stream`.  Needs M % 512 == 0, bn % 256 == 0 and
+ * bk % 256 == 0 (SB_ERR_TILING otherwise).
+ */
+SB_API size_t sb_quad_workspace_bytes(int64_t m, int64_t n, int64_t k);
+SB_API int sb_strassen_gemm_quad(sb_stream_t stream,
+                                 const void* a, const void* b, void* c,
+                                 int64_t m, int64_t n, int64_t k,
+                                 int64_t lda, int64_t ldb, int64_t ldc,
+                                 int32_t bm, int32_t bn, int32_t bk, int32_t out_dtype,
+                                 void* workspace, size_t workspace_bytes);
+
+/*
  * sb_strassen_gemm_norm_residual_noalloc -- the norm_residual_add epilogue of
  * sb_strassen_gemm, with its fp32 scratch in a device array built into the
  * library instead of a caller workspace.  No counterpart in the reference.

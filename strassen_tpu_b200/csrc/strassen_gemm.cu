@@ -1048,6 +1048,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 
 // The two-CTA product-split kernel (sb_strassen_gemm_pair).
 #include "strassen_pair.cuh"
+// The four-CTA kernel on CTA pairs (sb_strassen_gemm_quad).
+#include "strassen_quad.cuh"
 
 // Failure-detection self-test (sb_wait_selftest): warp 0 waits on a barrier
 // nobody arrives on and gives up after the bounded-wait limit, raising the abort
@@ -1587,6 +1589,139 @@ int run_pair(cudaStream_t stream, const void* a, const void* b, const void* b_pl
   return out_dtype == SB_F32 ? launch_pair<true, false>(stream, maps, p) : launch_pair<false, false>(stream, maps, p);
 }
 
+// Tensor maps of the four-CTA kernel (strassen_quad.cuh):
+//   a:  the A operand array [M/2][4K] of a_operand_pass_kernel, 2-D, box {64, 128},
+//       128-byte swizzle (one 128-byte row = a pair's four operands, 16 deep);
+//   b:  the B operand planes [7][K/2][N/2] as dims (column in a 64-column
+//       chunk, kappa, chunk, plane), box {64, 16, 1, 3}, 128-byte swizzle;
+//   bh: the planes as dims (column, kappa, plane), box {32, 16, 1}, 64-byte
+//       swizzle (a CTA's 32 columns of P1's half tile).
+struct QuadMaps {
+  CUtensorMap a, b, bh;
+};
+
+int make_quad_maps(const void* ops, const void* planes, int64_t m, int64_t n, int64_t k, QuadMaps* maps) {
+  EncodeTiledFn enc = encode_fn();
+  if (!enc) return fail(SB_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  auto encode = [&](CUtensorMap* map, const void* base, cuuint32_t rank, const cuuint64_t* dims,
+                    const cuuint64_t* strides, const cuuint32_t* box, CUtensorMapSwizzle sw,
+                    const char* what) -> int {
+    CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, rank, const_cast<void*>(base), dims, strides, box,
+                     estr, CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS)
+      return fail(SB_ERR_CUDA, std::string("cuTensorMapEncodeTiled(") + what + ") failed: " + std::to_string((int)r));
+    return SB_OK;
+  };
+  const int64_t kh = k / 2, nh = n / 2;
+  {
+    cuuint64_t dims[2] = {(cuuint64_t)(4 * k), (cuuint64_t)(m / 2)};
+    cuuint64_t strides[1] = {(cuuint64_t)(4 * k * 2)};
+    cuuint32_t box[2] = {64, 128};
+    int st = encode(&maps->a, ops, 2, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B, "A operands, quad");
+    if (st != SB_OK) return st;
+  }
+  {
+    cuuint64_t dims[4] = {64, (cuuint64_t)kh, (cuuint64_t)(nh / 64), 7};
+    cuuint64_t strides[3] = {(cuuint64_t)(nh * 2), 128, (cuuint64_t)(kh * nh * 2)};
+    cuuint32_t box[4] = {64, 16, 1, 3};
+    int st = encode(&maps->b, planes, 4, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B, "B planes, quad");
+    if (st != SB_OK) return st;
+  }
+  cuuint64_t dims[3] = {(cuuint64_t)nh, (cuuint64_t)kh, 7};
+  cuuint64_t strides[2] = {(cuuint64_t)(nh * 2), (cuuint64_t)(kh * nh * 2)};
+  cuuint32_t box[3] = {32, 16, 1};
+  return encode(&maps->bh, planes, 3, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_64B, "B plane half, quad");
+}
+
+// Launches the four-CTA kernel: clusters of four consecutive CTAs (two CTA
+// pairs), one cluster per 256 x 128 product tile.
+template <bool kOutF32>
+int launch_quad(cudaStream_t stream, const QuadMaps& m, const GemmParams& p) {
+  auto kernel = strassen_quad_kernel<kOutF32>;
+  constexpr int kSmem = quad::Geo::SMEM;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64)
+    return fail(SB_ERR_DEVICE, "no usable current device");
+  static std::once_flag once[64];
+  static cudaError_t attr_err[64];
+  std::call_once(once[dev], [&]() {
+    attr_err[dev] = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
+  });
+  if (attr_err[dev] != cudaSuccess)
+    return fail(SB_ERR_CUDA, std::string("cudaFuncSetAttribute: ") + cudaGetErrorString(attr_err[dev]));
+  cudaLaunchConfig_t cfg;
+  std::memset(&cfg, 0, sizeof(cfg));
+  cfg.gridDim = dim3((unsigned)(4 * p.tiles_m * p.tiles_n), 1, 1);
+  cfg.blockDim = dim3(quad::kThreadsQ, 1, 1);
+  cfg.dynamicSmemBytes = kSmem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 4;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, m.a, m.b, m.bh, p);
+  if (e != cudaSuccess) return fail(SB_ERR_CUDA, std::string("quad kernel launch: ") + cudaGetErrorString(e));
+  return SB_OK;
+}
+
+// Bytes of the A operand array and of the B planes the four-CTA path forms.
+size_t quad_ops_bytes(int64_t m, int64_t k) { return (size_t)(m / 2) * (size_t)(4 * k) * 2u; }
+size_t quad_planes_bytes(int64_t k, int64_t n) { return (size_t)7 * (size_t)(k / 2) * (size_t)(n / 2) * 2u; }
+
+// Shape rules of the four-CTA kernel beyond validate_core: 256-row product
+// tiles (M % 512), 128-column product tiles inside one block half (bn % 256),
+// the B planes' tile rule (bk % 256).
+int check_quad_shape(int64_t m, int32_t bn, int32_t bk) {
+  if (m % 512)
+    return fail(SB_ERR_TILING, "the four-CTA kernel needs M divisible by 512 (256-row product tiles), got M=" +
+                                   std::to_string(m));
+  if (bn % 256 || bk % 256) return fail(SB_ERR_TILING, "the four-CTA kernel needs bn and bk multiples of 256");
+  return SB_OK;
+}
+
+// A operand pass, B planes (unless given) and the GEMM, in stream order.
+int run_quad(cudaStream_t stream, const void* a, const void* b, const void* b_planes, void* c, int64_t m,
+             int64_t n, int64_t k, int64_t lda, int64_t ldb, int64_t ldc, int32_t bm, int32_t bn, int32_t bk,
+             int32_t out_dtype, void* workspace, size_t workspace_bytes) {
+  if (ldc < n) return fail(SB_ERR_ALIGNMENT, "ldc must be >= N");
+  int st = check_quad_shape(m, bn, bk);
+  if (st != SB_OK) return st;
+  const size_t need = quad_ops_bytes(m, k) + (b_planes ? 0 : quad_planes_bytes(k, n));
+  if (!workspace || workspace_bytes < need)
+    return fail(SB_ERR_WORKSPACE, "the four-CTA path needs a workspace of " + std::to_string(need) +
+                                      " bytes (sb_quad_workspace_bytes), got " + std::to_string(workspace_bytes));
+  if (!aligned16(workspace)) return fail(SB_ERR_ALIGNMENT, "workspace must be 16-byte aligned");
+  st = check_device();
+  if (st != SB_OK) return st;
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  __nv_bfloat16* ops = reinterpret_cast<__nv_bfloat16*>(ws);
+  const void* planes = b_planes;
+  if (!planes) {
+    void* pl = ws + quad_ops_bytes(m, k);
+    st = sb_strassen_b_operands(reinterpret_cast<sb_stream_t>(stream), b, pl, k, n, ldb, bn, bk);
+    if (st != SB_OK) return st;
+    planes = pl;
+  }
+  const int64_t items = (m / 2) * (k / 16);
+  const unsigned grid = (unsigned)std::min<int64_t>((items + 255) / 256, 148 * 16);
+  a_operand_pass_kernel<<<grid, 256, 0, stream>>>(reinterpret_cast<const __nv_bfloat16*>(a), lda, (int32_t)m,
+                                                  (int32_t)k, bm, bk, ops);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return fail(SB_ERR_CUDA, std::string("A operand pass launch: ") + cudaGetErrorString(e));
+  QuadMaps maps;
+  st = make_quad_maps(ops, planes, m, n, k, &maps);
+  if (st != SB_OK) return st;
+  GemmParams p = base_params(m, n, k, bm, bn, bk, c, ldc, 16);
+  p.tiles_m = (int32_t)(p.Mp / quad::kTileRows);
+  p.tiles_n = (int32_t)(p.Np / quad::kCols);
+  return out_dtype == SB_F32 ? launch_quad<true>(stream, maps, p) : launch_quad<false>(stream, maps, p);
+}
+
 void apply_options(GemmParams& p, int formula, int perm, const int32_t* schedule) {
   p.formula = formula == SB_FORMULA_DUAL ? 1 : formula == SB_FORMULA_POWERS ? 2 : 0;
   p.swap_m = perm & 1;
@@ -1973,6 +2108,20 @@ int sb_wait_selftest(sb_stream_t stream) {
   e = cudaGetLastError();
   if (e != cudaSuccess) return fail(SB_ERR_CUDA, std::string("selftest launch: ") + cudaGetErrorString(e));
   return SB_OK;
+}
+
+size_t sb_quad_workspace_bytes(int64_t m, int64_t n, int64_t k) {
+  if (m <= 0 || n <= 0 || k <= 0) return 0;
+  return quad_ops_bytes(m, k) + quad_planes_bytes(k, n);
+}
+
+int sb_strassen_gemm_quad(sb_stream_t stream_, const void* a, const void* b, void* c, int64_t m, int64_t n,
+                          int64_t k, int64_t lda, int64_t ldb, int64_t ldc, int32_t bm, int32_t bn, int32_t bk,
+                          int32_t out_dtype, void* workspace, size_t workspace_bytes) {
+  int st = validate_core(a, b, c, m, n, k, lda, ldb, ldc, bm, bn, bk, out_dtype);
+  if (st != SB_OK) return st;
+  return run_quad(reinterpret_cast<cudaStream_t>(stream_), a, b, nullptr, c, m, n, k, lda, ldb, ldc, bm, bn, bk,
+                  out_dtype, workspace, workspace_bytes);
 }
 
 const char* sb_version(void) { return "strassen_b200 0.1.0 (sm_100a, tcgen05)"; }

@@ -639,6 +639,57 @@ def pair_matmul(a, b, *, bm=TUNED_BM, bn=TUNED_BN, bk=TUNED_BK, output_dtype=Non
     return out
 
 
+def quad_matmul(a, b, *, bm=TUNED_BM, bn=TUNED_BN, bk=TUNED_BK, output_dtype=None, out=None, workspace=None):
+    """``strassen_matmul(a, b, bm=, bn=, bk=, output_dtype=)`` without an epilogue,
+    on the four-CTA kernel (``sb_strassen_gemm_quad``): clusters of two CTA
+    pairs on B200's paired tensor cores (tcgen05 ``cta_group::2``), one
+    256 x 128 product tile per cluster, each pair 3.5 of the seven products.
+    Same algorithm and operand pairing as strassen_pallas.py:156-880; the
+    recombination's fp32 order differs from :func:`strassen_matmul`.
+
+    The call forms A's operands and B's operand planes in a workspace (the
+    ``sb_quad_workspace_bytes`` of the shape; allocated here unless
+    ``workspace=`` passes a uint8 CUDA tensor at least that large) before the
+    GEMM, all on the current stream.  Needs M % 512 == 0, bn % 256 == 0 and
+    bk % 256 == 0.
+    """
+    if a.ndim != 2 or b.ndim != 2:
+        raise ValueError("quad_matmul expects two rank-2 matrices")
+    m, k = a.shape
+    k2, n = b.shape
+    if k != k2:
+        raise ValueError(f"inner dimensions disagree: {k} vs {k2}")
+    if a.dtype != torch.bfloat16 or b.dtype != torch.bfloat16:
+        raise ValueError("inputs must be BF16")
+    for name, dimension, block in (("M", m, bm), ("N", n, bn), ("K", k, bk)):
+        if dimension % block:
+            raise ValueError(f"{name}={dimension} is not divisible by {block}")
+    check_tiling(bm, bn, bk)
+    if m % 512 or bn % 256 or bk % 256:
+        raise ValueError("the four-CTA kernel needs M % 512 == 0, bn % 256 == 0 and bk % 256 == 0")
+    if a.device.type != "cuda" or b.device.type != "cuda":
+        raise ValueError("quad_matmul runs on a CUDA device (no CPU fallback)")
+    out_dt = _as_torch_dtype(output_dtype) or torch.bfloat16
+    device = a.device
+    a = _rowmajor(a)
+    b = _rowmajor(b)
+    if out is None:
+        out = torch.empty((m, n), dtype=out_dt, device=device)
+    lib = _native.load()
+    need = int(lib.sb_quad_workspace_bytes(m, n, k))
+    if workspace is None:
+        workspace = torch.empty(need, dtype=torch.uint8, device=device)
+    elif workspace.dtype != torch.uint8 or workspace.numel() < need or workspace.device != device:
+        raise ValueError(f"workspace must be a uint8 tensor of at least {need} bytes on {device}")
+    od = SB_F32 if out_dt == torch.float32 else SB_BF16
+    with torch.cuda.device(device):
+        status = lib.sb_strassen_gemm_quad(_stream_handle(device), a.data_ptr(), b.data_ptr(), out.data_ptr(),
+                                           m, n, k, _ld(a), _ld(b), _ld(out), bm, bn, bk, od,
+                                           workspace.data_ptr(), workspace.numel())
+    _native.check(status)
+    return out
+
+
 def rms_norm(x, scale, eps: float = 1e-6, out=None):
     """bf16 RMSNorm with fp32 math on the sm_100a row kernel.
 
