@@ -12,9 +12,16 @@ steps.
 
 N > 1 runs under torchrun, one rank per GPU; every rank computes its own
 independent GEMM of the same shape (weak scaling, no collective on the data
-path); times are CUDA-event times, max over ranks.  ``--impl reference`` times
-the CPU restatement of the reference's algorithm (``oracle/``) on the host
-cores -- the reference itself is JAX/Pallas-on-TPU and cannot run here.
+path); times are CUDA-event times, max over ranks.  The same run also measures
+the tensor-parallel decoder the north star scales (Qwen3-8B
+prefill, batch 8 x 2048, TP = N over NCCL) and reports it in a ``decoder``
+object with TP=1 measured on rank 0's GPU, so the 1..8-GPU runs carry the
+decoder's scaling curve.  ``--impl reference`` times the CPU restatement of the
+reference's algorithm (``oracle/``) on the host cores -- the reference itself
+is JAX/Pallas-on-TPU and cannot run here.
+
+  python bench.py --profile --steps 3 --warmup 2   # only the timed GEMM launches
+                                                  # (the command the ncu captures run)
 """
 
 from __future__ import annotations
@@ -50,9 +57,14 @@ def parse():
     p.add_argument("--no-cpu-baseline", action="store_true",
                    help="skip the CPU oracle timing (used for ncu captures)")
     p.add_argument("--no-e2e", action="store_true", help="skip the host-buffer end-to-end loop")
-    p.add_argument("--kernel", default="single", choices=["single", "pair", "pair-planes"],
-                   help="GEMM workload: the one-CTA Strassen kernel, the two-CTA cluster kernel, or the "
-                        "two-CTA kernel on B operand planes formed inside each step")
+    p.add_argument("--kernel", default="single", choices=["single", "pair", "pair-planes", "quad"],
+                   help="GEMM workload: the one-CTA Strassen kernel, the two-CTA cluster kernel, the "
+                        "two-CTA kernel on B operand planes formed inside each step, or the four-CTA "
+                        "paired-tensor-core kernel (its operand passes inside each step)")
+    p.add_argument("--profile", action="store_true",
+                   help="time only the GEMM launches (no comparisons, e2e, CPU baseline or decoder); "
+                        "the command the committed ncu captures run")
+    p.add_argument("--no-decoder", action="store_true", help="skip the decoder measurement of the GEMM run")
     p.add_argument("--workload", default="gemm", choices=["gemm", "qwen3-8b", "qwen3-32b"],
                    help="gemm: the 8192^3 Strassen GEMM (default, the driver's line); "
                         "qwen3-*: tensor-parallel decoder prefill tokens/s (BASELINE configs 4/5)")
@@ -162,6 +174,17 @@ def cpu_baseline(a_bits, b_bits, rows: int, cols: int | None = None, repeats: in
     return flops / t / 1e12, t, rows, n
 
 
+# The CPU sample both CPU legs time: the first Strassen block row (bm = 1024
+# rows of A against all of B) of the 8192^3 GEMM -- a block row depends only on
+# its own A rows, so this is a self-contained slice of the workload.
+CPU_SAMPLE_ROWS = TILE[0]
+
+
+def cpu_sample_text(threads: int) -> str:
+    return (f"first block row ({CPU_SAMPLE_ROWS} x {N} output, K={K}) of the {M}x{N}x{K} GEMM per step, "
+            f"tile {TILE}, numpy/BLAS restatement of the reference, {threads} threads")
+
+
 def cpu_threads() -> int:
     try:
         from threadpoolctl import threadpool_info
@@ -179,19 +202,18 @@ def run_reference(args):
     if rank != 0:
         return 0
     a_bits, b_bits = host_inputs()
-    rows = cols = TILE[0]  # one (1024 x 1024) output tile of the 8192^3 GEMM per step
+    rows = CPU_SAMPLE_ROWS
     for _ in range(args.warmup):
-        cpu_baseline(a_bits, b_bits, rows, cols)
+        cpu_baseline(a_bits, b_bits, rows)
     vals, ts = [], []
     for _ in range(args.steps):
-        v, t, _, _ = cpu_baseline(a_bits, b_bits, rows, cols)
+        v, t, _, _ = cpu_baseline(a_bits, b_bits, rows)
         vals.append(v)
         ts.append(t)
     total_t = sum(ts)
-    value = args.steps * 2.0 * rows * cols * K / total_t / 1e12
+    value = args.steps * 2.0 * rows * N * K / total_t / 1e12
     threads = cpu_threads()
-    sample = (f"one {rows}x{cols} output tile (K={K}) of the {M}x{N}x{K} GEMM per step, "
-              f"tile {TILE}, numpy/BLAS oracle")
+    sample = cpu_sample_text(threads)
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT,
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
@@ -217,6 +239,7 @@ def run_ours(args):
 
     rank, world, local = dist_env()
     if world > 1:
+        nccl_init_log()
         torch.cuda.set_device(local)
         from datetime import timedelta
         dist.init_process_group("nccl", timeout=timedelta(seconds=300),
@@ -242,6 +265,12 @@ def run_ours(args):
             # B's operand planes are formed inside the timed step (B is an input).
             ops = sb.strassen_b_operands(b, bn=TILE[1], bk=TILE[2], out=planes)
             sb.pair_matmul(a, None, b_operands=ops, bm=TILE[0], bn=TILE[1], bk=TILE[2], out=c)
+    elif args.kernel == "quad":
+        workspace = torch.empty(_native.load().sb_quad_workspace_bytes(M, N, K), dtype=torch.uint8, device=device)
+        launches_per_step = 3  # A operand pass, B operand planes, the four-CTA GEMM
+
+        def step():
+            sb.quad_matmul(a, b, bm=TILE[0], bn=TILE[1], bk=TILE[2], out=c, workspace=workspace)
     else:
         gemm = sb.pair_matmul if args.kernel == "pair" else sb.strassen_matmul
 
@@ -300,35 +329,56 @@ def run_ours(args):
         traffic = json.loads(traffic_path.read_text()).get("dram_bytes_per_launch")
 
     # --- comparison arms on identical tensors (informational)
-    cublas_ms = timed(lambda: torch.matmul(a, b, out=c), max(10, args.steps // 2), 3) / max(10, args.steps // 2)
-    control_ms = timed(lambda: sb.classical_matmul(a, b, bm=TILE[0], bn=TILE[1], bk=TILE[2], out=c),
-                       max(10, args.steps // 2), 3) / max(10, args.steps // 2)
+    cublas_ms = control_ms = None
+    if not args.profile:
+        n_cmp = max(10, args.steps // 2)
+        cublas_ms = timed(lambda: torch.matmul(a, b, out=c), n_cmp, 3) / n_cmp
+        control_ms = timed(lambda: sb.classical_matmul(a, b, bm=TILE[0], bn=TILE[1], bk=TILE[2], out=c),
+                           n_cmp, 3) / n_cmp
 
-    # --- end to end through the public API with host buffers
-    e2e = None
-    if not args.no_e2e:
+    # --- end to end through the reference-facing operator with host buffers:
+    # every step copies A and B from pinned host memory, calls strassen_matmul
+    # (the drop-in for strassen_pallas.strassen_matmul) and copies C back.
+    e2e = e2e_streamed = None
+    if not args.no_e2e and not args.profile:
         c_host = torch.empty(M, N, dtype=torch.bfloat16).pin_memory()
+        a_in = torch.empty_like(a)
+        b_in = torch.empty_like(b)
 
         def e2e_step():
-            # Host operands in, host product out: B, then A in row chunks, each
-            # chunk's GEMM and its copy back overlapping the later transfers.
-            sb.strassen_matmul_streamed(a_host, b_host, bm=TILE[0], bn=TILE[1], bk=TILE[2], device=device,
-                                        out=c_host)
+            a_in.copy_(a_host, non_blocking=True)
+            b_in.copy_(b_host, non_blocking=True)
+            sb.strassen_matmul(a_in, b_in, bm=TILE[0], bn=TILE[1], bk=TILE[2], out=c)
+            c_host.copy_(c, non_blocking=True)
 
         e2e_steps = max(5, args.steps // 5)
         e2e_ms = timed(e2e_step, e2e_steps, 2) / e2e_steps
         e2e = {"value": world * flops / (e2e_ms * 1e-3) / 1e12, "unit": UNIT,
                "h2d_bytes_per_step": 2 * M * K * 2, "d2h_bytes_per_step": M * N * 2,
-               "ms_per_step": e2e_ms}
+               "ms_per_step": e2e_ms, "api": "strassen_matmul (sb_strassen_gemm), copies in stream order"}
 
-    # --- CPU baseline (rank 0 at N=1 only)
+        def streamed_step():
+            # The same copies overlapped with the GEMMs: B, then A in block-row
+            # chunks on a copy stream, each chunk's GEMM and copy-back overlapping.
+            sb.strassen_matmul_streamed(a_host, b_host, bm=TILE[0], bn=TILE[1], bk=TILE[2], device=device,
+                                        out=c_host)
+
+        st_ms = timed(streamed_step, e2e_steps, 2) / e2e_steps
+        e2e_streamed = {"value": world * flops / (st_ms * 1e-3) / 1e12, "unit": UNIT, "ms_per_step": st_ms,
+                        "api": "strassen_matmul_streamed (copies overlapped with block-row GEMMs)"}
+
+    # --- CPU baseline (rank 0 at N=1 only): the reference arm's sample
     cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        rows = 2 * TILE[0]
-        v, t, r, n = cpu_baseline(a_bits, b_bits, rows)
-        cpu = {"value": v, "unit": UNIT, "cores": cpu_threads(), "kind": "port",
-               "sample": f"first {r} rows (2 block rows) of the {M}x{N}x{K} GEMM, tile {TILE}, "
-                         f"{t:.1f} s, numpy/BLAS restatement of the reference"}
+    if rank == 0 and world == 1 and not args.no_cpu_baseline and not args.profile:
+        v, t, r, n = cpu_baseline(a_bits, b_bits, CPU_SAMPLE_ROWS, repeats=2)
+        threads = cpu_threads()
+        cpu = {"value": v, "unit": UNIT, "cores": threads, "kind": "port",
+               "sample": cpu_sample_text(threads) + f", {t:.1f} s"}
+
+    # --- the tensor-parallel decoder at TP = world
+    decoder = None
+    if not args.no_decoder and not args.profile:
+        decoder = decoder_scaling(rank, world, local, device)
 
     if world > 1:
         barrier()
@@ -344,7 +394,9 @@ def run_ours(args):
                    "kernel": {"single": "one-CTA (sb_strassen_gemm)",
                               "pair": "two-CTA cluster (sb_strassen_gemm_pair)",
                               "pair-planes": "B operand planes + two-CTA cluster (sb_strassen_b_operands, "
-                                             "sb_strassen_gemm_pair_planes), both timed"}[args.kernel],
+                                             "sb_strassen_gemm_pair_planes), both timed",
+                              "quad": "four-CTA paired-tensor-core kernel (sb_strassen_gemm_quad: A operand "
+                                      "pass, B operand planes, GEMM), all timed"}[args.kernel],
                    "l2": "inputs 256 MiB > 126 MiB L2, no flush",
                    "inputs": f"N(0,1) bf16, default_rng({SEED_A}) / ({SEED_B})",
                    "parallelism": f"replicas x{world}" if world > 1 else "single GPU"},
@@ -354,16 +406,146 @@ def run_ours(args):
                      "peak_source": peak_src, "effective_tflops": flops / (ms * 1e-3) / 1e12},
         "cpu_baseline": cpu,
         "e2e": e2e,
+        "e2e_streamed": e2e_streamed,
         "clocks": clock,
         "gpu_launches": args.steps * launches_per_step,
-        "comparison": {
+        "comparison": None if cublas_ms is None else {
             "cublas_tflops": flops / (cublas_ms * 1e-3) / 1e12,
             "strassen_vs_cublas": (flops / (ms * 1e-3)) / (flops / (cublas_ms * 1e-3)),
             "classical_control_tflops": flops / (control_ms * 1e-3) / 1e12,
         },
+        "decoder": decoder,
     }
     print(json.dumps(line), flush=True)
     return 0
+
+
+# ------------------------------------------------------------ decoder helpers
+def nccl_init_log():
+    """NCCL's communicator-init lines (ranks, devices, NVLS/NVLink choice) on
+    stderr, so a run's rank count can be read from its log; stdout keeps the
+    single JSON line.  Settings the caller exported win."""
+    os.environ.setdefault("NCCL_DEBUG", "INFO")
+    os.environ.setdefault("NCCL_DEBUG_SUBSYS", "INIT")
+    os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")
+
+
+def measure_prefill(workload, tp, device, steps, warmup, chunks, backend="strassen", eager=False, layers=None,
+                    group=None):
+    """Qwen3 prefill on `tp`'s ranks: ms per forward (CUDA events, max over the
+    group's ranks), tokens/s, FLOP rate, an end-to-end figure with the token
+    ids copied in and the logits copied out, and the launch count per step."""
+    import torch
+    import torch.distributed as dist
+
+    from strassen_tpu_b200 import qwen3
+
+    cfg, (batch, seq) = ({"qwen3-8b": (qwen3.QWEN3_8B, (8, 2048)),
+                          "qwen3-32b": (qwen3.QWEN3_32B, (16, 4096))}[workload])
+    model = qwen3.Qwen3Prefill(cfg, tp, device, backend=backend, layers=layers)
+    g = torch.Generator().manual_seed(20260911)
+    tokens_host = torch.randint(0, cfg.vocab, (batch, seq), generator=g).pin_memory()
+    tokens = tokens_host.to(device)
+    rope = model.rope(batch, seq)
+    stream = torch.cuda.current_stream(device)
+    multi = tp.world > 1
+
+    def barrier():
+        if multi:
+            dist.barrier(group=group, device_ids=[device.index])
+
+    def max_over_ranks(x):
+        if not multi:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX, group=group)
+        return float(t.item())
+
+    def timed(fn, n, w):
+        for _ in range(w):
+            fn()
+        barrier()
+        torch.cuda.synchronize(device)
+        s0, e0 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s0.record(stream)
+        for _ in range(n):
+            fn()
+        e0.record(stream)
+        torch.cuda.synchronize(device)
+        barrier()
+        return max_over_ranks(s0.elapsed_time(e0))
+
+    if eager:
+        forward = lambda t: model.forward(t, rope, chunks=chunks)  # noqa: E731
+        captured = None
+    else:
+        # One CUDA graph of the whole prefill (kernels, torch ops, NCCL calls).
+        captured = qwen3.CapturedPrefill(model, tokens, rope, chunks=chunks)
+        forward = captured
+    ms = timed(lambda: forward(tokens), steps, warmup) / steps
+    logits_host = torch.empty(batch, cfg.vocab, dtype=torch.bfloat16).pin_memory()
+
+    def e2e_step():
+        t = tokens_host.to(device, non_blocking=True)
+        logits_host.copy_(forward(t), non_blocking=True)
+
+    e2e_n = max(2, steps // 2)
+    e2e_ms = timed(e2e_step, e2e_n, 1) / e2e_n
+    n_layers = len(model.blocks)
+    flops = qwen3.prefill_flops(cfg, batch, seq, n_layers)
+    strassen_sites = sorted(k for k, v in model.blocks[0].sites.items() if v.strassen)
+    per_chunk = chunks if batch % chunks == 0 else 1
+    launches = 0
+    if backend == "strassen":
+        # two RMSNorm row passes + one GEMM per Strassen site, per block and token chunk
+        launches = n_layers * (2 + len(strassen_sites)) * per_chunk
+    if tp.peer_reduce:
+        launches += n_layers * 2 * per_chunk  # sb_p2p_reduce
+    if captured is not None:
+        torch.cuda.synchronize(device)
+        captured.release()  # a graph holding NCCL calls goes before the process group
+    del model, captured, forward
+    torch.cuda.empty_cache()
+    tok = batch * seq
+    return {"ms": ms, "tokens_per_s": tok / (ms * 1e-3), "tflops": flops / (ms * 1e-3) / 1e12,
+            "e2e_tokens_per_s": tok / (e2e_ms * 1e-3), "launches": launches, "batch": batch, "seq": seq,
+            "layers": n_layers, "strassen_sites": strassen_sites, "vocab": cfg.vocab}
+
+
+def decoder_scaling(rank, world, local, device, workload="qwen3-8b", steps=3, warmup=1):
+    """The decoder the north star scales, inside the GEMM run: Qwen3-8B prefill
+    (8 x 2048 tokens, 36 layers, Strassen sites, NCCL) at TP = world, and at
+    TP = 1 on rank 0's GPU for the strong-scaling efficiency."""
+    import torch.distributed as dist
+
+    from strassen_tpu_b200 import qwen3
+
+    chunks_n = 2 if world > 1 else 1
+    solo = dist.new_group([0]) if world > 1 else None  # every rank takes part in creating it
+    tp1 = None
+    if rank == 0:
+        tp = qwen3.TensorParallel(group=solo) if world > 1 else qwen3.TensorParallel()
+        tp1 = measure_prefill(workload, tp, device, steps, warmup, chunks=1, group=solo)
+    if world > 1:
+        dist.barrier(device_ids=[local])
+        tpn = measure_prefill(workload, qwen3.TensorParallel(), device, steps, warmup, chunks=chunks_n)
+    else:
+        tpn = tp1
+    if rank != 0:
+        return None
+    return {
+        "metric": f"{workload.replace('-', '_')}_prefill_tokens_per_s", "unit": "tokens/s",
+        "tokens_per_s": tpn["tokens_per_s"], "tp": world, "ms_per_step": tpn["ms"],
+        "tp1_tokens_per_s": tp1["tokens_per_s"],
+        "efficiency": tpn["tokens_per_s"] / (world * tp1["tokens_per_s"]),
+        "achieved_tflops": tpn["tflops"], "e2e_tokens_per_s": tpn["e2e_tokens_per_s"],
+        "config": {"model": workload, "global_batch": tpn["batch"], "seq_len": tpn["seq"],
+                   "layers": tpn["layers"], "parallelism": f"tp{world}", "collective": "nccl",
+                   "token_chunks": chunks_n, "cuda_graph": True, "strassen_sites": tpn["strassen_sites"],
+                   "lm_head": "last position per sequence", "steps": steps, "warmup": warmup,
+                   "tp1": "rank 0's GPU alone, same box, same run"},
+        "gpu_launches_per_step": tpn["launches"],
+    }
 
 
 # --------------------------------------------------------------- decoder arm
@@ -378,96 +560,37 @@ def run_decoder(args):
     device = torch.device("cuda", local)
     torch.cuda.set_device(device)
     if world > 1:
+        nccl_init_log()
         from datetime import timedelta
         dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=device)
-    cfg, (batch, seq) = ({"qwen3-8b": (qwen3.QWEN3_8B, (8, 2048)),
-                          "qwen3-32b": (qwen3.QWEN3_32B, (16, 4096))}[args.workload])
     tp = qwen3.TensorParallel(collective=args.collective)
-    model = qwen3.Qwen3Prefill(cfg, tp, device, backend=args.backend, layers=args.layers)
-    g = torch.Generator().manual_seed(20260911)
-    tokens_host = torch.randint(0, cfg.vocab, (batch, seq), generator=g).pin_memory()
-    tokens = tokens_host.to(device)
-    rope = model.rope(batch, seq)
-    stream = torch.cuda.current_stream(device)
-
-    def barrier():
-        if world > 1:
-            dist.barrier(device_ids=[local])
-
-    def max_over_ranks(x):
-        if world == 1:
-            return x
-        t = torch.tensor([x], dtype=torch.float64, device=device)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        return float(t.item())
-
-    def timed(fn, steps, warmup):
-        for _ in range(warmup):
-            fn()
-        barrier()
-        torch.cuda.synchronize(device)
-        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        s.record(stream)
-        for _ in range(steps):
-            fn()
-        e.record(stream)
-        torch.cuda.synchronize(device)
-        barrier()
-        return max_over_ranks(s.elapsed_time(e))
-
     chunks = args.chunks if args.chunks is not None else (2 if world > 1 else 1)
-    if args.eager:
-        forward = lambda t: model.forward(t, rope, chunks=chunks)  # noqa: E731
-        captured = None
-    else:
-        # One CUDA graph of the whole prefill (kernels, torch ops, NCCL calls).
-        captured = qwen3.CapturedPrefill(model, tokens, rope, chunks=chunks)
-        forward = captured
-
     with ClockSampler(device.index) as clocks:
-        ms = timed(lambda: forward(tokens), args.steps, args.warmup) / args.steps
-    logits_host = torch.empty(batch, cfg.vocab, dtype=torch.bfloat16).pin_memory()
-
-    def e2e_step():
-        t = tokens_host.to(device, non_blocking=True)
-        logits_host.copy_(forward(t), non_blocking=True)
-
-    e2e_ms = timed(e2e_step, max(2, args.steps // 2), 1) / max(2, args.steps // 2)
-    n_layers = len(model.blocks)
-    flops = qwen3.prefill_flops(cfg, batch, seq, n_layers)
-    strassen_sites = sorted(k for k, v in model.blocks[0].sites.items() if v.strassen)
-    launches = 0
-    if args.backend == "strassen":
-        # two RMSNorm row passes + one GEMM per Strassen site, per block and token chunk
-        launches = n_layers * (2 + len(strassen_sites)) * (chunks if batch % chunks == 0 else 1)
-    if tp.peer_reduce:
-        launches += n_layers * 2 * (chunks if batch % chunks == 0 else 1)  # sb_p2p_reduce
-    if captured is not None:
-        torch.cuda.synchronize(device)
-        captured.release()  # a graph holding NCCL calls goes before the process group
+        r = measure_prefill(args.workload, tp, device, args.steps, args.warmup, chunks, backend=args.backend,
+                            eager=args.eager, layers=args.layers)
     tp.close()
     if world > 1:
-        barrier()
+        dist.barrier(device_ids=[local])
         dist.destroy_process_group()
     if rank != 0:
         return 0
-    tok = batch * seq
+    tok = r["batch"] * r["seq"]
     line = {
-        "metric": f"{args.workload.replace('-', '_')}_prefill_tokens_per_s", "value": tok / (ms * 1e-3),
+        "metric": f"{args.workload.replace('-', '_')}_prefill_tokens_per_s", "value": r["tokens_per_s"],
         "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": ms, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+        "ms_per_step": r["ms"], "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
         "dtype": "bf16", "data": "synthetic (uniform token ids, random N(0,0.02) weights)",
-        "config": {"workload": args.workload, "model": args.workload, "global_batch": batch,
-                   "seq_len": seq, "layers": n_layers, "parallelism": f"tp{world}",
-                   "backend": args.backend, "strassen_sites": strassen_sites,
+        "config": {"workload": args.workload, "model": args.workload, "global_batch": r["batch"],
+                   "seq_len": r["seq"], "layers": r["layers"], "parallelism": f"tp{world}",
+                   "backend": args.backend, "strassen_sites": r["strassen_sites"],
                    "token_chunks": chunks, "cuda_graph": not args.eager,
                    "collective": args.collective if world > 1 else None,
                    "lm_head": "last position per sequence"},
-        "achieved_tflops": flops / (ms * 1e-3) / 1e12,
-        "e2e": {"value": tok / (e2e_ms * 1e-3), "unit": "tokens/s",
-                "h2d_bytes_per_step": tok * 8, "d2h_bytes_per_step": batch * cfg.vocab * 2},
+        "achieved_tflops": r["tflops"],
+        "e2e": {"value": r["e2e_tokens_per_s"], "unit": "tokens/s",
+                "h2d_bytes_per_step": tok * 8, "d2h_bytes_per_step": r["batch"] * r["vocab"] * 2},
         "clocks": clocks.summary(),
-        "gpu_launches": launches * args.steps,
+        "gpu_launches": r["launches"] * args.steps,
     }
     print(json.dumps(line), flush=True)
     return 0
