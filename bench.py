@@ -239,11 +239,11 @@ def run_ours(args):
 
     rank, world, local = dist_env()
     if world > 1:
-        nccl_init_log()
         torch.cuda.set_device(local)
         from datetime import timedelta
         dist.init_process_group("nccl", timeout=timedelta(seconds=300),
                                 device_id=torch.device("cuda", local))
+        nccl_init_log(rank, world, torch.device("cuda", local))
     device = torch.device("cuda", local)
     torch.cuda.set_device(device)
 
@@ -421,13 +421,15 @@ def run_ours(args):
 
 
 # ------------------------------------------------------------ decoder helpers
-def nccl_init_log():
-    """NCCL's communicator-init lines (ranks, devices, NVLS/NVLink choice) on
-    stderr, so a run's rank count can be read from its log; stdout keeps the
-    single JSON line.  Settings the caller exported win."""
-    os.environ.setdefault("NCCL_DEBUG", "INFO")
-    os.environ.setdefault("NCCL_DEBUG_SUBSYS", "INIT")
-    os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")
+def nccl_init_log(rank: int, world: int, device) -> None:
+    """One line per rank on stderr once the NCCL process group is up (rank,
+    world size, NCCL version, device), so a run's rank count can be read from
+    its log; stdout keeps the single JSON line."""
+    import torch
+    v = torch.cuda.nccl.version()
+    ver = ".".join(str(x) for x in v) if isinstance(v, tuple) else str(v)
+    print(f"nccl communicator: rank {rank} of {world}, NCCL {ver}, {torch.cuda.get_device_name(device)} "
+          f"cuda:{device.index}", file=sys.stderr, flush=True)
 
 
 def measure_prefill(workload, tp, device, steps, warmup, chunks, backend="strassen", eager=False, layers=None,
@@ -560,9 +562,9 @@ def run_decoder(args):
     device = torch.device("cuda", local)
     torch.cuda.set_device(device)
     if world > 1:
-        nccl_init_log()
         from datetime import timedelta
         dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=device)
+        nccl_init_log(rank, world, device)
     tp = qwen3.TensorParallel(collective=args.collective)
     chunks = args.chunks if args.chunks is not None else (2 if world > 1 else 1)
     with ClockSampler(device.index) as clocks:

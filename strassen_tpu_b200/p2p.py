@@ -184,3 +184,70 @@ class PeerReduce:
             for ptr in self._own:
                 _native.check(self.lib.sb_p2p_buffer_free(ptr))
         self._opened, self._own, self._partial = [], [], None
+
+
+def benchmark(sizes_mib=(32, 128), cols: int = 4096, steps: int = 20, warmup: int = 5) -> list[dict]:
+    """Times one ``PeerReduce.reduce`` (with a bf16 residual) against NCCL's
+    in-place all-reduce of the same [rows, cols] bf16 partial (without one), per
+    size, on the default process group: CUDA events around ``steps`` calls after
+    ``warmup`` calls, max over ranks.  Run under torchrun, one rank per GPU:
+
+      python -m torch.distributed.run --nproc-per-node 2 -m strassen_tpu_b200.p2p
+    """
+    import torch.distributed as dist
+
+    rank, world = dist.get_rank(), dist.get_world_size()
+    dev = torch.device("cuda", torch.cuda.current_device())
+    results = []
+    for mib in sizes_mib:
+        rows = mib * (1 << 20) // (cols * 2)
+        pr = PeerReduce(rows, cols, dev)
+        part = pr.partial_rows(0, rows)
+        part.copy_(torch.randn(rows, cols, device=dev).to(torch.bfloat16))
+        residual = torch.randn(rows, cols, device=dev).to(torch.bfloat16)
+        x = torch.randn(rows, cols, device=dev).to(torch.bfloat16)
+        out = torch.empty_like(part)
+
+        def timed(fn):
+            for _ in range(warmup):
+                fn()
+            torch.cuda.synchronize(dev)
+            dist.barrier()
+            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s.record()
+            for _ in range(steps):
+                fn()
+            e.record()
+            torch.cuda.synchronize(dev)
+            t = torch.tensor([s.elapsed_time(e) / steps], dtype=torch.float64, device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            return float(t.item()) * 1e3  # microseconds
+
+        p2p_us = timed(lambda: pr.reduce(part, residual, out=out))
+        nccl_us = timed(lambda: dist.all_reduce(x))
+        status = _native.device_status()
+        pr.close()
+        results.append({"ranks": world, "mib": mib, "rows": rows, "cols": cols, "p2p_us": p2p_us,
+                        "nccl_us": nccl_us, "p2p_bus_gbs": 2 * (world - 1) / world * mib * (1 << 20) / p2p_us / 1e3,
+                        "nccl_bus_gbs": 2 * (world - 1) / world * mib * (1 << 20) / nccl_us / 1e3,
+                        "device_status": status, "rank": rank})
+    return results
+
+
+if __name__ == "__main__":
+    import json
+    import os
+    from datetime import timedelta
+
+    import torch.distributed as _dist
+
+    _local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(_local)
+    _dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", _local))
+    try:
+        for _r in benchmark():
+            if _r["rank"] == 0:
+                print(json.dumps(_r), flush=True)
+    finally:
+        _dist.barrier()
+        _dist.destroy_process_group()
