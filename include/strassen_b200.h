@@ -105,6 +105,12 @@ typedef struct sb_options {
    * as eight exact sub-block products instead of Strassen (the reference's
    * classical_panels / panel_schedule).  NULL = none. */
   const int32_t* panel_schedule;
+  /* B200 extension (no counterpart in the reference, whose TPU lane rule asks
+   * bn % 256 == 0): nonzero accepts any bn that is a multiple of 128, and
+   * qk_norm_rope then needs bn % head_dim == 0 (each half block holds whole
+   * half-heads).  The tensor-parallel decoder uses it for one-head k/v shards
+   * (128 columns).  0 = the reference's rules. */
+  int32_t narrow_bn;
 } sb_options;
 
 /*

@@ -49,6 +49,7 @@ class SbOptions(ctypes.Structure):
         ("formula_variant", ctypes.c_int32),
         ("block_permutation", ctypes.c_int32),
         ("panel_schedule", ctypes.c_void_p),
+        ("narrow_bn", ctypes.c_int32),
     ]
 
 

@@ -1079,19 +1079,9 @@ __global__ void __launch_bounds__(64, 1) wait_selftest_kernel(int* err) {
 // Row pass of norm_residual_add (strassen_pallas.py:836-866): the GEMM has
 // written fp32 pre-norm rows to `x`; one CTA normalises one row:
 // out = bf16(x * rsqrt((sum(left^2) + sum(right^2)) / n + eps) * scale + residual).
-__global__ void __launch_bounds__(256) norm_residual_rows_kernel(
-    const float* __restrict__ x, int64_t n, const void* __restrict__ scale, int scale_f32,
-    const void* __restrict__ residual, int64_t ldr, int residual_f32, float eps,
-    __nv_bfloat16* __restrict__ out, int64_t ldo) {
-  const int64_t row = blockIdx.x;
-  const float* xr = x + row * n;
-  const int64_t half = n / 2;
-  float sl = 0.f, sr = 0.f;
-  for (int64_t i = threadIdx.x; i < half; i += blockDim.x) {
-    const float a = xr[i], b = xr[half + i];
-    sl += a * a;
-    sr += b * b;
-  }
+//
+// Block reduction of the two half-row sums; every thread receives both totals.
+__device__ __forceinline__ float2 block_sum2(float sl, float sr) {
   __shared__ float red[2][32];
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) {
@@ -1119,8 +1109,89 @@ __global__ void __launch_bounds__(256) norm_residual_rows_kernel(
     }
   }
   __syncthreads();
-  const float squares = red[0][0] + red[1][0];
-  const float recip = 1.0f / sqrtf(squares * (1.0f / (float)n) + eps);
+  return make_float2(red[0][0], red[1][0]);
+}
+
+// Eight consecutive values of a bf16 or fp32 vector as fp32 (16- or 32-byte loads).
+__device__ __forceinline__ void load8_f32(const void* base, bool f32, int64_t off, float* f) {
+  if (f32) {
+    const float4* q = reinterpret_cast<const float4*>(static_cast<const float*>(base) + off);
+    const float4 u = q[0], v = q[1];
+    f[0] = u.x; f[1] = u.y; f[2] = u.z; f[3] = u.w;
+    f[4] = v.x; f[5] = v.y; f[6] = v.z; f[7] = v.w;
+  } else {
+    const uint4 u = *reinterpret_cast<const uint4*>(static_cast<const __nv_bfloat16*>(base) + off);
+    const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float2 t = __bfloat1622float2(h[j]);
+      f[2 * j] = t.x;
+      f[2 * j + 1] = t.y;
+    }
+  }
+}
+
+// Vector form: each thread keeps up to kChunks 8-wide pieces of the row in
+// registers between the two passes (one read of `x`), with 32-byte fp32 and
+// 16-byte bf16 loads and 16-byte bf16 stores.  Needs n % 16 == 0 (a piece never
+// straddles the two halves), n <= 8 * 256 * kChunks, 16-byte aligned rows
+// (x, residual, out and scale), launched with 256 threads.
+template <int kChunks>
+__global__ void __launch_bounds__(256) norm_residual_rows_kernel(
+    const float* __restrict__ x, int64_t n, const void* __restrict__ scale, int scale_f32,
+    const void* __restrict__ residual, int64_t ldr, int residual_f32, float eps,
+    __nv_bfloat16* __restrict__ out, int64_t ldo) {
+  const int64_t row = blockIdx.x;
+  const float* xr = x + row * n;
+  const int pieces = (int)(n / 8), half = pieces / 2;
+  float v[kChunks][8];
+  float sl = 0.f, sr = 0.f;
+#pragma unroll
+  for (int c = 0; c < kChunks; ++c) {
+    const int p = threadIdx.x + c * 256;
+    if (p < pieces) {
+      load8_f32(xr, true, (int64_t)p * 8, v[c]);
+      float s = 0.f;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) s += v[c][j] * v[c][j];
+      if (p < half) sl += s; else sr += s;
+    }
+  }
+  const float2 sums = block_sum2(sl, sr);
+  const float recip = 1.0f / sqrtf((sums.x + sums.y) * (1.0f / (float)n) + eps);
+#pragma unroll
+  for (int c = 0; c < kChunks; ++c) {
+    const int p = threadIdx.x + c * 256;
+    if (p < pieces) {
+      float sc[8], r[8], o[8];
+      load8_f32(scale, scale_f32, (int64_t)p * 8, sc);
+      load8_f32(residual, residual_f32, row * ldr + (int64_t)p * 8, r);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) o[j] = v[c][j] * recip * sc[j] + r[j];
+      *reinterpret_cast<uint4*>(out + row * ldo + (int64_t)p * 8) =
+          make_uint4(pack_bf16x2(o[0], o[1]), pack_bf16x2(o[2], o[3]), pack_bf16x2(o[4], o[5]),
+                     pack_bf16x2(o[6], o[7]));
+    }
+  }
+}
+
+// Scalar form for rows the vector form cannot take (odd widths, unaligned
+// residual or output rows, n above 8192): the same arithmetic, reading `x` twice.
+__global__ void __launch_bounds__(256) norm_residual_rows_scalar_kernel(
+    const float* __restrict__ x, int64_t n, const void* __restrict__ scale, int scale_f32,
+    const void* __restrict__ residual, int64_t ldr, int residual_f32, float eps,
+    __nv_bfloat16* __restrict__ out, int64_t ldo) {
+  const int64_t row = blockIdx.x;
+  const float* xr = x + row * n;
+  const int64_t half = n / 2;
+  float sl = 0.f, sr = 0.f;
+  for (int64_t i = threadIdx.x; i < half; i += blockDim.x) {
+    const float a = xr[i], b = xr[half + i];
+    sl += a * a;
+    sr += b * b;
+  }
+  const float2 sums = block_sum2(sl, sr);
+  const float recip = 1.0f / sqrtf((sums.x + sums.y) * (1.0f / (float)n) + eps);
   for (int64_t i = threadIdx.x; i < n; i += blockDim.x) {
     const float s = scale_f32 ? reinterpret_cast<const float*>(scale)[i]
                               : __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(scale)[i]);
@@ -1313,7 +1384,7 @@ int check_device() {
 // reference's host-side checks (strassen_pallas.py:927-1047, :127-140).
 int validate_core(const void* a, const void* b, const void* c, int64_t m, int64_t n, int64_t k,
                   int64_t lda, int64_t ldb, int64_t ldc, int32_t bm, int32_t bn, int32_t bk,
-                  int32_t out_dtype) {
+                  int32_t out_dtype, int32_t bn_align = 256) {
   if (!a || !b || !c) return fail(SB_ERR_RANK, "null matrix pointer");
   if (m <= 0 || n <= 0 || k <= 0) return fail(SB_ERR_RANK, "matrix dimensions must be positive");
   if (bm <= 0 || bn <= 0 || bk <= 0) return fail(SB_ERR_TILING, "tile sizes must be positive");
@@ -1327,7 +1398,7 @@ int validate_core(const void* a, const void* b, const void* c, int64_t m, int64_
   }
   std::string tiling;
   if (bm % 16) tiling += "\n  bm=" + std::to_string(bm) + " must be a multiple of 16";
-  if (bn % 256) tiling += "\n  bn=" + std::to_string(bn) + " must be a multiple of 256";
+  if (bn % bn_align) tiling += "\n  bn=" + std::to_string(bn) + " must be a multiple of " + std::to_string(bn_align);
   if (bk % 256) tiling += "\n  bk=" + std::to_string(bk) + " must be a multiple of 256";
   if (!tiling.empty()) return fail(SB_ERR_TILING, "tile breaks TPU v5e alignment:" + tiling);
   if (out_dtype != SB_BF16 && out_dtype != SB_F32)
@@ -1379,6 +1450,31 @@ int make_maps(const void* a, const void* b, int64_t m, int64_t n, int64_t k, int
                      CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) return fail(SB_ERR_CUDA, "cuTensorMapEncodeTiled(B) failed: " + std::to_string((int)r));
   }
+  return SB_OK;
+}
+
+// Row pass of norm_residual_add over M rows of fp32 pre-norm values `x` [M, n]:
+// the register-resident vector kernel when the row fits 8 * 256 * 4 values and
+// every row start is 16-byte aligned, else the scalar kernel.
+int launch_norm_rows(cudaStream_t stream, const float* x, int64_t m, int64_t n, const sb_epilogue* ep,
+                     __nv_bfloat16* c, int64_t ldc) {
+  const bool res_f32 = ep->residual_dtype == SB_F32, scale_f32 = ep->aux_dtype == SB_F32;
+  const int64_t pieces = n / 8;
+  const bool vec = n % 16 == 0 && pieces <= 4 * 256 && aligned16(x) && aligned16(c) && ldc % 8 == 0 &&
+                   aligned16(ep->norm_scale) && aligned16(ep->residual) &&
+                   ep->ld_residual % (res_f32 ? 4 : 8) == 0;
+  const int chunks = (int)((pieces + 255) / 256);
+  auto args = [&](auto kernel) {
+    kernel<<<(unsigned)m, 256, 0, stream>>>(x, n, ep->norm_scale, scale_f32, ep->residual, ep->ld_residual,
+                                            res_f32, ep->norm_eps, c, ldc);
+  };
+  if (!vec) args(norm_residual_rows_scalar_kernel);
+  else if (chunks <= 1) args(norm_residual_rows_kernel<1>);
+  else if (chunks == 2) args(norm_residual_rows_kernel<2>);
+  else if (chunks == 3) args(norm_residual_rows_kernel<3>);
+  else args(norm_residual_rows_kernel<4>);
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return fail(SB_ERR_CUDA, std::string("norm rows launch: ") + cudaGetErrorString(e));
   return SB_OK;
 }
 
@@ -1758,7 +1854,8 @@ int sb_strassen_gemm_ex(sb_stream_t stream_, const void* a, const void* b, void*
                         const sb_options* opt, void* workspace, size_t workspace_bytes) {
   cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_);
   const int epi = ep ? ep->kind : SB_EPI_NONE;
-  int st = validate_core(a, b, c, m, n, k, lda, ldb, ldc, bm, bn, bk, out_dtype);
+  const bool narrow = opt && opt->narrow_bn;  // B200 extension: bn a multiple of 128
+  int st = validate_core(a, b, c, m, n, k, lda, ldb, ldc, bm, bn, bk, out_dtype, narrow ? 128 : 256);
   if (st != SB_OK) return st;
   if (epi < SB_EPI_NONE || epi > SB_EPI_NORM_RESIDUAL_ADD)
     return fail(SB_ERR_EPILOGUE, "unknown epilogue kind " + std::to_string(epi));
@@ -1796,9 +1893,12 @@ int sb_strassen_gemm_ex(sb_stream_t stream_, const void* a, const void* b, void*
       return fail(SB_ERR_EPILOGUE, "qk_norm_rope epilogue requires rope_cos=, rope_sin= and rope_scale= "
                                    "(use rope_layout_tables and rope_scale_layout)");
     const int hd = ep->rope_head_dim;
-    if (hd <= 0 || bn % (2 * hd))
-      return fail(SB_ERR_EPILOGUE, "qk_norm_rope needs bn a multiple of 2*head_dim=" + std::to_string(2 * hd) +
-                                       " so a tile half holds whole heads, got bn=" + std::to_string(bn));
+    if (narrow ? (hd <= 0 || bn % hd) : (hd <= 0 || bn % (2 * hd)))
+      return fail(SB_ERR_EPILOGUE,
+                  narrow ? "qk_norm_rope with narrow tiles needs bn a multiple of head_dim=" + std::to_string(hd) +
+                               " so a tile half holds whole half-heads, got bn=" + std::to_string(bn)
+                         : "qk_norm_rope needs bn a multiple of 2*head_dim=" + std::to_string(2 * hd) +
+                               " so a tile half holds whole heads, got bn=" + std::to_string(bn));
     if (!(hd / 2 == 8 || hd / 2 == 16 || hd / 2 == 32 || hd / 2 == 64))
       return fail(SB_ERR_UNSUPPORTED, "qk_norm_rope on B200 supports head_dim in {16, 32, 64, 128}");
     if (ep->ld_rope < bn / 2) return fail(SB_ERR_EPILOGUE, "rope tables must have bn/2 columns");
@@ -1822,13 +1922,8 @@ int sb_strassen_gemm_ex(sb_stream_t stream_, const void* a, const void* b, void*
     apply_options(p, formula, perm, schedule);
     st = dispatch(true, SB_EPI_NONE, true, stream, ta, tb, p);
     if (st != SB_OK) return st;
-    norm_residual_rows_kernel<<<(unsigned)m, 256, 0, stream>>>(
-        reinterpret_cast<const float*>(workspace), n, ep->norm_scale, ep->aux_dtype == SB_F32,
-        ep->residual, ep->ld_residual, ep->residual_dtype == SB_F32, ep->norm_eps,
-        reinterpret_cast<__nv_bfloat16*>(c), ldc);
-    const cudaError_t e = cudaGetLastError();
-    if (e != cudaSuccess) return fail(SB_ERR_CUDA, std::string("norm rows launch: ") + cudaGetErrorString(e));
-    return SB_OK;
+    return launch_norm_rows(stream, reinterpret_cast<const float*>(workspace), m, n, ep,
+                            reinterpret_cast<__nv_bfloat16*>(c), ldc);
   }
 
   GemmParams p = base_params(m, n, k, bm, bn, bk, c, ldc, StrassenPipe::BK);
@@ -1928,12 +2023,7 @@ extern "C" int sb_strassen_gemm_norm_residual_noalloc(sb_stream_t stream_, const
   GemmParams p = base_params(m, n, k, bm, bn, bk, scratch, n, StrassenPipe::BK);
   st = dispatch(true, SB_EPI_NONE, true, stream, ta, tb, p);
   if (st != SB_OK) return st;
-  norm_residual_rows_kernel<<<(unsigned)m, 256, 0, stream>>>(
-      scratch, n, ep->norm_scale, ep->aux_dtype == SB_F32, ep->residual, ep->ld_residual,
-      ep->residual_dtype == SB_F32, ep->norm_eps, reinterpret_cast<__nv_bfloat16*>(c), ldc);
-  const cudaError_t e = cudaGetLastError();
-  if (e != cudaSuccess) return fail(SB_ERR_CUDA, std::string("norm rows launch: ") + cudaGetErrorString(e));
-  return SB_OK;
+  return launch_norm_rows(stream, scratch, m, n, ep, reinterpret_cast<__nv_bfloat16*>(c), ldc);
 }
 
 extern "C" {

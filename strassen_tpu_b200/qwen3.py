@@ -18,9 +18,11 @@ Backends: ``"strassen"`` runs every eligible site on the sm_100a kernels
 (strassen_matmul with the reference's fused epilogues, rms_norm row kernel);
 ``"native"`` is the reference's XLA-classical arm (torch.matmul = cuBLAS on GPU,
 unfused torch math) and is also what the CPU multi-process tests run.  A site
-whose per-rank width cannot satisfy the reference's tile rules (e.g. k at TP=8:
-one 128-wide kv head, below bn = 2*head_dim) uses the native arm for that site,
-the same per-site choice the reference's harness makes.
+whose per-rank width no 256-multiple tile divides (k and v at TP=8: one
+128-wide kv head, below the reference's bn = 2*head_dim) runs on 128-wide tiles
+(strassen_matmul(narrow_bn=True), a B200 extension: one head per tile, so the
+weight needs no relayout); a site that fits neither uses the native arm, the
+same per-site choice the reference's harness makes.
 
 Weights are random (N(0, 0.02); norm weights 1 + N(0, 0.02)) from per-tensor
 seeds: every rank generates the same full tensor and keeps its shard.
@@ -151,6 +153,15 @@ def _pick_bn(width: int, preferred: int, minimum: int) -> int | None:
     return None
 
 
+def _narrow_bn(width: int, head_dim: int) -> int | None:
+    """bn = 128 for a rank-local width that no 256-multiple tile divides (one
+    128-wide head per rank: k and v of Qwen3-8B at TP=8), under
+    strassen_matmul(narrow_bn=True); qk_norm_rope then needs head_dim | 128."""
+    if width % 128 == 0 and 128 % head_dim == 0:
+        return 128
+    return None
+
+
 def _randn(shape, seed, device, scale=0.02, offset=0.0):
     g = torch.Generator(device=device)
     g.manual_seed(seed)
@@ -187,6 +198,7 @@ class _Site:
     weight: torch.Tensor          # [K, N_rank] as the site's GEMM consumes it
     strassen: bool
     bn: int | None = None
+    narrow: bool = False          # bn = 128 under strassen_matmul(narrow_bn=True)
 
 
 @dataclass
@@ -242,12 +254,20 @@ def build_layer(cfg: Qwen3Config, index: int, tp: TensorParallel, device, backen
 
     for name, wt in (("q", wq), ("k", wk)):
         bn = _pick_bn(wt.shape[1], tiles.qk_bn, 2 * hd) if use else None
+        narrow = _narrow_bn(wt.shape[1], hd) if use and bn is None and hd == 128 else None
         if bn is not None:
             layer.sites[name] = _Site(layouts.rope_weight_layout(wt, bn, head_dim=hd), True, bn)
+        elif narrow is not None:
+            # 128-wide tiles hold one head each, already in the a|b half order
+            # qk_norm_rope reads (first half-head, then its rotation partners).
+            layer.sites[name] = _Site(wt, True, narrow, narrow=True)
         else:
             layer.sites[name] = _Site(wt, False)
     bn = _pick_bn(wv.shape[1], tiles.bn, 256) if use else None
-    layer.sites["v"] = _Site(wv, bn is not None, bn)
+    if bn is None and use and _narrow_bn(wv.shape[1], 1) is not None:
+        layer.sites["v"] = _Site(wv, True, 128, narrow=True)
+    else:
+        layer.sites["v"] = _Site(wv, bn is not None, bn)
     bn = _pick_bn(cfg.hidden, tiles.bn, 256) if use and wo.shape[0] % tiles.bk == 0 else None
     layer.sites["o"] = _Site(wo, bn is not None, bn)
     gate_up = torch.cat([wg, wu], dim=1)
@@ -271,7 +291,8 @@ def _qk(layer: Qwen3Layer, name: str, h, heads, norm_w, cos, sin, cos_laid, sin_
         c, s = cos_laid[bn], sin_laid[bn]
         flat = sp.strassen_matmul(h, site.weight, bm=layer.tiles.bm, bn=bn, bk=layer.tiles.bk,
                                   epilogue="qk_norm_rope", rope_cos=c, rope_sin=s, rope_scale=scale,
-                                  rope_head_dim=cfg.head_dim, rope_eps=cfg.rms_eps)
+                                  rope_head_dim=cfg.head_dim, rope_eps=cfg.rms_eps,
+                                  narrow_bn=site.narrow)
         return layouts.rope_layout_to_heads(flat, heads, bn, head_dim=cfg.head_dim)
     x = sp.native_matmul(h, site.weight).view(t, heads, cfg.head_dim)
     x = rms_norm_torch(x, norm_w, cfg.rms_eps)
@@ -285,7 +306,7 @@ def _plain(layer: Qwen3Layer, name: str, h, residual=None, out=None):
         if residual is not None:
             kw = dict(epilogue="residual_add", residual=residual)
         return sp.strassen_matmul(h, site.weight, bm=layer.tiles.bm, bn=site.bn, bk=layer.tiles.bk,
-                                  out=out, **kw)
+                                  out=out, narrow_bn=site.narrow, **kw)
     res = sp.native_matmul(h, site.weight)
     if residual is not None:
         res = (res.float() + residual.float()).to(torch.bfloat16)

@@ -110,14 +110,19 @@ def strassen_matmul(
     vmem_limit_bytes=None,
     out=None,
     workspace=None,
+    narrow_bn=False,
 ):
     """Compute ``a @ b`` with one tile-local classical Strassen level on B200.
 
     Mirrors strassen_pallas.strassen_matmul (strassen_pallas.py:882-1221).
-    Extra keyword arguments: ``out`` (a preallocated output tensor) and
+    Extra keyword arguments: ``out`` (a preallocated output tensor),
     ``workspace`` (a caller-owned uint8 CUDA buffer of at least
     :func:`workspace_bytes` bytes; allocated from torch's caching allocator
-    when omitted).
+    when omitted) and ``narrow_bn`` (B200 extension, no reference counterpart:
+    bn may be any multiple of 128 instead of the reference's TPU lane rule of
+    256, and qk_norm_rope then needs bn % rope_head_dim == 0 -- each half block
+    holds whole half-heads; the tensor-parallel decoder uses it for one-head k/v
+    shards).
     """
     # --- the reference's validation, in its order (strassen_pallas.py:927-1047)
     if a.ndim != 2 or b.ndim != 2:
@@ -170,7 +175,11 @@ def strassen_matmul(
             raise ValueError(
                 "qk_norm_rope epilogue requires rope_cos=, rope_sin= and "
                 "rope_scale= (use rope_layout_tables and rope_scale_layout)")
-        if bn % (2 * rope_head_dim):
+        if narrow_bn and bn % rope_head_dim:
+            raise ValueError(
+                f"qk_norm_rope with narrow_bn needs bn a multiple of head_dim={rope_head_dim} so a "
+                f"tile half holds whole half-heads, got bn={bn}")
+        if not narrow_bn and bn % (2 * rope_head_dim):
             raise ValueError(
                 f"qk_norm_rope needs bn a multiple of 2*head_dim={2 * rope_head_dim} so a "
                 f"tile half holds whole heads, got bn={bn}")
@@ -211,7 +220,12 @@ def strassen_matmul(
     for name, dimension, block in (("M", m, bm), ("N", n, bn), ("K", k, bk)):
         if dimension % block:
             raise ValueError(f"{name}={dimension} is not divisible by {block}")
-    check_tiling(bm, bn, bk)
+    if narrow_bn:
+        if bn % 128:
+            raise ValueError(f"narrow_bn: bn={bn} must be a multiple of 128")
+        check_tiling(bm, 2 * LANE, bk)
+    else:
+        check_tiling(bm, bn, bk)
     out_dt = a.dtype if out_dt is None else out_dt
     if out_dt not in (torch.bfloat16, torch.float32):
         raise ValueError("output_dtype must be BF16 or FP32")
@@ -306,6 +320,7 @@ def strassen_matmul(
     opts = SbOptions()
     opts.formula_variant = FORMULAS[formula_variant]
     opts.block_permutation = int(block_permutation)
+    opts.narrow_bn = 1 if narrow_bn else 0
     if classical_panels or panel_schedule is not None:
         if panel_schedule is not None:
             sched = torch.as_tensor(panel_schedule).to(device=device, dtype=torch.int32).contiguous()

@@ -189,3 +189,26 @@ def test_strassen_b_operands_refuses_host_tensors_and_other_dtypes():
         sb.strassen_b_operands(torch.zeros(512, 512, dtype=torch.float32), bn=256, bk=256)
     with pytest.raises(ValueError, match="CUDA device"):
         sb.strassen_b_operands(torch.zeros(512, 512, dtype=BF), bn=256, bk=256)
+
+
+# --- narrow_bn (B200 extension: bn a multiple of 128) -------------------------
+
+def test_narrow_bn_admits_128_wide_tiles():
+    # Valid arguments reach the device check; without narrow_bn the reference's rule stands.
+    with pytest.raises(ValueError, match="runs on a CUDA device"):
+        call(bn=128, narrow_bn=True)
+    with pytest.raises(ValueError, match="bn=128 must be a multiple of 256"):
+        call(bn=128)
+    with pytest.raises(ValueError, match="narrow_bn: bn=64 must be a multiple of 128"):
+        call(bn=64, narrow_bn=True)
+
+
+def test_narrow_bn_qk_norm_rope_needs_whole_half_heads():
+    rope = dict(epilogue="qk_norm_rope", rope_cos=torch.zeros(256, 64, dtype=BF),
+                rope_sin=torch.zeros(256, 64, dtype=BF), rope_scale=torch.zeros(128, dtype=BF))
+    with pytest.raises(ValueError, match="runs on a CUDA device"):
+        call(bn=128, narrow_bn=True, rope_head_dim=128, **rope)
+    with pytest.raises(ValueError, match="narrow_bn needs bn a multiple of head_dim=256"):
+        call(bn=128, narrow_bn=True, rope_head_dim=256, **rope)
+    with pytest.raises(ValueError, match="needs bn a multiple of 2\\*head_dim=512"):
+        call(bn=256, rope_head_dim=256, **rope)

@@ -146,3 +146,26 @@ def test_tp2_chunked_matches_unchunked_on_cpu_ranks(tmp_path):
     # The all-reduces sum the same partials; only their message sizes differ.
     rel = (outs[1] - outs[0]).norm() / outs[0].norm()
     assert rel < 1e-2, rel.item()
+
+
+def test_one_head_kv_shards_take_narrow_tiles():
+    """At TP=8 with 8 kv heads every rank holds one 128-wide k and v head: those
+    sites run on 128-wide Strassen tiles (narrow_bn) instead of the native arm,
+    with the weight in its natural order (one head per tile is already the rope
+    layout)."""
+    class FakeTP:
+        rank, world = 3, 8
+
+    cfg = qwen3.Qwen3Config(hidden=1024, layers=1, heads=16, kv_heads=8, head_dim=128,
+                            intermediate=4096, vocab=1000)
+    layer = qwen3.build_layer(cfg, 0, FakeTP(), "cpu", backend="strassen")
+    native = qwen3.build_layer(cfg, 0, FakeTP(), "cpu", backend="native")
+    for name in ("k", "v"):
+        site = layer.sites[name]
+        assert (site.strassen, site.bn, site.narrow) == (True, 128, True), name
+        assert torch.equal(site.weight, native.sites[name].weight), name
+    q = layer.sites["q"]
+    assert (q.strassen, q.bn, q.narrow) == (True, 256, False)
+    # Two heads per rank fit the reference's bn = 2*head_dim rule: no narrow tiles.
+    layer2 = qwen3.build_layer(cfg, 0, type("TP4", (), {"rank": 1, "world": 4})(), "cpu", backend="strassen")
+    assert (layer2.sites["k"].bn, layer2.sites["k"].narrow) == (256, False)
