@@ -65,6 +65,10 @@ def parse():
                    help="time only the GEMM launches (no comparisons, e2e, CPU baseline or decoder); "
                         "the command the committed ncu captures run")
     p.add_argument("--no-decoder", action="store_true", help="skip the decoder measurement of the GEMM run")
+    p.add_argument("--epilogue", default="none", choices=["none", "norm_residual_add"],
+                   help="GEMM workload with a fused epilogue (one-CTA kernel): norm_residual_add runs "
+                        "the GEMM into an fp32 workspace and the row pass, tile (1024, N, 512) since "
+                        "the norm spans the row; the command the row pass's ncu capture runs")
     p.add_argument("--workload", default="gemm", choices=["gemm", "qwen3-8b", "qwen3-32b"],
                    help="gemm: the 8192^3 Strassen GEMM (default, the driver's line); "
                         "qwen3-*: tensor-parallel decoder prefill tokens/s (BASELINE configs 4/5)")
@@ -257,7 +261,22 @@ def run_ours(args):
     flops = 2.0 * M * N * K
 
     launches_per_step = 1
-    if args.kernel == "pair-planes":
+    tile = TILE
+    if args.epilogue != "none" and args.kernel != "single":
+        raise SystemExit("--epilogue runs on the one-CTA kernel (--kernel single)")
+    if args.epilogue == "norm_residual_add":
+        tile = (TILE[0], N, TILE[2])  # the norm spans the whole row: bn = N
+        g = torch.Generator(device=device).manual_seed(SEED_B + 1)
+        residual = torch.randn(M, N, device=device, generator=g).to(torch.bfloat16)
+        norm_scale = (1.0 + 0.02 * torch.randn(N, device=device, generator=g)).to(torch.bfloat16)
+        workspace = torch.empty(sb.workspace_bytes(M, N, K, epilogue="norm_residual_add"),
+                                dtype=torch.uint8, device=device)
+        launches_per_step = 2  # the GEMM into the fp32 workspace, the row pass
+
+        def step():
+            sb.strassen_matmul(a, b, bm=tile[0], bn=tile[1], bk=tile[2], epilogue="norm_residual_add",
+                               residual=residual, norm_scale=norm_scale, workspace=workspace, out=c)
+    elif args.kernel == "pair-planes":
         planes = torch.empty(7, K // 2, N // 2, dtype=torch.bfloat16, device=device)
         launches_per_step = 2
 
@@ -325,7 +344,7 @@ def run_ours(args):
     achieved = raw_flops / (ms * 1e-3) / 1e12
     traffic = None
     traffic_path = REPO / "profiles" / "strassen_gemm_8192_traffic.json"
-    if traffic_path.exists():
+    if traffic_path.exists() and args.epilogue == "none":
         traffic = json.loads(traffic_path.read_text()).get("dram_bytes_per_launch")
 
     # --- comparison arms on identical tensors (informational)
@@ -390,7 +409,8 @@ def run_ours(args):
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-        "config": {"workload": f"strassen_gemm_{M}x{N}x{K}_bf16", "tile": list(TILE),
+        "config": {"workload": f"strassen_gemm_{M}x{N}x{K}_bf16", "tile": list(tile),
+                   "epilogue": args.epilogue,
                    "kernel": {"single": "one-CTA (sb_strassen_gemm)",
                               "pair": "two-CTA cluster (sb_strassen_gemm_pair)",
                               "pair-planes": "B operand planes + two-CTA cluster (sb_strassen_b_operands, "
