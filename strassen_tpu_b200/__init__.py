@@ -30,12 +30,13 @@ from .strassen import (
     strassen_matmul_streamed,
     workspace_bytes,
 )
+from .torch_ops import strassen_matmul_op  # registers torch.ops.strassen_b200.strassen_matmul
 
 __all__ = [
     "TUNED_BM", "TUNED_BN", "TUNED_BK",
     "check_tiling", "classical_matmul", "native_matmul", "rms_norm", "strassen_matmul",
     "pair_matmul", "quad_matmul", "StrassenBOperands", "strassen_b_operands", "strassen_matmul_lhs_transposed", "strassen_matmul_streamed", "tuned_matmul",
-    "workspace_bytes",
+    "workspace_bytes", "strassen_matmul_op",
     "rope_layout_tables", "rope_layout_to_heads", "rope_scale_layout", "rope_weight_layout",
     "swiglu_weight_layout",
 ]
