@@ -61,6 +61,8 @@ def parse():
                    help="GEMM workload: the one-CTA Strassen kernel, the two-CTA cluster kernel, the "
                         "two-CTA kernel on B operand planes formed inside each step, or the four-CTA "
                         "paired-tensor-core kernel (its operand passes inside each step)")
+    p.add_argument("--quad-raster", type=int, default=0,
+                   help="--kernel quad: product-row tiles per column sweep (0 = the kernel's default)")
     p.add_argument("--profile", action="store_true",
                    help="time only the GEMM launches (no comparisons, e2e, CPU baseline or decoder); "
                         "the command the committed ncu captures run")
@@ -289,7 +291,8 @@ def run_ours(args):
         launches_per_step = 3  # A operand pass, B operand planes, the four-CTA GEMM
 
         def step():
-            sb.quad_matmul(a, b, bm=TILE[0], bn=TILE[1], bk=TILE[2], out=c, workspace=workspace)
+            sb.quad_matmul(a, b, bm=TILE[0], bn=TILE[1], bk=TILE[2], out=c, workspace=workspace,
+                           raster=args.quad_raster)
     else:
         gemm = sb.pair_matmul if args.kernel == "pair" else sb.strassen_matmul
 

@@ -217,7 +217,8 @@ SB_API int sb_strassen_gemm_pair_planes(sb_stream_t stream,
  * operands (a pass over A) and B's operand planes (sb_strassen_b_operands) in
  * `workspace` (sb_quad_workspace_bytes(m, n, k) bytes, 16-byte aligned) and
  * then runs the GEMM, all on `stream`.  Needs M % 512 == 0, bn % 256 == 0 and
- * bk % 256 == 0 (SB_ERR_TILING otherwise).
+ * bk % 256 == 0 (SB_ERR_TILING otherwise).  `raster`: product-row tiles the
+ * cluster tiles walk per column sweep (L2 reuse; 0 = the kernel's default of 2).
  */
 SB_API size_t sb_quad_workspace_bytes(int64_t m, int64_t n, int64_t k);
 SB_API int sb_strassen_gemm_quad(sb_stream_t stream,
@@ -225,7 +226,7 @@ SB_API int sb_strassen_gemm_quad(sb_stream_t stream,
                                  int64_t m, int64_t n, int64_t k,
                                  int64_t lda, int64_t ldb, int64_t ldc,
                                  int32_t bm, int32_t bn, int32_t bk, int32_t out_dtype,
-                                 void* workspace, size_t workspace_bytes);
+                                 void* workspace, size_t workspace_bytes, int32_t raster);
 
 /*
  * sb_strassen_gemm_norm_residual_noalloc -- the norm_residual_add epilogue of

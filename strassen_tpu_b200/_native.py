@@ -99,7 +99,7 @@ SIGNATURES = {
     "sb_quad_workspace_bytes": (_c_size, [_c_i64, _c_i64, _c_i64]),
     "sb_strassen_gemm_quad": (_c_int, [_c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_i64, _c_i64, _c_i64,
                                        _c_i64, _c_i64, _c_i64, _c_int, _c_int, _c_int, _c_int,
-                                       _c_ptr, _c_size]),
+                                       _c_ptr, _c_size, _c_int]),
     "sb_strassen_gemm_lhs_transposed": (_c_int, [_c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_i64, _c_i64,
                                                  _c_i64, _c_i64, _c_i64, _c_i64, _c_int, _c_int,
                                                  _c_int, _c_int]),

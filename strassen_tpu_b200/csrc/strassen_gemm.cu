@@ -247,6 +247,7 @@ struct GemmParams {
   int32_t swap_m, swap_k, swap_n;  // block_permutation bits
   const int32_t* panel_schedule;   // device [num_panels], nonzero = exact panel; may be null
   int32_t num_panels;
+  int32_t raster;                  // four-CTA kernel: tile rows per column sweep (0 = its default)
 };
 
 // Whether K chunk c lies in an exact classical panel.
@@ -1783,8 +1784,9 @@ int check_quad_shape(int64_t m, int32_t bn, int32_t bk) {
 // A operand pass, B planes (unless given) and the GEMM, in stream order.
 int run_quad(cudaStream_t stream, const void* a, const void* b, const void* b_planes, void* c, int64_t m,
              int64_t n, int64_t k, int64_t lda, int64_t ldb, int64_t ldc, int32_t bm, int32_t bn, int32_t bk,
-             int32_t out_dtype, void* workspace, size_t workspace_bytes) {
+             int32_t out_dtype, void* workspace, size_t workspace_bytes, int32_t raster) {
   if (ldc < n) return fail(SB_ERR_ALIGNMENT, "ldc must be >= N");
+  if (raster < 0) return fail(SB_ERR_UNSUPPORTED, "raster must be >= 0 (0 = the kernel's default)");
   int st = check_quad_shape(m, bn, bk);
   if (st != SB_OK) return st;
   const size_t need = quad_ops_bytes(m, k) + (b_planes ? 0 : quad_planes_bytes(k, n));
@@ -1815,6 +1817,7 @@ int run_quad(cudaStream_t stream, const void* a, const void* b, const void* b_pl
   GemmParams p = base_params(m, n, k, bm, bn, bk, c, ldc, 16);
   p.tiles_m = (int32_t)(p.Mp / quad::kTileRows);
   p.tiles_n = (int32_t)(p.Np / quad::kCols);
+  p.raster = raster;
   return out_dtype == SB_F32 ? launch_quad<true>(stream, maps, p) : launch_quad<false>(stream, maps, p);
 }
 
@@ -2207,11 +2210,11 @@ size_t sb_quad_workspace_bytes(int64_t m, int64_t n, int64_t k) {
 
 int sb_strassen_gemm_quad(sb_stream_t stream_, const void* a, const void* b, void* c, int64_t m, int64_t n,
                           int64_t k, int64_t lda, int64_t ldb, int64_t ldc, int32_t bm, int32_t bn, int32_t bk,
-                          int32_t out_dtype, void* workspace, size_t workspace_bytes) {
+                          int32_t out_dtype, void* workspace, size_t workspace_bytes, int32_t raster) {
   int st = validate_core(a, b, c, m, n, k, lda, ldb, ldc, bm, bn, bk, out_dtype);
   if (st != SB_OK) return st;
   return run_quad(reinterpret_cast<cudaStream_t>(stream_), a, b, nullptr, c, m, n, k, lda, ldb, ldc, bm, bn, bk,
-                  out_dtype, workspace, workspace_bytes);
+                  out_dtype, workspace, workspace_bytes, raster);
 }
 
 const char* sb_version(void) { return "strassen_b200 0.1.0 (sm_100a, tcgen05)"; }

@@ -52,9 +52,12 @@ constexpr int kThreadsQ = 14 * 32;
 #endif
 constexpr int kGroup = SB_QUAD_GROUP;  // K steps per hand-off to the MMA warp
 #ifndef SB_QUAD_RASTER
-#define SB_QUAD_RASTER 16
+#define SB_QUAD_RASTER 2
 #endif
-constexpr int kRaster = SB_QUAD_RASTER;  // product-row tiles per column sweep (L2 reuse)
+// Default product-row tiles per column sweep (GemmParams::raster overrides it).
+// Two keeps A' (the larger operand stream) in L2 across the column tiles in
+// flight: 2.7 GB of DRAM reads per 8192^3 launch against 6.8 GB at 16.
+constexpr int kRaster = SB_QUAD_RASTER;
 
 // Stage layout (bytes, the same in every CTA).
 struct Geo {
@@ -204,10 +207,11 @@ __global__ void __launch_bounds__(quad::kThreadsQ, 1)
 
   // Grouped rasterisation over cluster tiles (as the other kernels).
   const int tile = blockIdx.x >> 2;
-  const int per_group = kRaster * p.tiles_n;
+  const int raster = p.raster > 0 ? p.raster : kRaster;
+  const int per_group = raster * p.tiles_n;
   const int group = tile / per_group;
-  const int first_m = group * kRaster;
-  const int rows_in_group = min(p.tiles_m - first_m, kRaster);
+  const int first_m = group * raster;
+  const int rows_in_group = min(p.tiles_m - first_m, raster);
   const int in_group = tile - group * per_group;
   const int tt0 = (first_m + in_group % rows_in_group) * kTileRows;  // first product row of the tile
   const int t0 = tt0 + 128 * (int)half;                               // this CTA's first product row

@@ -654,7 +654,8 @@ def pair_matmul(a, b, *, bm=TUNED_BM, bn=TUNED_BN, bk=TUNED_BK, output_dtype=Non
     return out
 
 
-def quad_matmul(a, b, *, bm=TUNED_BM, bn=TUNED_BN, bk=TUNED_BK, output_dtype=None, out=None, workspace=None):
+def quad_matmul(a, b, *, bm=TUNED_BM, bn=TUNED_BN, bk=TUNED_BK, output_dtype=None, out=None, workspace=None,
+                raster=0):
     """``strassen_matmul(a, b, bm=, bn=, bk=, output_dtype=)`` without an epilogue,
     on the four-CTA kernel (``sb_strassen_gemm_quad``): clusters of two CTA
     pairs on B200's paired tensor cores (tcgen05 ``cta_group::2``), one
@@ -666,7 +667,8 @@ def quad_matmul(a, b, *, bm=TUNED_BM, bn=TUNED_BN, bk=TUNED_BK, output_dtype=Non
     ``sb_quad_workspace_bytes`` of the shape; allocated here unless
     ``workspace=`` passes a uint8 CUDA tensor at least that large) before the
     GEMM, all on the current stream.  Needs M % 512 == 0, bn % 256 == 0 and
-    bk % 256 == 0.
+    bk % 256 == 0.  ``raster``: product-row tiles per column sweep of the
+    cluster tiles (0 = the kernel's default); the result does not depend on it.
     """
     if a.ndim != 2 or b.ndim != 2:
         raise ValueError("quad_matmul expects two rank-2 matrices")
@@ -700,7 +702,7 @@ def quad_matmul(a, b, *, bm=TUNED_BM, bn=TUNED_BN, bk=TUNED_BK, output_dtype=Non
     with torch.cuda.device(device):
         status = lib.sb_strassen_gemm_quad(_stream_handle(device), a.data_ptr(), b.data_ptr(), out.data_ptr(),
                                            m, n, k, _ld(a), _ld(b), _ld(out), bm, bn, bk, od,
-                                           workspace.data_ptr(), workspace.numel())
+                                           workspace.data_ptr(), workspace.numel(), int(raster))
     _native.check(status)
     return out
 

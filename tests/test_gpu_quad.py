@@ -91,6 +91,15 @@ def test_quad_matches_one_cta_kernel(m, n, k):
     assert _native.device_status() == 0
 
 
+def test_quad_raster_does_not_change_the_result():
+    import strassen_tpu_b200 as sb
+    a = dev_bf16(ref.normal_bf16((2048, 1024), 5))
+    b = dev_bf16(ref.normal_bf16((1024, 2048), 6))
+    outs = [sb.quad_matmul(a, b, bm=512, bn=512, bk=512, raster=r) for r in (0, 1, 3, 16)]
+    for o in outs[1:]:
+        assert torch.equal(o, outs[0])
+
+
 def test_quad_accumulators_reset_between_calls():
     import strassen_tpu_b200 as sb
     a = dev_bf16(ref.normal_bf16((512, 512), 1))
