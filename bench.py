@@ -82,6 +82,13 @@ def parse():
     p.add_argument("--chunks", type=int, default=None,
                    help="decoder: token chunks pipelined so all-reduces overlap compute "
                         "(default: 2 with more than one rank, else 1)")
+    p.add_argument("--site-times", type=int, default=0, metavar="TP",
+                   help="decoder: time every op of one layer of rank 0's shard at tensor-parallel size TP "
+                        "for both backends on one GPU (per-rank shapes of a TP run, no collectives)")
+    p.add_argument("--site-policy", default="measured", choices=["measured", "all"],
+                   help="decoder, strassen backend: each GEMM site on the faster of its Strassen and "
+                        "native arms at the shard's shapes (measured before the timed region), or every "
+                        "site a Strassen tile fits on Strassen")
     p.add_argument("--collective", default="nccl", choices=["nccl", "p2p"],
                    help="decoder: row-parallel sums by NCCL all-reduce (residual fused on rank 0) "
                         "or by sb_p2p_reduce over NVLink peer memory")
@@ -456,10 +463,15 @@ def nccl_init_log(rank: int, world: int, device) -> None:
 
 
 def measure_prefill(workload, tp, device, steps, warmup, chunks, backend="strassen", eager=False, layers=None,
-                    group=None):
+                    group=None, site_policy="measured"):
     """Qwen3 prefill on `tp`'s ranks: ms per forward (CUDA events, max over the
     group's ranks), tokens/s, FLOP rate, an end-to-end figure with the token
-    ids copied in and the logits copied out, and the launch count per step."""
+    ids copied in and the logits copied out, and the launch count per step.
+
+    site_policy "measured": each GEMM site takes the faster of its Strassen and
+    native arms at this shard's shapes (qwen3.measured_native_sites, timed before
+    the model is built, outside the timed region); "all": every site a Strassen
+    tile fits runs on Strassen."""
     import torch
     import torch.distributed as dist
 
@@ -467,7 +479,10 @@ def measure_prefill(workload, tp, device, steps, warmup, chunks, backend="strass
 
     cfg, (batch, seq) = ({"qwen3-8b": (qwen3.QWEN3_8B, (8, 2048)),
                           "qwen3-32b": (qwen3.QWEN3_32B, (16, 4096))}[workload])
-    model = qwen3.Qwen3Prefill(cfg, tp, device, backend=backend, layers=layers)
+    native_sites = frozenset()
+    if backend == "strassen" and site_policy == "measured":
+        native_sites = qwen3.measured_native_sites(cfg, tp, batch * seq // max(1, chunks), device, seq=seq)
+    model = qwen3.Qwen3Prefill(cfg, tp, device, backend=backend, layers=layers, native_sites=native_sites)
     g = torch.Generator().manual_seed(20260911)
     tokens_host = torch.randint(0, cfg.vocab, (batch, seq), generator=g).pin_memory()
     tokens = tokens_host.to(device)
@@ -534,7 +549,8 @@ def measure_prefill(workload, tp, device, steps, warmup, chunks, backend="strass
     tok = batch * seq
     return {"ms": ms, "tokens_per_s": tok / (ms * 1e-3), "tflops": flops / (ms * 1e-3) / 1e12,
             "e2e_tokens_per_s": tok / (e2e_ms * 1e-3), "launches": launches, "batch": batch, "seq": seq,
-            "layers": n_layers, "strassen_sites": strassen_sites, "vocab": cfg.vocab}
+            "layers": n_layers, "strassen_sites": strassen_sites, "vocab": cfg.vocab,
+            "site_policy": site_policy if backend == "strassen" else None}
 
 
 def decoder_scaling(rank, world, local, device, workload="qwen3-8b", steps=3, warmup=1):
@@ -567,6 +583,7 @@ def decoder_scaling(rank, world, local, device, workload="qwen3-8b", steps=3, wa
         "config": {"model": workload, "global_batch": tpn["batch"], "seq_len": tpn["seq"],
                    "layers": tpn["layers"], "parallelism": f"tp{world}", "collective": "nccl",
                    "token_chunks": chunks_n, "cuda_graph": True, "strassen_sites": tpn["strassen_sites"],
+                   "site_policy": tpn["site_policy"], "tp1_strassen_sites": tp1["strassen_sites"],
                    "lm_head": "last position per sequence", "steps": steps, "warmup": warmup,
                    "tp1": "rank 0's GPU alone, same box, same run"},
         "gpu_launches_per_step": tpn["launches"],
@@ -592,7 +609,7 @@ def run_decoder(args):
     chunks = args.chunks if args.chunks is not None else (2 if world > 1 else 1)
     with ClockSampler(device.index) as clocks:
         r = measure_prefill(args.workload, tp, device, args.steps, args.warmup, chunks, backend=args.backend,
-                            eager=args.eager, layers=args.layers)
+                            eager=args.eager, layers=args.layers, site_policy=args.site_policy)
     tp.close()
     if world > 1:
         dist.barrier(device_ids=[local])
@@ -608,6 +625,7 @@ def run_decoder(args):
         "config": {"workload": args.workload, "model": args.workload, "global_batch": r["batch"],
                    "seq_len": r["seq"], "layers": r["layers"], "parallelism": f"tp{world}",
                    "backend": args.backend, "strassen_sites": r["strassen_sites"],
+                   "site_policy": r["site_policy"],
                    "token_chunks": chunks, "cuda_graph": not args.eager,
                    "collective": args.collective if world > 1 else None,
                    "lm_head": "last position per sequence"},
@@ -621,10 +639,34 @@ def run_decoder(args):
     return 0
 
 
+def run_site_times(args):
+    """One line: per-op device ms of one decoder layer at TP = --site-times, both backends."""
+    import torch
+
+    from strassen_tpu_b200 import qwen3
+
+    cfg, (batch, seq) = ({"qwen3-8b": (qwen3.QWEN3_8B, (8, 2048)),
+                          "qwen3-32b": (qwen3.QWEN3_32B, (16, 4096))}[args.workload])
+    tp = args.site_times
+    chunks = args.chunks if args.chunks is not None else (2 if tp > 1 else 1)
+    tokens = batch * seq // chunks
+    device = torch.device("cuda", 0)
+    torch.cuda.set_device(device)
+    times = qwen3.site_times(cfg, tp, tokens, device, steps=args.steps, warmup=args.warmup, seq=seq)
+    total = {arm: sum(t[arm] for t in times.values()) for arm in ("strassen", "native")}
+    print(json.dumps({"metric": f"{args.workload.replace('-', '_')}_layer_op_ms", "unit": "ms",
+                      "tp": tp, "token_rows": tokens, "token_chunks": chunks, "ops": times,
+                      "layer_ms": total, "steps": args.steps, "warmup": args.warmup,
+                      "note": "rank 0's shard on one GPU; collectives not included"}), flush=True)
+    return 0
+
+
 def main():
     args = parse()
     if args.impl == "reference":
         return run_reference(args)
+    if args.workload != "gemm" and args.site_times:
+        return run_site_times(args)
     if args.workload != "gemm":
         return run_decoder(args)
     return run_ours(args)

@@ -227,8 +227,12 @@ class Qwen3Layer:
 
 
 def build_layer(cfg: Qwen3Config, index: int, tp: TensorParallel, device, backend="strassen",
-                tiles: StrassenTiles = StrassenTiles(), seed: int = 20260910) -> Qwen3Layer:
-    """Random-init layer `index`, sharded for this rank and laid out for the fused epilogues."""
+                tiles: StrassenTiles = StrassenTiles(), seed: int = 20260910,
+                native_sites=frozenset()) -> Qwen3Layer:
+    """Random-init layer `index`, sharded for this rank and laid out for the fused epilogues.
+
+    ``native_sites``: GEMM sites (q, k, v, o, up, down) that take the native arm
+    even where a Strassen tile fits (see :func:`measured_native_sites`)."""
     if cfg.heads % tp.world or cfg.kv_heads % tp.world or cfg.intermediate % tp.world:
         raise ValueError(f"tensor parallel size {tp.world} does not divide heads/kv heads/intermediate")
     hd, r, w = cfg.head_dim, tp.rank, tp.world
@@ -253,8 +257,9 @@ def build_layer(cfg: Qwen3Config, index: int, tp: TensorParallel, device, backen
     wd = _randn((cfg.intermediate, cfg.hidden), base + 16, device)[r * ir:(r + 1) * ir].contiguous()
 
     for name, wt in (("q", wq), ("k", wk)):
-        bn = _pick_bn(wt.shape[1], tiles.qk_bn, 2 * hd) if use else None
-        narrow = _narrow_bn(wt.shape[1], hd) if use and bn is None and hd == 128 else None
+        on = use and name not in native_sites
+        bn = _pick_bn(wt.shape[1], tiles.qk_bn, 2 * hd) if on else None
+        narrow = _narrow_bn(wt.shape[1], hd) if on and bn is None and hd == 128 else None
         if bn is not None:
             layer.sites[name] = _Site(layouts.rope_weight_layout(wt, bn, head_dim=hd), True, bn)
         elif narrow is not None:
@@ -263,20 +268,23 @@ def build_layer(cfg: Qwen3Config, index: int, tp: TensorParallel, device, backen
             layer.sites[name] = _Site(wt, True, narrow, narrow=True)
         else:
             layer.sites[name] = _Site(wt, False)
-    bn = _pick_bn(wv.shape[1], tiles.bn, 256) if use else None
-    if bn is None and use and _narrow_bn(wv.shape[1], 1) is not None:
+    on = use and "v" not in native_sites
+    bn = _pick_bn(wv.shape[1], tiles.bn, 256) if on else None
+    if bn is None and on and _narrow_bn(wv.shape[1], 1) is not None:
         layer.sites["v"] = _Site(wv, True, 128, narrow=True)
     else:
         layer.sites["v"] = _Site(wv, bn is not None, bn)
-    bn = _pick_bn(cfg.hidden, tiles.bn, 256) if use and wo.shape[0] % tiles.bk == 0 else None
+    on = use and "o" not in native_sites
+    bn = _pick_bn(cfg.hidden, tiles.bn, 256) if on and wo.shape[0] % tiles.bk == 0 else None
     layer.sites["o"] = _Site(wo, bn is not None, bn)
     gate_up = torch.cat([wg, wu], dim=1)
-    bn = _pick_bn(2 * ir, tiles.up_bn, 256) if use else None
+    bn = _pick_bn(2 * ir, tiles.up_bn, 256) if use and "up" not in native_sites else None
     if bn is not None and ir % (bn // 2) == 0:
         layer.sites["up"] = _Site(layouts.swiglu_weight_layout(gate_up, bn), True, bn)
     else:
         layer.sites["up"] = _Site(gate_up, False)
-    bn = _pick_bn(cfg.hidden, tiles.bn, 256) if use and ir % tiles.bk == 0 else None
+    on = use and "down" not in native_sites
+    bn = _pick_bn(cfg.hidden, tiles.bn, 256) if on and ir % tiles.bk == 0 else None
     layer.sites["down"] = _Site(wd, bn is not None, bn)
     return layer
 
@@ -429,13 +437,15 @@ class Qwen3Prefill:
     """
 
     def __init__(self, cfg: Qwen3Config, tp: TensorParallel, device, backend="strassen",
-                 tiles: StrassenTiles = StrassenTiles(), layers: int | None = None, seed=20260910):
+                 tiles: StrassenTiles = StrassenTiles(), layers: int | None = None, seed=20260910,
+                 native_sites=frozenset()):
         self.cfg, self.tp, self.device, self.backend = cfg, tp, device, backend
         self.embed = _randn((cfg.vocab, cfg.hidden), seed, device)
         self.final_norm = _randn((cfg.hidden,), seed + 7, device, offset=1.0)
         self.lm_head = _randn((cfg.hidden, cfg.vocab), seed + 8, device)
         n = cfg.layers if layers is None else layers
-        self.blocks = [build_layer(cfg, i, tp, device, backend, tiles, seed) for i in range(n)]
+        self.native_sites = frozenset(native_sites)
+        self.blocks = [build_layer(cfg, i, tp, device, backend, tiles, seed, self.native_sites) for i in range(n)]
 
     def rope(self, batch: int, seq: int):
         pos = torch.arange(seq, device=self.device).repeat(batch)
@@ -516,3 +526,105 @@ def prefill_flops(cfg: Qwen3Config, batch: int, seq: int, layers: int | None = N
         + 2 * t * cfg.intermediate * cfg.hidden
     attn = 2 * 2 * batch * cfg.heads * hd * seq * seq / 2
     return n * (gemm + attn) + 2 * batch * cfg.hidden * cfg.vocab
+
+
+class _Shard:
+    """Rank and world size of one tensor-parallel shard, without a process group."""
+
+    def __init__(self, rank: int, world: int):
+        self.rank, self.world = rank, world
+
+
+def site_times(cfg: Qwen3Config, world: int, tokens: int, device, steps: int = 20, warmup: int = 3,
+               seq: int = 2048) -> dict:
+    """Device time (ms, CUDA events, mean of `steps` calls) of every op of one
+    decoder layer of rank 0's shard at tensor-parallel size `world`, for both
+    backends, on one GPU: the per-rank shapes of a TP=`world` prefill on `tokens`
+    token rows (``tokens // seq`` whole sequences), without its collectives.
+
+    Returns {op: {"strassen": ms, "native": ms, "strassen_site": bool, "bn": int|None}}
+    for ln1, q, k, v, attention, o, ln2, up, down, where o and down include the
+    residual add that rank 0 fuses.  Sites whose shard fits no Strassen tile run
+    the native arm in both columns (strassen_site False)."""
+    shard = _Shard(0, world)
+    layers = {b: build_layer(cfg, 0, shard, device, backend=b) for b in ("strassen", "native")}
+    model = Qwen3Prefill.__new__(Qwen3Prefill)
+    model.cfg, model.device, model.blocks = cfg, device, [layers["strassen"]]
+    batch = max(1, tokens // seq)
+    rope = model.rope(batch, seq)
+    cos, sin, cos_laid, sin_laid = rope
+    g = torch.Generator(device=device).manual_seed(20260912)
+    x = torch.randn(tokens, cfg.hidden, device=device, generator=g).to(torch.bfloat16)
+    hq, hkv, hd, ir = cfg.heads // world, cfg.kv_heads // world, cfg.head_dim, cfg.intermediate // world
+    attn_in = torch.randn(tokens, hq * hd, device=device, generator=g).to(torch.bfloat16)
+    g_in = torch.randn(tokens, ir, device=device, generator=g).to(torch.bfloat16)
+    qkv = [torch.randn(batch, n, seq, hd, device=device, generator=g).to(torch.bfloat16) for n in (hq, hkv, hkv)]
+
+    def ops(layer):
+        norm = sp.rms_norm if layer.backend == "strassen" else (lambda a, b, eps: rms_norm_torch(a, b, eps))
+
+        def up():
+            site = layer.sites["up"]
+            if site.strassen:
+                return sp.strassen_matmul(x, site.weight, bm=layer.tiles.bm, bn=site.bn, bk=layer.tiles.bk,
+                                          epilogue="swiglu", product_aware_swiglu=True, interleave_products=True)
+            gu = sp.native_matmul(x, site.weight).float()
+            gate, upv = gu.chunk(2, dim=-1)
+            return (F.silu(gate) * upv).to(torch.bfloat16)
+
+        return {
+            "ln1": lambda: norm(x, layer.ln1, cfg.rms_eps),
+            "q": lambda: _qk(layer, "q", x, hq, layer.q_norm, cos, sin, cos_laid, sin_laid),
+            "k": lambda: _qk(layer, "k", x, hkv, layer.k_norm, cos, sin, cos_laid, sin_laid),
+            "v": lambda: _plain(layer, "v", x),
+            "attention": lambda: F.scaled_dot_product_attention(*qkv, is_causal=True, enable_gqa=hkv != hq),
+            "o": lambda: _plain(layer, "o", attn_in, residual=x),
+            "ln2": lambda: norm(x, layer.ln2, cfg.rms_eps),
+            "up": up,
+            "down": lambda: _plain(layer, "down", g_in, residual=x),
+        }
+
+    def timed(fn):
+        for _ in range(warmup):
+            fn()
+        torch.cuda.synchronize(device)
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record()
+        for _ in range(steps):
+            fn()
+        end.record()
+        torch.cuda.synchronize(device)
+        return start.elapsed_time(end) / steps
+
+    out = {}
+    s_ops, n_ops = ops(layers["strassen"]), ops(layers["native"])
+    for name in s_ops:
+        site = layers["strassen"].sites.get(name)
+        out[name] = {"strassen": timed(s_ops[name]), "native": timed(n_ops[name]),
+                     "strassen_site": bool(site.strassen) if site is not None else None,
+                     "bn": site.bn if site is not None and site.strassen else None}
+    return out
+
+
+GEMM_SITES = ("q", "k", "v", "o", "up", "down")
+
+
+def measured_native_sites(cfg: Qwen3Config, tp, tokens: int, device, seq: int = 2048, steps: int = 10,
+                          warmup: int = 3) -> frozenset:
+    """The GEMM sites whose native arm (cuBLAS + unfused torch epilogue) is faster
+    than the Strassen site at this rank's shard shapes: the per-site choice the
+    reference's harness makes from measurements (it runs Strassen only at the
+    sites where it wins).  Rank 0 of ``tp``'s group times one layer with
+    :func:`site_times` on ``tokens`` token rows and every rank takes its answer,
+    so all ranks run the same kernels."""
+    choice = None
+    if tp.rank == 0:
+        times = site_times(cfg, tp.world, tokens, device, steps=steps, warmup=warmup, seq=seq)
+        choice = sorted(name for name in GEMM_SITES
+                        if times[name]["strassen_site"] and times[name]["native"] < times[name]["strassen"])
+    if tp.world > 1:
+        box = [choice]
+        src = tp.dist.get_global_rank(tp.group, 0) if tp.group is not None else 0
+        tp.dist.broadcast_object_list(box, src=src, group=tp.group)
+        choice = box[0]
+    return frozenset(choice)

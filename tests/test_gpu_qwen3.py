@@ -63,3 +63,28 @@ def test_captured_prefill_replays_the_eager_forward():
         torch.cuda.synchronize()
         cap.release()
         assert torch.equal(got, want)
+
+
+def test_measured_site_choice_and_mixed_layer():
+    """measured_native_sites names only GEMM sites whose native arm it timed faster;
+    a layer built with that choice matches the native arm like the all-Strassen one."""
+    cfg = qwen3.QWEN3_8B
+    tp = qwen3.TensorParallel()
+    batch, seq = 1, 2048
+    times = qwen3.site_times(cfg, 8, batch * seq, "cuda", steps=3, warmup=1, seq=seq)
+    assert set(times) == {"ln1", "q", "k", "v", "attention", "o", "ln2", "up", "down"}
+    assert all(t["strassen"] > 0 and t["native"] > 0 for t in times.values())
+    assert times["k"]["bn"] == 128 and times["v"]["bn"] == 128  # one-head shards on narrow tiles
+    chosen = qwen3.measured_native_sites(cfg, tp, batch * seq, "cuda", seq=seq, steps=3, warmup=1)
+    assert chosen <= set(qwen3.GEMM_SITES)
+    mixed = qwen3.build_layer(cfg, 0, tp, "cuda", backend="strassen", native_sites=frozenset({"v", "up"}))
+    native = qwen3.build_layer(cfg, 0, tp, "cuda", backend="native")
+    assert not mixed.sites["v"].strassen and not mixed.sites["up"].strassen and mixed.sites["q"].strassen
+    model = qwen3.Qwen3Prefill.__new__(qwen3.Qwen3Prefill)
+    model.cfg, model.device, model.blocks = cfg, "cuda", [mixed]
+    rope = model.rope(batch, seq)
+    x = torch.randn(batch * seq, cfg.hidden, device="cuda", generator=torch.Generator("cuda").manual_seed(4)
+                    ).to(torch.bfloat16)
+    got = qwen3.layer_forward(mixed, x, batch, seq, rope)
+    want = qwen3.layer_forward(native, x, batch, seq, rope)
+    assert _rel(got - x, want - x) < 3e-2

@@ -169,3 +169,15 @@ def test_one_head_kv_shards_take_narrow_tiles():
     # Two heads per rank fit the reference's bn = 2*head_dim rule: no narrow tiles.
     layer2 = qwen3.build_layer(cfg, 0, type("TP4", (), {"rank": 1, "world": 4})(), "cpu", backend="strassen")
     assert (layer2.sites["k"].bn, layer2.sites["k"].narrow) == (256, False)
+
+
+def test_native_sites_take_the_native_arm():
+    class FakeTP:
+        rank, world = 0, 2
+
+    layer = qwen3.build_layer(CFG, 0, FakeTP(), "cpu", backend="strassen", native_sites=frozenset({"v", "up"}))
+    native = qwen3.build_layer(CFG, 0, FakeTP(), "cpu", backend="native")
+    for name in ("v", "up"):
+        assert not layer.sites[name].strassen
+        assert torch.equal(layer.sites[name].weight, native.sites[name].weight), name
+    assert layer.sites["q"].strassen and layer.sites["down"].strassen
