@@ -229,6 +229,28 @@ SB_API int sb_strassen_gemm_quad(sb_stream_t stream,
                                  void* workspace, size_t workspace_bytes, int32_t raster);
 
 /*
+ * sb_strassen_gemm_planes -- C = A·B, no epilogue, as seven full-width product
+ * GEMMs: two passes form the A operand planes [7][M/2][K/2] and the B operand
+ * planes [7][K/2][N/2] (the reference's pre-adds, strassen_pallas.py:324-379,
+ * each rounded once to bf16), a persistent kernel on CTA pairs (tcgen05
+ * cta_group::2, 256 x 256 product tiles) writes the seven fp32 products, and a
+ * last pass recombines C11 = M1+M4-M5+M7, C12 = M3+M5, C21 = M2+M4,
+ * C22 = M1-M2+M3+M6 into C.  Replaces strassen_pallas.strassen_matmul(a, b,
+ * bm=, bn=, bk=, output_dtype=) without an epilogue (strassen_pallas.py:882-1221);
+ * same operand pairing, rounding and recombination order as sb_strassen_gemm.
+ * `workspace`: sb_planes_workspace_bytes(m, n, k) bytes, 16-byte aligned.
+ * Needs M % 512 == 0, N % 512 == 0 and K % 128 == 0 (SB_ERR_TILING otherwise).
+ * `raster`: product-row tiles per column sweep (0 = the kernel's default).
+ */
+SB_API size_t sb_planes_workspace_bytes(int64_t m, int64_t n, int64_t k);
+SB_API int sb_strassen_gemm_planes(sb_stream_t stream,
+                                   const void* a, const void* b, void* c,
+                                   int64_t m, int64_t n, int64_t k,
+                                   int64_t lda, int64_t ldb, int64_t ldc,
+                                   int32_t bm, int32_t bn, int32_t bk, int32_t out_dtype,
+                                   void* workspace, size_t workspace_bytes, int32_t raster);
+
+/*
  * sb_strassen_gemm_norm_residual_noalloc -- the norm_residual_add epilogue of
  * sb_strassen_gemm, with its fp32 scratch in a device array built into the
  * library instead of a caller workspace.  No counterpart in the reference.

@@ -21,6 +21,7 @@ from .strassen import (
     classical_matmul,
     native_matmul,
     pair_matmul,
+    planes_matmul,
     quad_matmul,
     rms_norm,
     StrassenBOperands,
@@ -35,7 +36,7 @@ from .torch_ops import strassen_matmul_op  # registers torch.ops.strassen_b200.s
 __all__ = [
     "TUNED_BM", "TUNED_BN", "TUNED_BK",
     "check_tiling", "classical_matmul", "native_matmul", "rms_norm", "strassen_matmul",
-    "pair_matmul", "quad_matmul", "StrassenBOperands", "strassen_b_operands", "strassen_matmul_lhs_transposed", "strassen_matmul_streamed", "tuned_matmul",
+    "pair_matmul", "planes_matmul", "quad_matmul", "StrassenBOperands", "strassen_b_operands", "strassen_matmul_lhs_transposed", "strassen_matmul_streamed", "tuned_matmul",
     "workspace_bytes", "strassen_matmul_op",
     "rope_layout_tables", "rope_layout_to_heads", "rope_scale_layout", "rope_weight_layout",
     "swiglu_weight_layout",

@@ -1051,6 +1051,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 #include "strassen_pair.cuh"
 // The four-CTA kernel on CTA pairs (sb_strassen_gemm_quad).
 #include "strassen_quad.cuh"
+// Seven full-width product GEMMs on CTA pairs (sb_strassen_gemm_planes).
+#include "strassen_planes.cuh"
 
 // Failure-detection self-test (sb_wait_selftest): warp 0 waits on a barrier
 // nobody arrives on and gives up after the bounded-wait limit, raising the abort
@@ -1821,6 +1823,139 @@ int run_quad(cudaStream_t stream, const void* a, const void* b, const void* b_pl
   return out_dtype == SB_F32 ? launch_quad<true>(stream, maps, p) : launch_quad<false>(stream, maps, p);
 }
 
+// ---------------------------------------------------------------- planes path
+// Workspace of sb_strassen_gemm_planes: A operand planes [7][M/2][K/2] bf16,
+// B operand planes [7][K/2][N/2] bf16, products [7][M/2][N/2] fp32.
+size_t planes_a_bytes(int64_t m, int64_t k) { return (size_t)7 * (size_t)(m / 2) * (size_t)(k / 2) * 2u; }
+size_t planes_prod_bytes(int64_t m, int64_t n) { return (size_t)7 * (size_t)(m / 2) * (size_t)(n / 2) * 4u; }
+
+// Tensor maps of the product GEMM:
+//   a: A operand planes as dims (kappa, t, plane), box {64, 128, 1}, 128-byte
+//      swizzle (a CTA's 128 product rows, 64 deep);
+//   b: B operand planes as dims (column in a 64-column chunk, kappa, chunk,
+//      plane), box {64, 64, 2, 1}, 128-byte swizzle (a CTA's 128 columns as two
+//      MN-major chunks, 64 deep).
+int make_planes_maps(const void* aop, const void* bop, int64_t m, int64_t n, int64_t k, CUtensorMap* ta,
+                     CUtensorMap* tb) {
+  EncodeTiledFn enc = encode_fn();
+  if (!enc) return fail(SB_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
+  const int64_t mh = m / 2, nh = n / 2, kh = k / 2;
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  {
+    cuuint64_t dims[3] = {(cuuint64_t)kh, (cuuint64_t)mh, 7};
+    cuuint64_t strides[2] = {(cuuint64_t)(kh * 2), (cuuint64_t)(mh * kh * 2)};
+    cuuint32_t box[3] = {(cuuint32_t)planes::kBK, 128, 1};
+    CUresult r = enc(ta, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(aop), dims, strides, box, estr,
+                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(SB_ERR_CUDA, "cuTensorMapEncodeTiled(A planes) failed: " + std::to_string((int)r));
+  }
+  cuuint64_t dims[4] = {64, (cuuint64_t)kh, (cuuint64_t)(nh / 64), 7};
+  cuuint64_t strides[3] = {(cuuint64_t)(nh * 2), 128, (cuuint64_t)(kh * nh * 2)};
+  cuuint32_t box[4] = {64, (cuuint32_t)planes::kBK, 2, 1};
+  CUresult r = enc(tb, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(bop), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(SB_ERR_CUDA, "cuTensorMapEncodeTiled(B planes) failed: " + std::to_string((int)r));
+  return SB_OK;
+}
+
+// Persistent launch: one cluster (CTA pair) per two SMs, each walking its tiles.
+int launch_planes_gemm(cudaStream_t stream, const CUtensorMap& ta, const CUtensorMap& tb, const PlanesParams& p) {
+  auto kernel = strassen_planes_gemm_kernel;
+  constexpr int kSmem = planes::kSmem;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64)
+    return fail(SB_ERR_DEVICE, "no usable current device");
+  static std::once_flag once[64];
+  static cudaError_t attr_err[64];
+  static int sms[64];
+  std::call_once(once[dev], [&]() {
+    attr_err[dev] = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
+    if (attr_err[dev] == cudaSuccess)
+      attr_err[dev] = cudaDeviceGetAttribute(&sms[dev], cudaDevAttrMultiProcessorCount, dev);
+  });
+  if (attr_err[dev] != cudaSuccess)
+    return fail(SB_ERR_CUDA, std::string("planes kernel setup: ") + cudaGetErrorString(attr_err[dev]));
+  const int clusters = std::max(1, std::min(sms[dev] / 2, p.num_tiles));
+  cudaLaunchConfig_t cfg;
+  std::memset(&cfg, 0, sizeof(cfg));
+  cfg.gridDim = dim3((unsigned)(2 * clusters), 1, 1);
+  cfg.blockDim = dim3(planes::kThreads, 1, 1);
+  cfg.dynamicSmemBytes = kSmem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, ta, tb, p);
+  if (e != cudaSuccess) return fail(SB_ERR_CUDA, std::string("planes kernel launch: ") + cudaGetErrorString(e));
+  return SB_OK;
+}
+
+// Operand passes, the seven product GEMMs and the recombination, in stream order.
+int run_planes(cudaStream_t stream, const void* a, const void* b, void* c, int64_t m, int64_t n, int64_t k,
+               int64_t lda, int64_t ldb, int64_t ldc, int32_t bm, int32_t bn, int32_t bk, int32_t out_dtype,
+               void* workspace, size_t workspace_bytes, int32_t raster) {
+  if (ldc < n) return fail(SB_ERR_ALIGNMENT, "ldc must be >= N");
+  if (raster < 0) return fail(SB_ERR_UNSUPPORTED, "raster must be >= 0 (0 = the kernel's default)");
+  if (m % 512 || n % 512 || k % 128)
+    return fail(SB_ERR_TILING, "the planes path needs M and N divisible by 512 and K by 128 (256 x 256 product "
+                               "tiles, 64-deep steps), got M=" + std::to_string(m) + " N=" + std::to_string(n) +
+                               " K=" + std::to_string(k));
+  const size_t a_bytes = planes_a_bytes(m, k), b_bytes = quad_planes_bytes(k, n), p_bytes = planes_prod_bytes(m, n);
+  const size_t need = a_bytes + b_bytes + p_bytes;
+  if (!workspace || workspace_bytes < need)
+    return fail(SB_ERR_WORKSPACE, "the planes path needs a workspace of " + std::to_string(need) +
+                                      " bytes (sb_planes_workspace_bytes), got " + std::to_string(workspace_bytes));
+  if (!aligned16(workspace)) return fail(SB_ERR_ALIGNMENT, "workspace must be 16-byte aligned");
+  int st = check_device();
+  if (st != SB_OK) return st;
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  __nv_bfloat16* aop = reinterpret_cast<__nv_bfloat16*>(ws);
+  void* bop = ws + a_bytes;
+  float* prod = reinterpret_cast<float*>(ws + a_bytes + b_bytes);
+  st = sb_strassen_b_operands(reinterpret_cast<sb_stream_t>(stream), b, bop, k, n, ldb, bn, bk);
+  if (st != SB_OK) return st;
+  {
+    const int64_t items = (m / 2) * (k / 2 / 8);
+    const unsigned grid = (unsigned)std::min<int64_t>((items + 255) / 256, 148 * 16);
+    a_operand_planes_kernel<<<grid, 256, 0, stream>>>(reinterpret_cast<const __nv_bfloat16*>(a), lda, (int32_t)m,
+                                                      (int32_t)k, bm, bk, aop);
+    const cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return fail(SB_ERR_CUDA, std::string("A planes launch: ") + cudaGetErrorString(e));
+  }
+  CUtensorMap ta, tb;
+  st = make_planes_maps(aop, bop, m, n, k, &ta, &tb);
+  if (st != SB_OK) return st;
+  PlanesParams p;
+  std::memset(&p, 0, sizeof(p));
+  p.mh = (int32_t)(m / 2);
+  p.nh = (int32_t)(n / 2);
+  p.kh = (int32_t)(k / 2);
+  p.tiles_m = p.mh / planes::kTileM;
+  p.tiles_n = p.nh / planes::kTileN;
+  p.num_tiles = 7 * p.tiles_m * p.tiles_n;
+  p.k_steps = p.kh / planes::kBK;
+  p.raster = raster;
+  p.prod = prod;
+  p.err = t_error_word;
+  st = launch_planes_gemm(stream, ta, tb, p);
+  if (st != SB_OK) return st;
+  const int64_t items = (m / 2) * (n / 2 / 8);
+  const unsigned grid = (unsigned)std::min<int64_t>((items + 255) / 256, 148 * 16);
+  if (out_dtype == SB_F32)
+    planes_recombine_kernel<true><<<grid, 256, 0, stream>>>(prod, p.mh, p.nh, bm, bn, c, ldc);
+  else
+    planes_recombine_kernel<false><<<grid, 256, 0, stream>>>(prod, p.mh, p.nh, bm, bn, c, ldc);
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return fail(SB_ERR_CUDA, std::string("recombination launch: ") + cudaGetErrorString(e));
+  return SB_OK;
+}
+
 void apply_options(GemmParams& p, int formula, int perm, const int32_t* schedule) {
   p.formula = formula == SB_FORMULA_DUAL ? 1 : formula == SB_FORMULA_POWERS ? 2 : 0;
   p.swap_m = perm & 1;
@@ -2206,6 +2341,20 @@ int sb_wait_selftest(sb_stream_t stream) {
 size_t sb_quad_workspace_bytes(int64_t m, int64_t n, int64_t k) {
   if (m <= 0 || n <= 0 || k <= 0) return 0;
   return quad_ops_bytes(m, k) + quad_planes_bytes(k, n);
+}
+
+size_t sb_planes_workspace_bytes(int64_t m, int64_t n, int64_t k) {
+  if (m <= 0 || n <= 0 || k <= 0) return 0;
+  return planes_a_bytes(m, k) + quad_planes_bytes(k, n) + planes_prod_bytes(m, n);
+}
+
+int sb_strassen_gemm_planes(sb_stream_t stream_, const void* a, const void* b, void* c, int64_t m, int64_t n,
+                            int64_t k, int64_t lda, int64_t ldb, int64_t ldc, int32_t bm, int32_t bn, int32_t bk,
+                            int32_t out_dtype, void* workspace, size_t workspace_bytes, int32_t raster) {
+  int st = validate_core(a, b, c, m, n, k, lda, ldb, ldc, bm, bn, bk, out_dtype);
+  if (st != SB_OK) return st;
+  return run_planes(reinterpret_cast<cudaStream_t>(stream_), a, b, c, m, n, k, lda, ldb, ldc, bm, bn, bk, out_dtype,
+                    workspace, workspace_bytes, raster);
 }
 
 int sb_strassen_gemm_quad(sb_stream_t stream_, const void* a, const void* b, void* c, int64_t m, int64_t n,

@@ -707,6 +707,57 @@ def quad_matmul(a, b, *, bm=TUNED_BM, bn=TUNED_BN, bk=TUNED_BK, output_dtype=Non
     return out
 
 
+def planes_matmul(a, b, *, bm=TUNED_BM, bn=TUNED_BN, bk=TUNED_BK, output_dtype=None, out=None, workspace=None,
+                  raster=0):
+    """``strassen_matmul(a, b, bm=, bn=, bk=, output_dtype=)`` without an epilogue,
+    as seven full-width product GEMMs (``sb_strassen_gemm_planes``): the A and
+    B operand planes of every Strassen block (the reference's pre-adds,
+    strassen_pallas.py:324-379, rounded once), the seven products on CTA pairs
+    with 256 x 256 tiles into an fp32 workspace, and the recombination into C
+    in the one-CTA kernel's fp32 order.
+
+    ``workspace``: a uint8 CUDA tensor of at least ``sb_planes_workspace_bytes``
+    of the shape (allocated here when omitted).  Needs M % 512 == 0,
+    N % 512 == 0 and K % 128 == 0.  ``raster``: product-row tiles per column
+    sweep (0 = the kernel's default); the result does not depend on it.
+    """
+    if a.ndim != 2 or b.ndim != 2:
+        raise ValueError("planes_matmul expects two rank-2 matrices")
+    m, k = a.shape
+    k2, n = b.shape
+    if k != k2:
+        raise ValueError(f"inner dimensions disagree: {k} vs {k2}")
+    if a.dtype != torch.bfloat16 or b.dtype != torch.bfloat16:
+        raise ValueError("inputs must be BF16")
+    for name, dimension, block in (("M", m, bm), ("N", n, bn), ("K", k, bk)):
+        if dimension % block:
+            raise ValueError(f"{name}={dimension} is not divisible by {block}")
+    check_tiling(bm, bn, bk)
+    if m % 512 or n % 512 or k % 128:
+        raise ValueError("the planes path needs M % 512 == 0, N % 512 == 0 and K % 128 == 0")
+    if a.device.type != "cuda" or b.device.type != "cuda":
+        raise ValueError("planes_matmul runs on a CUDA device (no CPU fallback)")
+    out_dt = _as_torch_dtype(output_dtype) or torch.bfloat16
+    device = a.device
+    a = _rowmajor(a)
+    b = _rowmajor(b)
+    if out is None:
+        out = torch.empty((m, n), dtype=out_dt, device=device)
+    lib = _native.load()
+    need = int(lib.sb_planes_workspace_bytes(m, n, k))
+    if workspace is None:
+        workspace = torch.empty(need, dtype=torch.uint8, device=device)
+    elif workspace.dtype != torch.uint8 or workspace.numel() < need or workspace.device != device:
+        raise ValueError(f"workspace must be a uint8 tensor of at least {need} bytes on {device}")
+    od = SB_F32 if out_dt == torch.float32 else SB_BF16
+    with torch.cuda.device(device):
+        status = lib.sb_strassen_gemm_planes(_stream_handle(device), a.data_ptr(), b.data_ptr(), out.data_ptr(),
+                                             m, n, k, _ld(a), _ld(b), _ld(out), bm, bn, bk, od,
+                                             workspace.data_ptr(), workspace.numel(), int(raster))
+    _native.check(status)
+    return out
+
+
 def rms_norm(x, scale, eps: float = 1e-6, out=None):
     """bf16 RMSNorm with fp32 math on the sm_100a row kernel.
 
