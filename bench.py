@@ -57,10 +57,12 @@ def parse():
     p.add_argument("--no-cpu-baseline", action="store_true",
                    help="skip the CPU oracle timing (used for ncu captures)")
     p.add_argument("--no-e2e", action="store_true", help="skip the host-buffer end-to-end loop")
-    p.add_argument("--kernel", default="single", choices=["single", "pair", "pair-planes", "quad"],
-                   help="GEMM workload: the one-CTA Strassen kernel, the two-CTA cluster kernel, the "
-                        "two-CTA kernel on B operand planes formed inside each step, or the four-CTA "
-                        "paired-tensor-core kernel (its operand passes inside each step)")
+    p.add_argument("--kernel", default="planes", choices=["planes", "single", "pair", "pair-planes", "quad"],
+                   help="GEMM workload: the seven full-width product GEMMs on CTA pairs (the default path "
+                        "of a plain strassen_matmul at this size: operand passes, GEMM, recombination, all "
+                        "timed), the one-CTA Strassen kernel, the two-CTA cluster kernel, the two-CTA kernel "
+                        "on B operand planes formed inside each step, or the four-CTA paired-tensor-core "
+                        "kernel (its operand passes inside each step)")
     p.add_argument("--quad-raster", type=int, default=0,
                    help="--kernel quad: product-row tiles per column sweep (0 = the kernel's default)")
     p.add_argument("--profile", action="store_true",
@@ -271,6 +273,9 @@ def run_ours(args):
 
     launches_per_step = 1
     tile = TILE
+    gemm_events = []  # (start, end) CUDA events around the dominant kernel, when it is one of several
+    if args.kernel == "planes" and args.epilogue != "none":
+        args.kernel = "single"  # the fused epilogues run on the one-CTA kernel
     if args.epilogue != "none" and args.kernel != "single":
         raise SystemExit("--epilogue runs on the one-CTA kernel (--kernel single)")
     if args.epilogue == "norm_residual_add":
@@ -285,6 +290,20 @@ def run_ours(args):
         def step():
             sb.strassen_matmul(a, b, bm=tile[0], bn=tile[1], bk=tile[2], epilogue="norm_residual_add",
                                residual=residual, norm_scale=norm_scale, workspace=workspace, out=c)
+    elif args.kernel == "planes":
+        ws_planes = torch.empty(sb.workspace_bytes(M, N, K), dtype=torch.uint8, device=device)
+        launches_per_step = 4  # B planes, A planes, the product GEMM, the recombination
+        kw_planes = dict(bm=TILE[0], bn=TILE[1], bk=TILE[2], out=c, workspace=ws_planes)
+
+        def step():
+            # One strassen_matmul, split at its stages so the product GEMM is timed alone.
+            sb.planes_matmul(a, b, stages=1, **kw_planes)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            sb.planes_matmul(a, b, stages=2, **kw_planes)
+            e1.record(stream)
+            gemm_events.append((e0, e1))
+            sb.planes_matmul(a, b, stages=4, **kw_planes)
     elif args.kernel == "pair-planes":
         planes = torch.empty(7, K // 2, N // 2, dtype=torch.bfloat16, device=device)
         launches_per_step = 2
@@ -300,11 +319,14 @@ def run_ours(args):
         def step():
             sb.quad_matmul(a, b, bm=TILE[0], bn=TILE[1], bk=TILE[2], out=c, workspace=workspace,
                            raster=args.quad_raster)
+    elif args.kernel == "pair":
+        def step():
+            sb.pair_matmul(a, b, bm=TILE[0], bn=TILE[1], bk=TILE[2], out=c)
     else:
-        gemm = sb.pair_matmul if args.kernel == "pair" else sb.strassen_matmul
+        one_ws = torch.empty(0, dtype=torch.uint8, device=device)  # keeps the product on the one-CTA kernel
 
         def step():
-            gemm(a, b, bm=TILE[0], bn=TILE[1], bk=TILE[2], out=c)
+            sb.strassen_matmul(a, b, bm=TILE[0], bn=TILE[1], bk=TILE[2], out=c, workspace=one_ws)
 
     def barrier():
         if world > 1:
@@ -336,6 +358,9 @@ def run_ours(args):
     with ClockSampler(device.index) as clocks:
         elapsed_ms = timed(step, args.steps, args.warmup)
     ms = elapsed_ms / args.steps
+    timed_events = gemm_events[-args.steps:]
+    kernel_ms = (max_over_ranks(sum(s.elapsed_time(e) for s, e in timed_events) / len(timed_events))
+                 if timed_events else ms)
     value = world * flops * args.steps / (elapsed_ms * 1e-3) / 1e12
     dev_err = _native.device_status(reset=True)
     if dev_err:
@@ -351,19 +376,23 @@ def run_ours(args):
     if peak is None:
         peak, peak_src = 1590.0, "fallback 1.59 PFLOP/s"
     raw_flops = flops * 7.0 / 8.0
-    achieved = raw_flops / (ms * 1e-3) / 1e12
+    achieved = raw_flops / (kernel_ms * 1e-3) / 1e12
     traffic = None
-    traffic_path = REPO / "profiles" / "strassen_gemm_8192_traffic.json"
+    traffic_path = REPO / "profiles" / ("strassen_planes_8192_traffic.json" if args.kernel == "planes"
+                                        else "strassen_gemm_8192_traffic.json")
     if traffic_path.exists() and args.epilogue == "none":
         traffic = json.loads(traffic_path.read_text()).get("dram_bytes_per_launch")
 
     # --- comparison arms on identical tensors (informational)
-    cublas_ms = control_ms = None
+    cublas_ms = control_ms = one_cta_ms = None
     if not args.profile:
         n_cmp = max(10, args.steps // 2)
         cublas_ms = timed(lambda: torch.matmul(a, b, out=c), n_cmp, 3) / n_cmp
         control_ms = timed(lambda: sb.classical_matmul(a, b, bm=TILE[0], bn=TILE[1], bk=TILE[2], out=c),
                            n_cmp, 3) / n_cmp
+        no_ws = torch.empty(0, dtype=torch.uint8, device=device)  # keeps the product on the one-CTA kernel
+        one_cta_ms = timed(lambda: sb.strassen_matmul(a, b, bm=TILE[0], bn=TILE[1], bk=TILE[2], out=c,
+                                                      workspace=no_ws), n_cmp, 3) / n_cmp
 
     # --- end to end through the reference-facing operator with host buffers:
     # every step copies A and B from pinned host memory, calls strassen_matmul
@@ -421,7 +450,9 @@ def run_ours(args):
         "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
         "config": {"workload": f"strassen_gemm_{M}x{N}x{K}_bf16", "tile": list(tile),
                    "epilogue": args.epilogue,
-                   "kernel": {"single": "one-CTA (sb_strassen_gemm)",
+                   "kernel": {"planes": "seven product GEMMs on CTA pairs (sb_strassen_gemm_planes: operand "
+                                        "passes, GEMM, recombination), all timed",
+                              "single": "one-CTA (sb_strassen_gemm)",
                               "pair": "two-CTA cluster (sb_strassen_gemm_pair)",
                               "pair-planes": "B operand planes + two-CTA cluster (sb_strassen_b_operands, "
                                              "sb_strassen_gemm_pair_planes), both timed",
@@ -433,6 +464,9 @@ def run_ours(args):
         "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": UNIT,
                      "frac": achieved / peak, "traffic": traffic,
                      "basis": "raw tensor FLOPs 7/8*2MNK per launch / CUDA-event launch time",
+                     "kernel": ("strassen_planes_gemm_kernel (the seven product GEMMs)" if gemm_events
+                                else "the step's Strassen GEMM launch"),
+                     "kernel_ms": kernel_ms,
                      "peak_source": peak_src, "effective_tflops": flops / (ms * 1e-3) / 1e12},
         "cpu_baseline": cpu,
         "e2e": e2e,
@@ -443,6 +477,7 @@ def run_ours(args):
             "cublas_tflops": flops / (cublas_ms * 1e-3) / 1e12,
             "strassen_vs_cublas": (flops / (ms * 1e-3)) / (flops / (cublas_ms * 1e-3)),
             "classical_control_tflops": flops / (control_ms * 1e-3) / 1e12,
+            "one_cta_tflops": None if one_cta_ms is None else flops / (one_cta_ms * 1e-3) / 1e12,
         },
         "decoder": decoder,
     }

@@ -241,6 +241,12 @@ SB_API int sb_strassen_gemm_quad(sb_stream_t stream,
  * `workspace`: sb_planes_workspace_bytes(m, n, k) bytes, 16-byte aligned.
  * Needs M % 512 == 0, N % 512 == 0 and K % 128 == 0 (SB_ERR_TILING otherwise).
  * `raster`: product-row tiles per column sweep (0 = the kernel's default).
+ * `stages`: which steps run (bit 0 the operand passes, bit 1 the product GEMM,
+ * bit 2 the recombination; 7 = the whole product); the workspace carries the
+ * intermediate results between calls, so a caller can time the GEMM alone.
+ * sb_strassen_gemm / sb_strassen_gemm_ex take this path for a plain product
+ * (no epilogue, no research option) when sb_workspace_bytes asks for the
+ * planes workspace and the caller passes it.
  */
 SB_API size_t sb_planes_workspace_bytes(int64_t m, int64_t n, int64_t k);
 SB_API int sb_strassen_gemm_planes(sb_stream_t stream,
@@ -248,7 +254,8 @@ SB_API int sb_strassen_gemm_planes(sb_stream_t stream,
                                    int64_t m, int64_t n, int64_t k,
                                    int64_t lda, int64_t ldb, int64_t ldc,
                                    int32_t bm, int32_t bn, int32_t bk, int32_t out_dtype,
-                                   void* workspace, size_t workspace_bytes, int32_t raster);
+                                   void* workspace, size_t workspace_bytes, int32_t raster,
+                                   int32_t stages);
 
 /*
  * sb_strassen_gemm_norm_residual_noalloc -- the norm_residual_add epilogue of

@@ -1860,6 +1860,16 @@ int make_planes_maps(const void* aop, const void* bop, int64_t m, int64_t n, int
   return SB_OK;
 }
 
+size_t planes_workspace(int64_t m, int64_t n, int64_t k) {
+  return planes_a_bytes(m, k) + quad_planes_bytes(k, n) + planes_prod_bytes(m, n);
+}
+
+// Shapes the planes path takes (256 x 256 product tiles, 64-deep steps) and that
+// give its persistent kernel at least two tiles per CTA pair of a B200.
+bool planes_preferred(int64_t m, int64_t n, int64_t k) {
+  return m % 512 == 0 && n % 512 == 0 && k % 128 == 0 && 7 * (m / 512) * (n / 512) >= 148;
+}
+
 // Persistent launch: one cluster (CTA pair) per two SMs, each walking its tiles.
 int launch_planes_gemm(cudaStream_t stream, const CUtensorMap& ta, const CUtensorMap& tb, const PlanesParams& p) {
   auto kernel = strassen_planes_gemm_kernel;
@@ -1896,18 +1906,22 @@ int launch_planes_gemm(cudaStream_t stream, const CUtensorMap& ta, const CUtenso
   return SB_OK;
 }
 
-// Operand passes, the seven product GEMMs and the recombination, in stream order.
+// Operand passes, the seven product GEMMs and the recombination, in stream
+// order.  `stages` selects them (bit 0 the operand passes, bit 1 the product
+// GEMM, bit 2 the recombination; 7 = all) so a caller can time the GEMM alone;
+// the workspace carries the intermediate results between separate calls.
 int run_planes(cudaStream_t stream, const void* a, const void* b, void* c, int64_t m, int64_t n, int64_t k,
                int64_t lda, int64_t ldb, int64_t ldc, int32_t bm, int32_t bn, int32_t bk, int32_t out_dtype,
-               void* workspace, size_t workspace_bytes, int32_t raster) {
+               void* workspace, size_t workspace_bytes, int32_t raster, int32_t stages = 7) {
   if (ldc < n) return fail(SB_ERR_ALIGNMENT, "ldc must be >= N");
   if (raster < 0) return fail(SB_ERR_UNSUPPORTED, "raster must be >= 0 (0 = the kernel's default)");
+  if (stages <= 0 || stages > 7) return fail(SB_ERR_UNSUPPORTED, "stages must be a nonzero mask of bits 0-2");
   if (m % 512 || n % 512 || k % 128)
     return fail(SB_ERR_TILING, "the planes path needs M and N divisible by 512 and K by 128 (256 x 256 product "
                                "tiles, 64-deep steps), got M=" + std::to_string(m) + " N=" + std::to_string(n) +
                                " K=" + std::to_string(k));
-  const size_t a_bytes = planes_a_bytes(m, k), b_bytes = quad_planes_bytes(k, n), p_bytes = planes_prod_bytes(m, n);
-  const size_t need = a_bytes + b_bytes + p_bytes;
+  const size_t a_bytes = planes_a_bytes(m, k), b_bytes = quad_planes_bytes(k, n);
+  const size_t need = planes_workspace(m, n, k);
   if (!workspace || workspace_bytes < need)
     return fail(SB_ERR_WORKSPACE, "the planes path needs a workspace of " + std::to_string(need) +
                                       " bytes (sb_planes_workspace_bytes), got " + std::to_string(workspace_bytes));
@@ -1918,9 +1932,9 @@ int run_planes(cudaStream_t stream, const void* a, const void* b, void* c, int64
   __nv_bfloat16* aop = reinterpret_cast<__nv_bfloat16*>(ws);
   void* bop = ws + a_bytes;
   float* prod = reinterpret_cast<float*>(ws + a_bytes + b_bytes);
-  st = sb_strassen_b_operands(reinterpret_cast<sb_stream_t>(stream), b, bop, k, n, ldb, bn, bk);
-  if (st != SB_OK) return st;
-  {
+  if (stages & 1) {
+    st = sb_strassen_b_operands(reinterpret_cast<sb_stream_t>(stream), b, bop, k, n, ldb, bn, bk);
+    if (st != SB_OK) return st;
     const int64_t items = (m / 2) * (k / 2 / 8);
     const unsigned grid = (unsigned)std::min<int64_t>((items + 255) / 256, 148 * 16);
     a_operand_planes_kernel<<<grid, 256, 0, stream>>>(reinterpret_cast<const __nv_bfloat16*>(a), lda, (int32_t)m,
@@ -1928,31 +1942,36 @@ int run_planes(cudaStream_t stream, const void* a, const void* b, void* c, int64
     const cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return fail(SB_ERR_CUDA, std::string("A planes launch: ") + cudaGetErrorString(e));
   }
-  CUtensorMap ta, tb;
-  st = make_planes_maps(aop, bop, m, n, k, &ta, &tb);
-  if (st != SB_OK) return st;
-  PlanesParams p;
-  std::memset(&p, 0, sizeof(p));
-  p.mh = (int32_t)(m / 2);
-  p.nh = (int32_t)(n / 2);
-  p.kh = (int32_t)(k / 2);
-  p.tiles_m = p.mh / planes::kTileM;
-  p.tiles_n = p.nh / planes::kTileN;
-  p.num_tiles = 7 * p.tiles_m * p.tiles_n;
-  p.k_steps = p.kh / planes::kBK;
-  p.raster = raster;
-  p.prod = prod;
-  p.err = t_error_word;
-  st = launch_planes_gemm(stream, ta, tb, p);
-  if (st != SB_OK) return st;
-  const int64_t items = (m / 2) * (n / 2 / 8);
-  const unsigned grid = (unsigned)std::min<int64_t>((items + 255) / 256, 148 * 16);
-  if (out_dtype == SB_F32)
-    planes_recombine_kernel<true><<<grid, 256, 0, stream>>>(prod, p.mh, p.nh, bm, bn, c, ldc);
-  else
-    planes_recombine_kernel<false><<<grid, 256, 0, stream>>>(prod, p.mh, p.nh, bm, bn, c, ldc);
-  const cudaError_t e = cudaGetLastError();
-  if (e != cudaSuccess) return fail(SB_ERR_CUDA, std::string("recombination launch: ") + cudaGetErrorString(e));
+  const int32_t mh = (int32_t)(m / 2), nh = (int32_t)(n / 2);
+  if (stages & 2) {
+    CUtensorMap ta, tb;
+    st = make_planes_maps(aop, bop, m, n, k, &ta, &tb);
+    if (st != SB_OK) return st;
+    PlanesParams p;
+    std::memset(&p, 0, sizeof(p));
+    p.mh = mh;
+    p.nh = nh;
+    p.kh = (int32_t)(k / 2);
+    p.tiles_m = p.mh / planes::kTileM;
+    p.tiles_n = p.nh / planes::kTileN;
+    p.num_tiles = 7 * p.tiles_m * p.tiles_n;
+    p.k_steps = p.kh / planes::kBK;
+    p.raster = raster;
+    p.prod = prod;
+    p.err = t_error_word;
+    st = launch_planes_gemm(stream, ta, tb, p);
+    if (st != SB_OK) return st;
+  }
+  if (stages & 4) {
+    const int64_t items = (int64_t)mh * (nh / 8);
+    const unsigned grid = (unsigned)std::min<int64_t>((items + 255) / 256, 148 * 16);
+    if (out_dtype == SB_F32)
+      planes_recombine_kernel<true><<<grid, 256, 0, stream>>>(prod, mh, nh, bm, bn, c, ldc);
+    else
+      planes_recombine_kernel<false><<<grid, 256, 0, stream>>>(prod, mh, nh, bm, bn, c, ldc);
+    const cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return fail(SB_ERR_CUDA, std::string("recombination launch: ") + cudaGetErrorString(e));
+  }
   return SB_OK;
 }
 
@@ -1973,8 +1992,9 @@ using namespace sb;
 extern "C" {
 
 size_t sb_workspace_bytes(int64_t m, int64_t n, int64_t k, int32_t epilogue_kind) {
-  (void)k;
   if (epilogue_kind == SB_EPI_NORM_RESIDUAL_ADD && m > 0 && n > 0) return (size_t)m * (size_t)n * 4u;
+  if (epilogue_kind == SB_EPI_NONE && m > 0 && n > 0 && k > 0 && planes_preferred(m, n, k))
+    return planes_workspace(m, n, k);
   return 0;
 }
 
@@ -2046,6 +2066,13 @@ int sb_strassen_gemm_ex(sb_stream_t stream_, const void* a, const void* b, void*
   } else if (ldc < n) {
     return fail(SB_ERR_ALIGNMENT, "ldc must be >= N");
   }
+  // A plain product with room for the planes workspace runs as seven
+  // full-width product GEMMs (same products, rounding and recombination order).
+  if (epi == SB_EPI_NONE && formula == SB_FORMULA_CLASSICAL && perm == 0 && !schedule && !narrow &&
+      planes_preferred(m, n, k) && workspace && aligned16(workspace) &&
+      workspace_bytes >= planes_workspace(m, n, k))
+    return run_planes(stream, a, b, c, m, n, k, lda, ldb, ldc, bm, bn, bk, out_dtype, workspace, workspace_bytes,
+                      0);
   st = check_device();
   if (st != SB_OK) return st;
 
@@ -2345,16 +2372,17 @@ size_t sb_quad_workspace_bytes(int64_t m, int64_t n, int64_t k) {
 
 size_t sb_planes_workspace_bytes(int64_t m, int64_t n, int64_t k) {
   if (m <= 0 || n <= 0 || k <= 0) return 0;
-  return planes_a_bytes(m, k) + quad_planes_bytes(k, n) + planes_prod_bytes(m, n);
+  return planes_workspace(m, n, k);
 }
 
 int sb_strassen_gemm_planes(sb_stream_t stream_, const void* a, const void* b, void* c, int64_t m, int64_t n,
                             int64_t k, int64_t lda, int64_t ldb, int64_t ldc, int32_t bm, int32_t bn, int32_t bk,
-                            int32_t out_dtype, void* workspace, size_t workspace_bytes, int32_t raster) {
+                            int32_t out_dtype, void* workspace, size_t workspace_bytes, int32_t raster,
+                            int32_t stages) {
   int st = validate_core(a, b, c, m, n, k, lda, ldb, ldc, bm, bn, bk, out_dtype);
   if (st != SB_OK) return st;
   return run_planes(reinterpret_cast<cudaStream_t>(stream_), a, b, c, m, n, k, lda, ldb, ldc, bm, bn, bk, out_dtype,
-                    workspace, workspace_bytes, raster);
+                    workspace, workspace_bytes, raster, stages);
 }
 
 int sb_strassen_gemm_quad(sb_stream_t stream_, const void* a, const void* b, void* c, int64_t m, int64_t n,

@@ -118,7 +118,9 @@ def strassen_matmul(
     Extra keyword arguments: ``out`` (a preallocated output tensor),
     ``workspace`` (a caller-owned uint8 CUDA buffer of at least
     :func:`workspace_bytes` bytes; allocated from torch's caching allocator
-    when omitted) and ``narrow_bn`` (B200 extension, no reference counterpart:
+    when omitted -- for a plain product on a large shape that is the planes
+    path's workspace, and a smaller buffer keeps the product on the one-CTA
+    kernel, see :func:`planes_matmul`) and ``narrow_bn`` (B200 extension, no reference counterpart:
     bn may be any multiple of 128 instead of the reference's TPU lane rule of
     256, and qk_norm_rope then needs bn % rope_head_dim == 0 -- each half block
     holds whole half-heads; the tensor-parallel decoder uses it for one-head k/v
@@ -338,8 +340,13 @@ def strassen_matmul(
         if workspace is None:
             workspace = torch.empty(ws_bytes, dtype=torch.uint8, device=device)
         if workspace.numel() * workspace.element_size() < ws_bytes:
-            raise ValueError(f"workspace must hold {ws_bytes} bytes")
-        ws_ptr = workspace.data_ptr()
+            if ep.kind != EPILOGUE_KINDS[None]:
+                raise ValueError(f"workspace must hold {ws_bytes} bytes")
+            # A plain product without room for the planes path runs on the
+            # one-CTA kernel, which needs no workspace.
+            ws_bytes = 0
+        else:
+            ws_ptr = workspace.data_ptr()
     with torch.cuda.device(device):
         status = lib.sb_strassen_gemm_ex(
             _stream_handle(device), a.data_ptr(), b.data_ptr(), out.data_ptr(),
@@ -708,7 +715,7 @@ def quad_matmul(a, b, *, bm=TUNED_BM, bn=TUNED_BN, bk=TUNED_BK, output_dtype=Non
 
 
 def planes_matmul(a, b, *, bm=TUNED_BM, bn=TUNED_BN, bk=TUNED_BK, output_dtype=None, out=None, workspace=None,
-                  raster=0):
+                  raster=0, stages=7):
     """``strassen_matmul(a, b, bm=, bn=, bk=, output_dtype=)`` without an epilogue,
     as seven full-width product GEMMs (``sb_strassen_gemm_planes``): the A and
     B operand planes of every Strassen block (the reference's pre-adds,
@@ -720,6 +727,9 @@ def planes_matmul(a, b, *, bm=TUNED_BM, bn=TUNED_BN, bk=TUNED_BK, output_dtype=N
     of the shape (allocated here when omitted).  Needs M % 512 == 0,
     N % 512 == 0 and K % 128 == 0.  ``raster``: product-row tiles per column
     sweep (0 = the kernel's default); the result does not depend on it.
+    ``stages``: bit 0 the operand passes, bit 1 the product GEMM, bit 2 the
+    recombination (7 = all); separate calls with the same ``workspace`` and
+    operands give the same result as one call (used to time the GEMM alone).
     """
     if a.ndim != 2 or b.ndim != 2:
         raise ValueError("planes_matmul expects two rank-2 matrices")
@@ -753,7 +763,7 @@ def planes_matmul(a, b, *, bm=TUNED_BM, bn=TUNED_BN, bk=TUNED_BK, output_dtype=N
     with torch.cuda.device(device):
         status = lib.sb_strassen_gemm_planes(_stream_handle(device), a.data_ptr(), b.data_ptr(), out.data_ptr(),
                                              m, n, k, _ld(a), _ld(b), _ld(out), bm, bn, bk, od,
-                                             workspace.data_ptr(), workspace.numel(), int(raster))
+                                             workspace.data_ptr(), workspace.numel(), int(raster), int(stages))
     _native.check(status)
     return out
 

@@ -211,18 +211,22 @@ def test_qwen3_06b_mlp_config2():
 
 
 @pytest.mark.slow
-def test_full_size_8192_block_row_and_global_error():
+@pytest.mark.parametrize("path", ["default", "one_cta"])
+def test_full_size_8192_block_row_and_global_error(path):
     """8192^3 at the reference tile (1024, 1024, 512): block-row 0 against the
     oracle (tile-local Strassen makes a block row depend only on its A rows),
     and the whole output against cuBLAS-fp32 through size-independent error
-    bounds (the reference's gate: rmse <= 4x native, maxnorm-relative <= 0.01)."""
+    bounds (the reference's gate: rmse <= 4x native, maxnorm-relative <= 0.01).
+    "default" is the plain product's default path (the seven product GEMMs),
+    "one_cta" the one-CTA kernel (an empty workspace selects it)."""
     import strassen_tpu_b200 as sb
     n, bm = 8192, 1024
     a = ref.normal_bf16((n, n), 20260902)
     b = ref.normal_bf16((n, n), 20260903)
     ad, bd = dev_bf16(a), dev_bf16(b)
-    got = sb.strassen_matmul(ad, bd, bm=bm, bn=1024, bk=512)
-    got32 = sb.strassen_matmul(ad[:bm], bd, bm=bm, bn=1024, bk=512, output_dtype=torch.float32)
+    kw = {} if path == "default" else dict(workspace=torch.empty(0, dtype=torch.uint8, device="cuda"))
+    got = sb.strassen_matmul(ad, bd, bm=bm, bn=1024, bk=512, **kw)
+    got32 = sb.strassen_matmul(ad[:bm], bd, bm=bm, bn=1024, bk=512, output_dtype=torch.float32, **kw)
     torch.cuda.synchronize()
     rows = slice(0, bm)
     exact_rows = ref.classical_f64(a[rows], b)
