@@ -1870,6 +1870,31 @@ bool planes_preferred(int64_t m, int64_t n, int64_t k) {
   return m % 512 == 0 && n % 512 == 0 && k % 128 == 0 && 7 * (m / 512) * (n / 512) >= 148;
 }
 
+// The fused epilogue's operands, as both GEMM layouts read them.
+void fill_epilogue(GemmParams& p, const sb_epilogue* ep, int epi) {
+  if (!ep) return;
+  p.residual = ep->residual;
+  p.ldr = ep->ld_residual;
+  p.residual_f32 = ep->residual_dtype == SB_F32;
+  p.aux_f32 = ep->aux_dtype == SB_F32;
+  p.bias = ep->bias;
+  p.rope_cos = ep->rope_cos;
+  p.rope_sin = ep->rope_sin;
+  p.ld_rope = ep->ld_rope;
+  p.rope_scale = ep->rope_scale;
+  if (epi == SB_EPI_QK_NORM_ROPE) {
+    p.half_head = ep->rope_head_dim / 2;
+    p.inv_head_dim = 1.0f / (float)ep->rope_head_dim;
+    p.eps = ep->rope_eps;
+  }
+}
+
+// Epilogues the planes path applies in its recombination pass.
+bool planes_epilogue(int epi) {
+  return epi == SB_EPI_NONE || epi == SB_EPI_RESIDUAL_ADD || epi == SB_EPI_BIAS_ADD || epi == SB_EPI_SWIGLU ||
+         epi == SB_EPI_GEGLU || epi == SB_EPI_QK_NORM_ROPE;
+}
+
 // Persistent launch: one cluster (CTA pair) per two SMs, each walking its tiles.
 int launch_planes_gemm(cudaStream_t stream, const CUtensorMap& ta, const CUtensorMap& tb, const PlanesParams& p) {
   auto kernel = strassen_planes_gemm_kernel;
@@ -1912,8 +1937,10 @@ int launch_planes_gemm(cudaStream_t stream, const CUtensorMap& ta, const CUtenso
 // the workspace carries the intermediate results between separate calls.
 int run_planes(cudaStream_t stream, const void* a, const void* b, void* c, int64_t m, int64_t n, int64_t k,
                int64_t lda, int64_t ldb, int64_t ldc, int32_t bm, int32_t bn, int32_t bk, int32_t out_dtype,
-               void* workspace, size_t workspace_bytes, int32_t raster, int32_t stages = 7) {
-  if (ldc < n) return fail(SB_ERR_ALIGNMENT, "ldc must be >= N");
+               void* workspace, size_t workspace_bytes, int32_t raster, int32_t stages = 7,
+               int epi = SB_EPI_NONE, const sb_epilogue* ep = nullptr) {
+  const bool gated = epi == SB_EPI_SWIGLU || epi == SB_EPI_GEGLU;  // output [M, N/2]
+  if (ldc < (gated ? n / 2 : n)) return fail(SB_ERR_ALIGNMENT, gated ? "ldc must be >= N/2" : "ldc must be >= N");
   if (raster < 0) return fail(SB_ERR_UNSUPPORTED, "raster must be >= 0 (0 = the kernel's default)");
   if (stages <= 0 || stages > 7) return fail(SB_ERR_UNSUPPORTED, "stages must be a nonzero mask of bits 0-2");
   if (m % 512 || n % 512 || k % 128)
@@ -1965,10 +1992,30 @@ int run_planes(cudaStream_t stream, const void* a, const void* b, void* c, int64
   if (stages & 4) {
     const int64_t items = (int64_t)mh * (nh / 8);
     const unsigned grid = (unsigned)std::min<int64_t>((items + 255) / 256, 148 * 16);
-    if (out_dtype == SB_F32)
-      planes_recombine_kernel<true><<<grid, 256, 0, stream>>>(prod, mh, nh, bm, bn, c, ldc);
-    else
-      planes_recombine_kernel<false><<<grid, 256, 0, stream>>>(prod, mh, nh, bm, bn, c, ldc);
+    GemmParams ep_p = base_params(m, n, k, bm, bn, bk, c, ldc, 16);
+    fill_epilogue(ep_p, ep, epi);
+    switch (epi) {
+      case SB_EPI_RESIDUAL_ADD:
+        planes_recombine_kernel<SB_EPI_RESIDUAL_ADD, false><<<grid, 256, 0, stream>>>(prod, mh, nh, ep_p);
+        break;
+      case SB_EPI_BIAS_ADD:
+        planes_recombine_kernel<SB_EPI_BIAS_ADD, false><<<grid, 256, 0, stream>>>(prod, mh, nh, ep_p);
+        break;
+      case SB_EPI_SWIGLU:
+        planes_recombine_kernel<SB_EPI_SWIGLU, false><<<grid, 256, 0, stream>>>(prod, mh, nh, ep_p);
+        break;
+      case SB_EPI_GEGLU:
+        planes_recombine_kernel<SB_EPI_GEGLU, false><<<grid, 256, 0, stream>>>(prod, mh, nh, ep_p);
+        break;
+      case SB_EPI_QK_NORM_ROPE:
+        planes_recombine_kernel<SB_EPI_QK_NORM_ROPE, false><<<grid, 256, 0, stream>>>(prod, mh, nh, ep_p);
+        break;
+      default:
+        if (out_dtype == SB_F32)
+          planes_recombine_kernel<SB_EPI_NONE, true><<<grid, 256, 0, stream>>>(prod, mh, nh, ep_p);
+        else
+          planes_recombine_kernel<SB_EPI_NONE, false><<<grid, 256, 0, stream>>>(prod, mh, nh, ep_p);
+    }
     const cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return fail(SB_ERR_CUDA, std::string("recombination launch: ") + cudaGetErrorString(e));
   }
@@ -1993,7 +2040,7 @@ extern "C" {
 
 size_t sb_workspace_bytes(int64_t m, int64_t n, int64_t k, int32_t epilogue_kind) {
   if (epilogue_kind == SB_EPI_NORM_RESIDUAL_ADD && m > 0 && n > 0) return (size_t)m * (size_t)n * 4u;
-  if (epilogue_kind == SB_EPI_NONE && m > 0 && n > 0 && k > 0 && planes_preferred(m, n, k))
+  if (planes_epilogue(epilogue_kind) && m > 0 && n > 0 && k > 0 && planes_preferred(m, n, k))
     return planes_workspace(m, n, k);
   return 0;
 }
@@ -2066,13 +2113,14 @@ int sb_strassen_gemm_ex(sb_stream_t stream_, const void* a, const void* b, void*
   } else if (ldc < n) {
     return fail(SB_ERR_ALIGNMENT, "ldc must be >= N");
   }
-  // A plain product with room for the planes workspace runs as seven
-  // full-width product GEMMs (same products, rounding and recombination order).
-  if (epi == SB_EPI_NONE && formula == SB_FORMULA_CLASSICAL && perm == 0 && !schedule && !narrow &&
+  // A product with room for the planes workspace runs as seven full-width
+  // product GEMMs (same products, rounding and recombination order; the fused
+  // epilogue applied to the recombined fp32 values as the one-CTA kernel does).
+  if (planes_epilogue(epi) && formula == SB_FORMULA_CLASSICAL && perm == 0 && !schedule && !narrow &&
       planes_preferred(m, n, k) && workspace && aligned16(workspace) &&
       workspace_bytes >= planes_workspace(m, n, k))
     return run_planes(stream, a, b, c, m, n, k, lda, ldb, ldc, bm, bn, bk, out_dtype, workspace, workspace_bytes,
-                      0);
+                      0, 7, epi, ep);
   st = check_device();
   if (st != SB_OK) return st;
 
@@ -2093,22 +2141,7 @@ int sb_strassen_gemm_ex(sb_stream_t stream_, const void* a, const void* b, void*
 
   GemmParams p = base_params(m, n, k, bm, bn, bk, c, ldc, StrassenPipe::BK);
   apply_options(p, formula, perm, schedule);
-  if (ep) {
-    p.residual = ep->residual;
-    p.ldr = ep->ld_residual;
-    p.residual_f32 = ep->residual_dtype == SB_F32;
-    p.aux_f32 = ep->aux_dtype == SB_F32;
-    p.bias = ep->bias;
-    p.rope_cos = ep->rope_cos;
-    p.rope_sin = ep->rope_sin;
-    p.ld_rope = ep->ld_rope;
-    p.rope_scale = ep->rope_scale;
-    if (epi == SB_EPI_QK_NORM_ROPE) {
-      p.half_head = ep->rope_head_dim / 2;
-      p.inv_head_dim = 1.0f / (float)ep->rope_head_dim;
-      p.eps = ep->rope_eps;
-    }
-  }
+  fill_epilogue(p, ep, epi);
   return dispatch(true, epi, out_dtype == SB_F32, stream, ta, tb, p);
 }
 

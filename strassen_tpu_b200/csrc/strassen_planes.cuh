@@ -117,43 +117,126 @@ __global__ void __launch_bounds__(256) a_operand_planes_kernel(const __nv_bfloat
 
 // C from the seven fp32 products (product coordinates -> matrix quadrants):
 // C11 = M1 + M4 - M5 + M7, C12 = M3 + M5, C21 = M2 + M4, C22 = M1 - M2 + M3 + M6,
-// summed left to right in fp32 (the one-CTA kernel's order), then stored as
-// bf16 (round to nearest even) or fp32.  One thread per 8 product columns.
-template <bool kOutF32>
+// summed left to right in fp32 (the one-CTA kernel's order), then the fused
+// epilogue on the fp32 quadrant values exactly as the one-CTA kernel applies
+// it (strassen_pallas.py:739-879): residual_add, bias_add, swiglu / geglu
+// (quadrants 0/2 gate, 1/3 up; output [M, N/2]) or qk_norm_rope (a head's
+// a-half in quadrant 0/2, its b-half at the same offset in 1/3), stored as bf16
+// (round to nearest even) or, without an epilogue, fp32.  One thread per 8
+// product columns of one product row; a warp covers 256 consecutive columns
+// of one row (nh % 256 == 0), so a head slot's sum of squares is a shuffle
+// reduction over half_head / 8 neighbouring lanes.  p: C, ldc, bm, bn,
+// half_bm, half_bn and the epilogue operands as the one-CTA kernel takes them.
+template <int kEpi, bool kOutF32>
 __global__ void __launch_bounds__(256) planes_recombine_kernel(const float* __restrict__ prod, int32_t mh, int32_t nh,
-                                                               int32_t bm, int32_t bn, void* __restrict__ c,
-                                                               int64_t ldc) {
+                                                               const GemmParams p) {
   const int64_t plane = (int64_t)mh * nh;
   const int64_t per_row = nh / 8;
   const int64_t items = (int64_t)mh * per_row;
-  const int64_t hbm = bm / 2, hbn = bn / 2;
+  const int64_t hbm = p.half_bm, hbn = p.half_bn;
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < items; i += (int64_t)gridDim.x * blockDim.x) {
     const int64_t t = i / per_row;
     const int64_t u = (i - t * per_row) * 8;
     const int64_t off = t * nh + u;
     float mv[7][8];
 #pragma unroll
-    for (int p = 0; p < 7; ++p) {
-      const float4 x = *reinterpret_cast<const float4*>(prod + p * plane + off);
-      const float4 y = *reinterpret_cast<const float4*>(prod + p * plane + off + 4);
-      mv[p][0] = x.x; mv[p][1] = x.y; mv[p][2] = x.z; mv[p][3] = x.w;
-      mv[p][4] = y.x; mv[p][5] = y.y; mv[p][6] = y.z; mv[p][7] = y.w;
+    for (int q = 0; q < 7; ++q) {
+      const float4 x = *reinterpret_cast<const float4*>(prod + q * plane + off);
+      const float4 y = *reinterpret_cast<const float4*>(prod + q * plane + off + 4);
+      mv[q][0] = x.x; mv[q][1] = x.y; mv[q][2] = x.z; mv[q][3] = x.w;
+      mv[q][4] = y.x; mv[q][5] = y.y; mv[q][6] = y.z; mv[q][7] = y.w;
     }
-    float q11[8], q12[8], q21[8], q22[8];
+    Quad8 v;
 #pragma unroll
     for (int e = 0; e < 8; ++e) {
-      q11[e] = ((mv[0][e] + mv[3][e]) - mv[4][e]) + mv[6][e];
-      q12[e] = mv[2][e] + mv[4][e];
-      q21[e] = mv[1][e] + mv[3][e];
-      q22[e] = ((mv[0][e] - mv[1][e]) + mv[2][e]) + mv[5][e];
+      v.c[0][e] = ((mv[0][e] + mv[3][e]) - mv[4][e]) + mv[6][e];  // C11
+      v.c[1][e] = mv[2][e] + mv[4][e];                            // C12
+      v.c[2][e] = mv[1][e] + mv[3][e];                            // C21
+      v.c[3][e] = ((mv[0][e] - mv[1][e]) + mv[2][e]) + mv[5][e];  // C22
     }
     const int64_t blk_i = t / hbm, blk_j = u / hbn;
-    const int64_t row = blk_i * bm + (t - blk_i * hbm);
-    const int64_t col = blk_j * bn + (u - blk_j * hbn);
-    store8<kOutF32>(c, row * ldc + col, q11);
-    store8<kOutF32>(c, row * ldc + col + hbn, q12);
-    store8<kOutF32>(c, (row + hbm) * ldc + col, q21);
-    store8<kOutF32>(c, (row + hbm) * ldc + col + hbn, q22);
+    const int64_t cp = u - blk_j * hbn;  // column inside the half block
+    const int64_t row_top = blk_i * p.bm + (t - blk_i * hbm), row_bot = row_top + hbm;
+    const int64_t cl = blk_j * p.bn + cp, cr = cl + hbn;
+    if constexpr (kEpi == SB_EPI_SWIGLU || kEpi == SB_EPI_GEGLU) {
+      float top[8], bot[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        if constexpr (kEpi == SB_EPI_SWIGLU) {
+          top[e] = silu_f32(v.c[0][e]) * v.c[1][e];
+          bot[e] = silu_f32(v.c[2][e]) * v.c[3][e];
+        } else {
+          top[e] = gelu_tanh_f32(v.c[0][e]) * v.c[1][e];
+          bot[e] = gelu_tanh_f32(v.c[2][e]) * v.c[3][e];
+        }
+      }
+      const int64_t oc = blk_j * hbn + cp;
+      store8<kOutF32>(p.C, row_top * p.ldc + oc, top);
+      store8<kOutF32>(p.C, row_bot * p.ldc + oc, bot);
+    } else if constexpr (kEpi == SB_EPI_QK_NORM_ROPE) {
+      // Per-head sums of squares over both halves (strassen_pallas.py:793-835):
+      // this thread's 8 columns, then the lanes of the same head slot.
+      float st = 0.f, sb2 = 0.f;
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        st += v.c[0][e] * v.c[0][e] + v.c[1][e] * v.c[1][e];
+        sb2 += v.c[2][e] * v.c[2][e] + v.c[3][e] * v.c[3][e];
+      }
+      for (int w = 1; w < p.half_head / 8; w <<= 1) {
+        st += __shfl_xor_sync(0xffffffffu, st, w);
+        sb2 += __shfl_xor_sync(0xffffffffu, sb2, w);
+      }
+#pragma unroll
+      for (int tb = 0; tb < 2; ++tb) {
+        const float sums = tb ? sb2 : st;
+        const float recip = 1.0f / sqrtf(sums * p.inv_head_dim + p.eps);
+        const int64_t row = tb ? row_bot : row_top;
+        float outa[8], outb[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          const float sa = load_aux(p.rope_scale, cp + e, p.aux_f32);
+          const float sbv = load_aux(p.rope_scale, hbn + cp + e, p.aux_f32);
+          const float cs = load_aux(p.rope_cos, row * p.ld_rope + cp + e, p.aux_f32);
+          const float sn = load_aux(p.rope_sin, row * p.ld_rope + cp + e, p.aux_f32);
+          const float na = v.c[2 * tb][e] * recip * sa;
+          const float nb = v.c[2 * tb + 1][e] * recip * sbv;
+          outa[e] = na * cs - nb * sn;
+          outb[e] = nb * cs + na * sn;
+        }
+        store8<kOutF32>(p.C, row * p.ldc + cl, outa);
+        store8<kOutF32>(p.C, row * p.ldc + cr, outb);
+      }
+    } else {
+      if constexpr (kEpi == SB_EPI_RESIDUAL_ADD) {
+        float r[8];
+        load8(p.residual, row_top * p.ldr + cl, p.residual_f32, r);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) v.c[0][e] += r[e];
+        load8(p.residual, row_top * p.ldr + cr, p.residual_f32, r);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) v.c[1][e] += r[e];
+        load8(p.residual, row_bot * p.ldr + cl, p.residual_f32, r);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) v.c[2][e] += r[e];
+        load8(p.residual, row_bot * p.ldr + cr, p.residual_f32, r);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) v.c[3][e] += r[e];
+      } else if constexpr (kEpi == SB_EPI_BIAS_ADD) {
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          const float bl = load_aux(p.bias, cl + e, p.aux_f32);
+          const float br = load_aux(p.bias, cr + e, p.aux_f32);
+          v.c[0][e] += bl;
+          v.c[2][e] += bl;
+          v.c[1][e] += br;
+          v.c[3][e] += br;
+        }
+      }
+      store8<kOutF32>(p.C, row_top * p.ldc + cl, v.c[0]);
+      store8<kOutF32>(p.C, row_top * p.ldc + cr, v.c[1]);
+      store8<kOutF32>(p.C, row_bot * p.ldc + cl, v.c[2]);
+      store8<kOutF32>(p.C, row_bot * p.ldc + cr, v.c[3]);
+    }
   }
 }
 

@@ -118,9 +118,11 @@ def strassen_matmul(
     Extra keyword arguments: ``out`` (a preallocated output tensor),
     ``workspace`` (a caller-owned uint8 CUDA buffer of at least
     :func:`workspace_bytes` bytes; allocated from torch's caching allocator
-    when omitted -- for a plain product on a large shape that is the planes
-    path's workspace, and a smaller buffer keeps the product on the one-CTA
-    kernel, see :func:`planes_matmul`) and ``narrow_bn`` (B200 extension, no reference counterpart:
+    when omitted -- for a large product without research options and with no
+    epilogue or a residual_add / bias_add / swiglu / geglu / qk_norm_rope
+    epilogue that is the planes path's workspace, and a smaller buffer keeps
+    the product on the one-CTA kernel, see :func:`planes_matmul`) and
+    ``narrow_bn`` (B200 extension, no reference counterpart:
     bn may be any multiple of 128 instead of the reference's TPU lane rule of
     256, and qk_norm_rope then needs bn % rope_head_dim == 0 -- each half block
     holds whole half-heads; the tensor-parallel decoder uses it for one-head k/v
@@ -340,10 +342,10 @@ def strassen_matmul(
         if workspace is None:
             workspace = torch.empty(ws_bytes, dtype=torch.uint8, device=device)
         if workspace.numel() * workspace.element_size() < ws_bytes:
-            if ep.kind != EPILOGUE_KINDS[None]:
+            if ep.kind == EPILOGUE_KINDS["norm_residual_add"]:
                 raise ValueError(f"workspace must hold {ws_bytes} bytes")
-            # A plain product without room for the planes path runs on the
-            # one-CTA kernel, which needs no workspace.
+            # Without room for the planes path the product runs on the one-CTA
+            # kernel, which needs no workspace.
             ws_bytes = 0
         else:
             ws_ptr = workspace.data_ptr()

@@ -117,3 +117,30 @@ def test_planes_validation():
     with pytest.raises(ValueError, match="workspace"):
         sb.planes_matmul(a, b, bm=256, bn=256, bk=256, workspace=torch.empty(16, dtype=torch.uint8, device="cuda"))
     assert _native.device_status() == 0
+
+
+@pytest.mark.parametrize("epilogue", ["residual_add", "bias_add", "swiglu", "geglu", "qk_norm_rope"])
+def test_planes_epilogues_match_one_cta_kernel(epilogue):
+    """A product on the planes path (large enough, workspace given) applies the
+    fused epilogue to the same recombined fp32 values as the one-CTA kernel."""
+    import strassen_tpu_b200 as sb
+    m, k, n = 4096, 1024, 4096
+    g = torch.Generator(device="cuda").manual_seed(11)
+    a = torch.randn(m, k, device="cuda", generator=g).to(torch.bfloat16)
+    b = (torch.randn(k, n, device="cuda", generator=g) * 0.05).to(torch.bfloat16)
+    kw = dict(bm=1024, bn=1024, bk=512, epilogue=epilogue)
+    if epilogue == "residual_add":
+        kw["residual"] = torch.randn(m, n, device="cuda", generator=g).to(torch.bfloat16)
+    elif epilogue == "bias_add":
+        kw["bias"] = torch.randn(n, device="cuda", generator=g).to(torch.bfloat16)
+    elif epilogue == "qk_norm_rope":
+        cos = torch.rand(m, 512, device="cuda", generator=g).to(torch.bfloat16)
+        sin = torch.rand(m, 512, device="cuda", generator=g).to(torch.bfloat16)
+        scale = (1 + 0.1 * torch.randn(1024, device="cuda", generator=g)).to(torch.bfloat16)
+        kw.update(rope_cos=cos, rope_sin=sin, rope_scale=scale, rope_head_dim=128)
+    assert sb.workspace_bytes(m, n, k, epilogue) > 0  # the planes path is the default here
+    seven = sb.strassen_matmul(a, b, **kw)
+    one = sb.strassen_matmul(a, b, **kw, workspace=torch.empty(0, dtype=torch.uint8, device="cuda"))
+    torch.cuda.synchronize()
+    assert seven.shape == one.shape
+    assert_parity(host(seven), host(one), rounding_step=True)
