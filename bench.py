@@ -87,10 +87,13 @@ def parse():
     p.add_argument("--site-times", type=int, default=0, metavar="TP",
                    help="decoder: time every op of one layer of rank 0's shard at tensor-parallel size TP "
                         "for both backends on one GPU (per-rank shapes of a TP run, no collectives)")
-    p.add_argument("--site-policy", default="measured", choices=["measured", "all"],
+    p.add_argument("--site-policy", default="measured", choices=["measured", "all", "fixed"],
                    help="decoder, strassen backend: each GEMM site on the faster of its Strassen and "
-                        "native arms at the shard's shapes (measured before the timed region), or every "
-                        "site a Strassen tile fits on Strassen")
+                        "native arms at the shard's shapes (measured before the timed region), every "
+                        "site a Strassen tile fits on Strassen, or the sites --native-sites names on the "
+                        "native arm (no timing run; used by the committed launch-list capture)")
+    p.add_argument("--native-sites", default="",
+                   help="with --site-policy fixed: comma-separated GEMM sites (q,k,v,o,up,down) on the native arm")
     p.add_argument("--collective", default="nccl", choices=["nccl", "p2p"],
                    help="decoder: row-parallel sums by NCCL all-reduce (residual fused on rank 0) "
                         "or by sb_p2p_reduce over NVLink peer memory")
@@ -498,7 +501,7 @@ def nccl_init_log(rank: int, world: int, device) -> None:
 
 
 def measure_prefill(workload, tp, device, steps, warmup, chunks, backend="strassen", eager=False, layers=None,
-                    group=None, site_policy="measured"):
+                    group=None, site_policy="measured", fixed_native=frozenset()):
     """Qwen3 prefill on `tp`'s ranks: ms per forward (CUDA events, max over the
     group's ranks), tokens/s, FLOP rate, an end-to-end figure with the token
     ids copied in and the logits copied out, and the launch count per step.
@@ -517,6 +520,11 @@ def measure_prefill(workload, tp, device, steps, warmup, chunks, backend="strass
     native_sites = frozenset()
     if backend == "strassen" and site_policy == "measured":
         native_sites = qwen3.measured_native_sites(cfg, tp, batch * seq // max(1, chunks), device, seq=seq)
+    elif backend == "strassen" and site_policy == "fixed":
+        unknown = set(fixed_native) - set(qwen3.GEMM_SITES)
+        if unknown:
+            raise ValueError(f"--native-sites names unknown sites {sorted(unknown)}; sites: {qwen3.GEMM_SITES}")
+        native_sites = frozenset(fixed_native)
     model = qwen3.Qwen3Prefill(cfg, tp, device, backend=backend, layers=layers, native_sites=native_sites)
     g = torch.Generator().manual_seed(20260911)
     tokens_host = torch.randint(0, cfg.vocab, (batch, seq), generator=g).pin_memory()
@@ -644,7 +652,8 @@ def run_decoder(args):
     chunks = args.chunks if args.chunks is not None else (2 if world > 1 else 1)
     with ClockSampler(device.index) as clocks:
         r = measure_prefill(args.workload, tp, device, args.steps, args.warmup, chunks, backend=args.backend,
-                            eager=args.eager, layers=args.layers, site_policy=args.site_policy)
+                            eager=args.eager, layers=args.layers, site_policy=args.site_policy,
+                            fixed_native=frozenset(s for s in args.native_sites.split(",") if s))
     tp.close()
     if world > 1:
         dist.barrier(device_ids=[local])
