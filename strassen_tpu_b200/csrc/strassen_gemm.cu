@@ -1864,10 +1864,22 @@ size_t planes_workspace(int64_t m, int64_t n, int64_t k) {
   return planes_a_bytes(m, k) + quad_planes_bytes(k, n) + planes_prod_bytes(m, n);
 }
 
-// Shapes the planes path takes (256 x 256 product tiles, 64-deep steps) and that
-// give its persistent kernel at least two tiles per CTA pair of a B200.
+// Shapes the planes path takes (256 x 256 product tiles, 64-deep steps, at
+// least two tiles per CTA pair of a B200) and where it is expected to beat the
+// one-CTA kernel.  The estimate uses rates measured on B200: the product GEMM
+// runs 1.36 PFLOP/s of raw tensor work, the one-CTA kernel 0.67, and the extra
+// passes move their bytes at 6 TB/s -- operand planes (7/4 of A and of B
+// written, A and B read), the fp32 products written and read back, C written.
+// Small K loses: at 8192 x 4096 x 512 the products' round trip (0.47 GB) costs
+// twice the one-CTA kernel's whole GEMM.
 bool planes_preferred(int64_t m, int64_t n, int64_t k) {
-  return m % 512 == 0 && n % 512 == 0 && k % 128 == 0 && 7 * (m / 512) * (n / 512) >= 148;
+  if (m % 512 || n % 512 || k % 128 || 7 * (m / 512) * (n / 512) < 148) return false;
+  const double md = (double)m, nd = (double)n, kd = (double)k;
+  const double raw_flops = 1.75 * md * nd * kd;
+  const double bytes = 2.75 * 2.0 * (md * kd + kd * nd) + 7.0 * (md / 2) * (nd / 2) * 8.0 + md * nd * 2.0;
+  const double t_planes = raw_flops / 1.36e15 + bytes / 6.0e12;
+  const double t_one_cta = raw_flops / 0.67e15;
+  return t_planes < 0.9 * t_one_cta;
 }
 
 // The fused epilogue's operands, as both GEMM layouts read them.

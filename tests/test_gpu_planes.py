@@ -124,7 +124,7 @@ def test_planes_epilogues_match_one_cta_kernel(epilogue):
     """A product on the planes path (large enough, workspace given) applies the
     fused epilogue to the same recombined fp32 values as the one-CTA kernel."""
     import strassen_tpu_b200 as sb
-    m, k, n = 4096, 1024, 4096
+    m, k, n = 8192, 4096, 4096
     g = torch.Generator(device="cuda").manual_seed(11)
     a = torch.randn(m, k, device="cuda", generator=g).to(torch.bfloat16)
     b = (torch.randn(k, n, device="cuda", generator=g) * 0.05).to(torch.bfloat16)
@@ -135,7 +135,7 @@ def test_planes_epilogues_match_one_cta_kernel(epilogue):
         kw["bias"] = torch.randn(n, device="cuda", generator=g).to(torch.bfloat16)
     elif epilogue == "qk_norm_rope":
         cos = torch.rand(m, 512, device="cuda", generator=g).to(torch.bfloat16)
-        sin = torch.rand(m, 512, device="cuda", generator=g).to(torch.bfloat16)
+        sin = torch.rand(m, 512, device="cuda", generator=g).to(torch.bfloat16)  # [M, bn/2]
         scale = (1 + 0.1 * torch.randn(1024, device="cuda", generator=g)).to(torch.bfloat16)
         kw.update(rope_cos=cos, rope_sin=sin, rope_scale=scale, rope_head_dim=128)
     assert sb.workspace_bytes(m, n, k, epilogue) > 0  # the planes path is the default here

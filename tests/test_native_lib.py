@@ -86,3 +86,18 @@ def test_status_strings():
     with pytest.raises(_native.StrassenError):
         assert _gemm(lib, m=300) == 4
         _native.check(4)
+
+
+def test_planes_path_choice_follows_the_cost_model():
+    """sb_workspace_bytes asks for the planes workspace only where the planes path
+    is expected to beat the one-CTA kernel: large squares and wide K, not the
+    small-K row-parallel shards of a tensor-parallel decoder."""
+    from strassen_tpu_b200 import _native
+    lib = _native.load()
+    wants = lambda m, n, k, e=0: lib.sb_workspace_bytes(m, n, k, e) > 0
+    assert wants(8192, 8192, 8192) and wants(16384, 16384, 16384)
+    assert wants(16384, 24576, 4096, 1)            # Qwen3-8B gate/up + SwiGLU at TP=1
+    assert not wants(8192, 4096, 512, 3)           # o projection shard at TP=8 (K = 512)
+    assert not wants(2048, 2048, 2048)             # too few tiles
+    # norm_residual_add stays on the one-CTA kernel: its workspace is the fp32 rows.
+    assert lib.sb_workspace_bytes(8192, 8192, 8192, 6) == 8192 * 8192 * 4
