@@ -5,9 +5,11 @@
  * returns an sb_status code; nothing throws and nothing traps.  Argument
  * errors are detected on the host before any launch.  The caller owns every
  * buffer: the library allocates device memory only in sb_p2p_buffer_alloc,
- * whose job that is.  Scratch space that an epilogue needs
- * (norm_residual_add) is passed in as `workspace`, sized by
- * sb_workspace_bytes(); the one exception is
+ * whose job that is.  Scratch space is passed in as `workspace`, sized by
+ * sb_workspace_bytes(): the fp32 rows of norm_residual_add, and for large
+ * products the operand planes and fp32 products of the planes path (a caller
+ * that passes less gets the one-CTA kernel, which needs none); the one
+ * exception is
  * sb_strassen_gemm_norm_residual_noalloc, whose scratch is a fixed 32 MiB
  * device array built into the library (see its declaration).
  *
@@ -122,8 +124,12 @@ typedef struct sb_options {
  * Shapes: A [M,K] (lda), B [K,N] (ldb), C [M,N] (ldc) -- or [M, N/2] for the
  * swiglu/geglu epilogues.  out_dtype: SB_BF16 or SB_F32 (SB_F32 only without
  * an epilogue, as in the reference).  `ep` may be NULL for no epilogue.
- * workspace / workspace_bytes: caller-owned scratch, required only when
- * sb_workspace_bytes() returns a non-zero size.  Asynchronous on `stream`.
+ * workspace / workspace_bytes: caller-owned scratch.  norm_residual_add
+ * requires sb_workspace_bytes() bytes.  For other products a non-zero
+ * sb_workspace_bytes() is the planes path's workspace (see
+ * sb_strassen_gemm_planes): passing at least that much, 16-byte aligned, runs
+ * the product there; passing less (or NULL) runs the one-CTA kernel.  Same
+ * result either way up to fp32 summation order.  Asynchronous on `stream`.
  */
 SB_API int sb_strassen_gemm(sb_stream_t stream,
                      const void* a, const void* b, void* c,
@@ -147,7 +153,10 @@ SB_API int sb_strassen_gemm_ex(sb_stream_t stream,
                                const sb_options* opt,
                                void* workspace, size_t workspace_bytes);
 
-/* Scratch bytes sb_strassen_gemm needs for this problem (0 for most).
+/* Scratch bytes sb_strassen_gemm wants for this problem: the norm_residual_add
+ * rows, the planes path's workspace where a cost model with rates measured on
+ * B200 expects it to beat the one-CTA kernel (no epilogue or residual_add /
+ * bias_add / swiglu / geglu / qk_norm_rope; M, N % 512, K % 128), else 0.
  * Replaces the reference's VMEM scratch_shapes sizing (strassen_pallas.py:1074-1078). */
 SB_API size_t sb_workspace_bytes(int64_t m, int64_t n, int64_t k, int32_t epilogue_kind);
 
@@ -230,7 +239,8 @@ SB_API int sb_strassen_gemm_quad(sb_stream_t stream,
 
 /*
  * sb_strassen_gemm_planes -- C = A·B, no epilogue, as seven full-width product
- * GEMMs: two passes form the A operand planes [7][M/2][K/2] and the B operand
+ * GEMMs (sb_strassen_gemm runs the same path, with its fused epilogues applied
+ * in the recombination, when given this workspace): two passes form the A operand planes [7][M/2][K/2] and the B operand
  * planes [7][K/2][N/2] (the reference's pre-adds, strassen_pallas.py:324-379,
  * each rounded once to bf16), a persistent kernel on CTA pairs (tcgen05
  * cta_group::2, 256 x 256 product tiles) writes the seven fp32 products, and a
@@ -244,9 +254,9 @@ SB_API int sb_strassen_gemm_quad(sb_stream_t stream,
  * `stages`: which steps run (bit 0 the operand passes, bit 1 the product GEMM,
  * bit 2 the recombination; 7 = the whole product); the workspace carries the
  * intermediate results between calls, so a caller can time the GEMM alone.
- * sb_strassen_gemm / sb_strassen_gemm_ex take this path for a plain product
- * (no epilogue, no research option) when sb_workspace_bytes asks for the
- * planes workspace and the caller passes it.
+ * sb_strassen_gemm / sb_strassen_gemm_ex take this path (no research option;
+ * no epilogue or residual_add / bias_add / swiglu / geglu / qk_norm_rope) when
+ * sb_workspace_bytes asks for the planes workspace and the caller passes it.
  */
 SB_API size_t sb_planes_workspace_bytes(int64_t m, int64_t n, int64_t k);
 SB_API int sb_strassen_gemm_planes(sb_stream_t stream,

@@ -212,3 +212,24 @@ def test_narrow_bn_qk_norm_rope_needs_whole_half_heads():
         call(bn=128, narrow_bn=True, rope_head_dim=256, **rope)
     with pytest.raises(ValueError, match="needs bn a multiple of 2\\*head_dim=512"):
         call(bn=256, rope_head_dim=256, **rope)
+
+
+# --- planes_matmul (the seven-product-GEMM path) --------------------------------
+
+@pytest.mark.parametrize("kw, match", [
+    (dict(a=torch.zeros(2, 2, 2, dtype=BF)), "two rank-2 matrices"),
+    (dict(a=torch.zeros(512, 256, dtype=BF), b=torch.zeros(512, 512, dtype=BF)), "inner dimensions disagree"),
+    (dict(a=torch.zeros(512, 256, dtype=torch.float32)), "inputs must be BF16"),
+    (dict(a=torch.zeros(256, 256, dtype=BF)), "M % 512 == 0"),
+    (dict(b=torch.zeros(256, 256, dtype=BF)), "N % 512 == 0"),
+    (dict(bn=128), "bn=128 must be a multiple of 256"),
+    (dict(), "runs on a CUDA device"),  # valid arguments, CPU tensors: no CPU fallback
+])
+def test_planes_matmul_value_errors(kw, match):
+    a = kw.pop("a", torch.zeros(512, 256, dtype=BF))
+    b = kw.pop("b", torch.zeros(256, 512, dtype=BF))
+    kw.setdefault("bm", 256)
+    kw.setdefault("bn", 256)
+    kw.setdefault("bk", 256)
+    with pytest.raises(ValueError, match=match):
+        sb.planes_matmul(a, b, **kw)
