@@ -70,9 +70,10 @@ def parse():
                         "the command the committed ncu captures run")
     p.add_argument("--no-decoder", action="store_true", help="skip the decoder measurement of the GEMM run")
     p.add_argument("--epilogue", default="none", choices=["none", "norm_residual_add"],
-                   help="GEMM workload with a fused epilogue (one-CTA kernel): norm_residual_add runs "
-                        "the GEMM into an fp32 workspace and the row pass, tile (1024, N, 512) since "
-                        "the norm spans the row; the command the row pass's ncu capture runs")
+                   help="GEMM workload with a fused epilogue, tile (1024, N, 512) since the norm spans "
+                        "the row: on the planes path (default) one pass over the products normalises; "
+                        "with --kernel single the GEMM writes fp32 rows and the row pass normalises "
+                        "(the command the row pass's ncu capture runs)")
     p.add_argument("--workload", default="gemm", choices=["gemm", "qwen3-8b", "qwen3-32b"],
                    help="gemm: the 8192^3 Strassen GEMM (default, the driver's line); "
                         "qwen3-*: tensor-parallel decoder prefill tokens/s (BASELINE configs 4/5)")
@@ -277,18 +278,23 @@ def run_ours(args):
     launches_per_step = 1
     tile = TILE
     gemm_events = []  # (start, end) CUDA events around the dominant kernel, when it is one of several
-    if args.kernel == "planes" and args.epilogue != "none":
-        args.kernel = "single"  # the fused epilogues run on the one-CTA kernel
-    if args.epilogue != "none" and args.kernel != "single":
-        raise SystemExit("--epilogue runs on the one-CTA kernel (--kernel single)")
+    if args.epilogue != "none" and args.kernel not in ("single", "planes"):
+        raise SystemExit("--epilogue runs with --kernel planes (the default) or --kernel single")
     if args.epilogue == "norm_residual_add":
         tile = (TILE[0], N, TILE[2])  # the norm spans the whole row: bn = N
         g = torch.Generator(device=device).manual_seed(SEED_B + 1)
         residual = torch.randn(M, N, device=device, generator=g).to(torch.bfloat16)
         norm_scale = (1.0 + 0.02 * torch.randn(N, device=device, generator=g)).to(torch.bfloat16)
-        workspace = torch.empty(sb.workspace_bytes(M, N, K, epilogue="norm_residual_add"),
-                                dtype=torch.uint8, device=device)
-        launches_per_step = 2  # the GEMM into the fp32 workspace, the row pass
+        if args.kernel == "single":
+            # The fp32 rows only: the one-CTA kernel's GEMM, then its row pass.
+            workspace = torch.empty(M * N * 4, dtype=torch.uint8, device=device)
+            launches_per_step = 2
+        else:
+            # The planes workspace: operand passes, product GEMMs, one pass over
+            # the products that recombines, normalises and adds the residual.
+            workspace = torch.empty(sb.workspace_bytes(M, N, K, epilogue="norm_residual_add"),
+                                    dtype=torch.uint8, device=device)
+            launches_per_step = 4
 
         def step():
             sb.strassen_matmul(a, b, bm=tile[0], bn=tile[1], bk=tile[2], epilogue="norm_residual_add",

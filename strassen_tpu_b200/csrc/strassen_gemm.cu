@@ -1205,6 +1205,74 @@ __global__ void __launch_bounds__(256) norm_residual_rows_scalar_kernel(
   }
 }
 
+// norm_residual_add on the planes path in one pass over the products: one CTA
+// per product row t, whose seven fp32 products give both of its output rows
+// whole (bn == n: C row I*bm + r' = [C11 | C12], row + bm/2 = [C21 | C22]).
+// Each thread recombines up to kChunks 8-column pieces in registers
+// (C11 = M1 + M4 - M5 + M7, C12 = M3 + M5, C21 = M2 + M4, C22 = M1 - M2 + M3 + M6,
+// the one-CTA kernel's order), the block reduces both rows' sums of squares,
+// and the normalised rows plus the residual are stored as bf16
+// (strassen_pallas.py:836-866).  No fp32 pre-norm row goes to memory.  Needs
+// nh = N/2 <= 8 * 256 * kChunks and 16-byte aligned residual, scale and C rows.
+template <int kChunks>
+__global__ void __launch_bounds__(256) planes_norm_rows_kernel(const float* __restrict__ prod, int32_t mh, int32_t nh,
+                                                               int32_t bm, const void* __restrict__ scale,
+                                                               int scale_f32, const void* __restrict__ residual,
+                                                               int64_t ldr, int residual_f32, float eps,
+                                                               __nv_bfloat16* __restrict__ out, int64_t ldo) {
+  const int64_t t = blockIdx.x;
+  const int64_t plane = (int64_t)mh * nh;
+  const int64_t hbm = bm / 2;
+  const int64_t blk = t / hbm;
+  const int64_t row_top = blk * bm + (t - blk * hbm), row_bot = row_top + hbm;
+  const int pieces = nh / 8;
+  float q[kChunks][4][8];
+  float s_top = 0.f, s_bot = 0.f;
+#pragma unroll
+  for (int c = 0; c < kChunks; ++c) {
+    const int pc = threadIdx.x + c * 256;
+    if (pc < pieces) {
+      float mv[7][8];
+#pragma unroll
+      for (int i = 0; i < 7; ++i) load8_f32(prod + i * plane, true, t * nh + 8 * (int64_t)pc, mv[i]);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        q[c][0][e] = ((mv[0][e] + mv[3][e]) - mv[4][e]) + mv[6][e];
+        q[c][1][e] = mv[2][e] + mv[4][e];
+        q[c][2][e] = mv[1][e] + mv[3][e];
+        q[c][3][e] = ((mv[0][e] - mv[1][e]) + mv[2][e]) + mv[5][e];
+        s_top += q[c][0][e] * q[c][0][e] + q[c][1][e] * q[c][1][e];
+        s_bot += q[c][2][e] * q[c][2][e] + q[c][3][e] * q[c][3][e];
+      }
+    }
+  }
+  const float2 sums = block_sum2(s_top, s_bot);
+  const float inv_n = 1.0f / (2.0f * (float)nh);
+  const float rt = 1.0f / sqrtf(sums.x * inv_n + eps), rb = 1.0f / sqrtf(sums.y * inv_n + eps);
+#pragma unroll
+  for (int c = 0; c < kChunks; ++c) {
+    const int pc = threadIdx.x + c * 256;
+    if (pc < pieces) {
+      const int64_t cl = 8 * (int64_t)pc, cr = cl + nh;
+      float sl[8], sr[8], r[8], o[8];
+      load8_f32(scale, scale_f32, cl, sl);
+      load8_f32(scale, scale_f32, cr, sr);
+#pragma unroll
+      for (int qd = 0; qd < 4; ++qd) {
+        const int64_t row = qd < 2 ? row_top : row_bot;
+        const int64_t col = (qd & 1) ? cr : cl;
+        const float rec = qd < 2 ? rt : rb;
+        load8_f32(residual, residual_f32, row * ldr + col, r);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) o[e] = q[c][qd][e] * rec * ((qd & 1) ? sr[e] : sl[e]) + r[e];
+        *reinterpret_cast<uint4*>(out + row * ldo + col) =
+            make_uint4(pack_bf16x2(o[0], o[1]), pack_bf16x2(o[2], o[3]), pack_bf16x2(o[4], o[5]),
+                       pack_bf16x2(o[6], o[7]));
+      }
+    }
+  }
+}
+
 // Standalone RMSNorm (experiments/qwen3/benchmark_qwen3_32b_layer.py:270-276):
 // y = bf16(x * rsqrt(mean(x^2) + eps) * w), fp32 math.  One CTA per row,
 // 16-byte vector loads.
@@ -1904,8 +1972,12 @@ void fill_epilogue(GemmParams& p, const sb_epilogue* ep, int epi) {
 // Epilogues the planes path applies in its recombination pass.
 bool planes_epilogue(int epi) {
   return epi == SB_EPI_NONE || epi == SB_EPI_RESIDUAL_ADD || epi == SB_EPI_BIAS_ADD || epi == SB_EPI_SWIGLU ||
-         epi == SB_EPI_GEGLU || epi == SB_EPI_QK_NORM_ROPE;
+         epi == SB_EPI_GEGLU || epi == SB_EPI_QK_NORM_ROPE || epi == SB_EPI_NORM_RESIDUAL_ADD;
 }
+
+// norm_residual_add on the planes path keeps a row's pieces in registers:
+// N/2 <= 8 * 256 * 2 (planes_norm_rows_kernel<2>).
+constexpr int64_t kPlanesNormMaxN = 2 * 8 * 256 * 2;
 
 // Persistent launch: one cluster (CTA pair) per two SMs, each walking its tiles.
 int launch_planes_gemm(cudaStream_t stream, const CUtensorMap& ta, const CUtensorMap& tb, const PlanesParams& p) {
@@ -2006,6 +2078,20 @@ int run_planes(cudaStream_t stream, const void* a, const void* b, void* c, int64
     const unsigned grid = (unsigned)std::min<int64_t>((items + 255) / 256, 148 * 16);
     GemmParams ep_p = base_params(m, n, k, bm, bn, bk, c, ldc, 16);
     fill_epilogue(ep_p, ep, epi);
+    if (epi == SB_EPI_NORM_RESIDUAL_ADD) {
+      const bool vec = aligned16(ep->norm_scale) && aligned16(ep->residual) && aligned16(c) && ldc % 8 == 0 &&
+                       ep->ld_residual % (ep->residual_dtype == SB_F32 ? 4 : 8) == 0;
+      if (!vec || n > kPlanesNormMaxN)
+        return fail(SB_ERR_ALIGNMENT, "norm_residual_add on the planes path needs N <= 8192 and 16-byte aligned "
+                                      "scale, residual and output rows");
+      auto kernel = (nh / 8 <= 256) ? planes_norm_rows_kernel<1> : planes_norm_rows_kernel<2>;
+      kernel<<<(unsigned)mh, 256, 0, stream>>>(prod, mh, nh, bm, ep->norm_scale, ep->aux_dtype == SB_F32,
+                                               ep->residual, ep->ld_residual, ep->residual_dtype == SB_F32,
+                                               ep->norm_eps, reinterpret_cast<__nv_bfloat16*>(c), ldc);
+      const cudaError_t e = cudaGetLastError();
+      if (e != cudaSuccess) return fail(SB_ERR_CUDA, std::string("planes norm rows launch: ") + cudaGetErrorString(e));
+      return SB_OK;
+    }
     switch (epi) {
       case SB_EPI_RESIDUAL_ADD:
         planes_recombine_kernel<SB_EPI_RESIDUAL_ADD, false><<<grid, 256, 0, stream>>>(prod, mh, nh, ep_p);
@@ -2051,9 +2137,12 @@ using namespace sb;
 extern "C" {
 
 size_t sb_workspace_bytes(int64_t m, int64_t n, int64_t k, int32_t epilogue_kind) {
-  if (epilogue_kind == SB_EPI_NORM_RESIDUAL_ADD && m > 0 && n > 0) return (size_t)m * (size_t)n * 4u;
-  if (planes_epilogue(epilogue_kind) && m > 0 && n > 0 && k > 0 && planes_preferred(m, n, k))
-    return planes_workspace(m, n, k);
+  if (m <= 0 || n <= 0 || k <= 0) return 0;
+  const bool planes = planes_epilogue(epilogue_kind) && planes_preferred(m, n, k) &&
+                      (epilogue_kind != SB_EPI_NORM_RESIDUAL_ADD || n <= kPlanesNormMaxN);
+  if (planes) return std::max(planes_workspace(m, n, k), epilogue_kind == SB_EPI_NORM_RESIDUAL_ADD
+                                                             ? (size_t)m * (size_t)n * 4u : (size_t)0);
+  if (epilogue_kind == SB_EPI_NORM_RESIDUAL_ADD) return (size_t)m * (size_t)n * 4u;
   return 0;
 }
 
@@ -2101,9 +2190,14 @@ int sb_strassen_gemm_ex(sb_stream_t stream_, const void* a, const void* b, void*
     if (bn != n)
       return fail(SB_ERR_EPILOGUE, "norm_residual_add normalises over the whole output row, so the tile must "
                                    "span it: bn=" + std::to_string(bn) + " must equal n=" + std::to_string(n));
-    if (!workspace || workspace_bytes < sb_workspace_bytes(m, n, k, epi) || !aligned16(workspace))
-      return fail(SB_ERR_WORKSPACE, "norm_residual_add needs a 16-byte aligned workspace of " +
-                                        std::to_string(sb_workspace_bytes(m, n, k, epi)) + " bytes");
+    // The fp32 rows of the one-CTA kernel's two passes at least; the planes
+    // path (sb_workspace_bytes) runs when the caller passes its larger workspace.
+    const size_t rows_bytes = (size_t)m * (size_t)n * 4u;
+    if (!workspace || workspace_bytes < rows_bytes || !aligned16(workspace))
+      return fail(SB_ERR_WORKSPACE, "norm_residual_add needs a 16-byte aligned workspace of at least " +
+                                        std::to_string(rows_bytes) + " bytes (" +
+                                        std::to_string(sb_workspace_bytes(m, n, k, epi)) +
+                                        " for the planes path)");
   }
   if (epi == SB_EPI_QK_NORM_ROPE) {
     if (!ep->rope_cos || !ep->rope_sin || !ep->rope_scale)
@@ -2128,7 +2222,11 @@ int sb_strassen_gemm_ex(sb_stream_t stream_, const void* a, const void* b, void*
   // A product with room for the planes workspace runs as seven full-width
   // product GEMMs (same products, rounding and recombination order; the fused
   // epilogue applied to the recombined fp32 values as the one-CTA kernel does).
-  if (planes_epilogue(epi) && formula == SB_FORMULA_CLASSICAL && perm == 0 && !schedule && !narrow &&
+  const bool norm_ok = epi != SB_EPI_NORM_RESIDUAL_ADD ||
+                       (n <= kPlanesNormMaxN && aligned16(ep->norm_scale) && aligned16(ep->residual) &&
+                        aligned16(c) && ldc % 8 == 0 &&
+                        ep->ld_residual % (ep->residual_dtype == SB_F32 ? 4 : 8) == 0);
+  if (planes_epilogue(epi) && norm_ok && formula == SB_FORMULA_CLASSICAL && perm == 0 && !schedule && !narrow &&
       planes_preferred(m, n, k) && workspace && aligned16(workspace) &&
       workspace_bytes >= planes_workspace(m, n, k))
     return run_planes(stream, a, b, c, m, n, k, lda, ldb, ldc, bm, bn, bk, out_dtype, workspace, workspace_bytes,

@@ -341,12 +341,18 @@ def strassen_matmul(
     if ws_bytes:
         if workspace is None:
             workspace = torch.empty(ws_bytes, dtype=torch.uint8, device=device)
-        if workspace.numel() * workspace.element_size() < ws_bytes:
+        have = workspace.numel() * workspace.element_size()
+        if have < ws_bytes:
             if ep.kind == EPILOGUE_KINDS["norm_residual_add"]:
-                raise ValueError(f"workspace must hold {ws_bytes} bytes")
-            # Without room for the planes path the product runs on the one-CTA
-            # kernel, which needs no workspace.
-            ws_bytes = 0
+                # The one-CTA kernel's two-pass norm needs the fp32 rows.
+                rows_bytes = m * n * 4
+                if have < rows_bytes:
+                    raise ValueError(f"workspace must hold {rows_bytes} bytes")
+                ws_bytes, ws_ptr = have, workspace.data_ptr()
+            else:
+                # Without room for the planes path the product runs on the
+                # one-CTA kernel, which needs no workspace.
+                ws_bytes = 0
         else:
             ws_ptr = workspace.data_ptr()
     with torch.cuda.device(device):

@@ -119,7 +119,8 @@ def test_planes_validation():
     assert _native.device_status() == 0
 
 
-@pytest.mark.parametrize("epilogue", ["residual_add", "bias_add", "swiglu", "geglu", "qk_norm_rope"])
+@pytest.mark.parametrize("epilogue", ["residual_add", "bias_add", "swiglu", "geglu", "qk_norm_rope",
+                                      "norm_residual_add"])
 def test_planes_epilogues_match_one_cta_kernel(epilogue):
     """A product on the planes path (large enough, workspace given) applies the
     fused epilogue to the same recombined fp32 values as the one-CTA kernel."""
@@ -129,7 +130,13 @@ def test_planes_epilogues_match_one_cta_kernel(epilogue):
     a = torch.randn(m, k, device="cuda", generator=g).to(torch.bfloat16)
     b = (torch.randn(k, n, device="cuda", generator=g) * 0.05).to(torch.bfloat16)
     kw = dict(bm=1024, bn=1024, bk=512, epilogue=epilogue)
-    if epilogue == "residual_add":
+    if epilogue == "norm_residual_add":
+        # The norm spans the row (bn == n): single pass over the products on
+        # the planes path, GEMM + fp32 rows + row pass on the one-CTA kernel.
+        kw["bn"] = n
+        kw["residual"] = torch.randn(m, n, device="cuda", generator=g).to(torch.bfloat16)
+        kw["norm_scale"] = (1 + 0.1 * torch.randn(n, device="cuda", generator=g)).to(torch.bfloat16)
+    elif epilogue == "residual_add":
         kw["residual"] = torch.randn(m, n, device="cuda", generator=g).to(torch.bfloat16)
     elif epilogue == "bias_add":
         kw["bias"] = torch.randn(n, device="cuda", generator=g).to(torch.bfloat16)
@@ -140,7 +147,10 @@ def test_planes_epilogues_match_one_cta_kernel(epilogue):
         kw.update(rope_cos=cos, rope_sin=sin, rope_scale=scale, rope_head_dim=128)
     assert sb.workspace_bytes(m, n, k, epilogue) > 0  # the planes path is the default here
     seven = sb.strassen_matmul(a, b, **kw)
-    one = sb.strassen_matmul(a, b, **kw, workspace=torch.empty(0, dtype=torch.uint8, device="cuda"))
+    # A workspace below the planes path's keeps the one-CTA kernel (for
+    # norm_residual_add: exactly its fp32 rows).
+    small = m * n * 4 if epilogue == "norm_residual_add" else 0
+    one = sb.strassen_matmul(a, b, **kw, workspace=torch.empty(small, dtype=torch.uint8, device="cuda"))
     torch.cuda.synchronize()
     assert seven.shape == one.shape
     assert_parity(host(seven), host(one), rounding_step=True)

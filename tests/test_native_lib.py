@@ -99,5 +99,8 @@ def test_planes_path_choice_follows_the_cost_model():
     assert wants(16384, 24576, 4096, 1)            # Qwen3-8B gate/up + SwiGLU at TP=1
     assert not wants(8192, 4096, 512, 3)           # o projection shard at TP=8 (K = 512)
     assert not wants(2048, 2048, 2048)             # too few tiles
-    # norm_residual_add stays on the one-CTA kernel: its workspace is the fp32 rows.
-    assert lib.sb_workspace_bytes(8192, 8192, 8192, 6) == 8192 * 8192 * 4
+    # norm_residual_add: the planes workspace where the planes path takes it
+    # (N <= 8192, one pass over the products), else the one-CTA kernel's fp32 rows.
+    assert lib.sb_workspace_bytes(8192, 8192, 8192, 6) == lib.sb_planes_workspace_bytes(8192, 8192, 8192)
+    assert lib.sb_workspace_bytes(8192, 16384, 8192, 6) == 8192 * 16384 * 4
+    assert lib.sb_workspace_bytes(1024, 1024, 1024, 6) == 1024 * 1024 * 4
