@@ -98,3 +98,28 @@ def test_sweep_shape(m, k, n):
     maxnorm = (err.abs().max() / fp32.abs().max()).item()
     assert rmse <= 4.0 * nat_rmse, (rmse, nat_rmse)
     assert maxnorm <= 0.01, maxnorm
+
+
+@pytest.mark.slow
+@pytest.mark.parametrize("path", ["one_cta", "planes"])
+def test_whole_output_against_the_oracle_2048(path):
+    """The parity rule on a whole 2048^3 output (not sampled rows): max|diff|
+    <= 2e-2 rms and rmse vs fp64 <= 2x the oracle's, in fp32 and in bf16, for
+    the one-CTA kernel and the planes path."""
+    import strassen_tpu_b200 as sb
+    m = k = n = 2048
+    tile = dict(bm=1024, bn=1024, bk=512)
+    a = ref.normal_bf16((m, k), 20260904)
+    b = ref.normal_bf16((k, n), 20260905)
+    ad, bd = dev_bf16(a), dev_bf16(b)
+    if path == "planes":
+        got32 = sb.planes_matmul(ad, bd, output_dtype=torch.float32, **tile)
+        got = sb.planes_matmul(ad, bd, **tile)
+    else:
+        got32 = sb.strassen_matmul(ad, bd, output_dtype=torch.float32, **tile)
+        got = sb.strassen_matmul(ad, bd, **tile)
+    torch.cuda.synchronize()
+    want32 = ref.strassen_matmul_ref(a, b, output_dtype="float32", **tile)
+    exact = ref.classical_f64(a, b)
+    assert_parity(host(got32), want32, exact)
+    assert_parity(host(got), ref.bf16_round(want32), exact, rounding_step=True)
