@@ -254,6 +254,12 @@ SB_API int sb_strassen_gemm_quad(sb_stream_t stream,
  * `stages`: which steps run (bit 0 the operand passes, bit 1 the product GEMM,
  * bit 2 the recombination; 7 = the whole product); the workspace carries the
  * intermediate results between calls, so a caller can time the GEMM alone.
+ * The whole product runs in two halves of product rows, the second on a
+ * stream of the library's (forked from and joined back into `stream`), so each
+ * half's passes and recombination overlap the other half's GEMM.
+ * `timing_events`: NULL, or four cudaEvent_t the call records around its GEMM
+ * launches (stages 7: first half on `stream`, second half on the side stream;
+ * stages 2: the one launch, events 0 and 1).
  * sb_strassen_gemm / sb_strassen_gemm_ex take this path (no research option;
  * no epilogue or residual_add / bias_add / swiglu / geglu / qk_norm_rope) when
  * sb_workspace_bytes asks for the planes workspace and the caller passes it.
@@ -265,7 +271,7 @@ SB_API int sb_strassen_gemm_planes(sb_stream_t stream,
                                    int64_t lda, int64_t ldb, int64_t ldc,
                                    int32_t bm, int32_t bn, int32_t bk, int32_t out_dtype,
                                    void* workspace, size_t workspace_bytes, int32_t raster,
-                                   int32_t stages);
+                                   int32_t stages, void* const* timing_events);
 
 /*
  * sb_strassen_gemm_norm_residual_noalloc -- the norm_residual_add epilogue of

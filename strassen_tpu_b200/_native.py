@@ -100,7 +100,7 @@ SIGNATURES = {
     "sb_planes_workspace_bytes": (_c_size, [_c_i64, _c_i64, _c_i64]),
     "sb_strassen_gemm_planes": (_c_int, [_c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_i64, _c_i64, _c_i64,
                                          _c_i64, _c_i64, _c_i64, _c_int, _c_int, _c_int, _c_int,
-                                         _c_ptr, _c_size, _c_int, _c_int]),
+                                         _c_ptr, _c_size, _c_int, _c_int, _c_ptr]),
     "sb_strassen_gemm_quad": (_c_int, [_c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_i64, _c_i64, _c_i64,
                                        _c_i64, _c_i64, _c_i64, _c_int, _c_int, _c_int, _c_int,
                                        _c_ptr, _c_size, _c_int]),

@@ -1219,8 +1219,9 @@ __global__ void __launch_bounds__(256) planes_norm_rows_kernel(const float* __re
                                                                int32_t bm, const void* __restrict__ scale,
                                                                int scale_f32, const void* __restrict__ residual,
                                                                int64_t ldr, int residual_f32, float eps,
-                                                               __nv_bfloat16* __restrict__ out, int64_t ldo) {
-  const int64_t t = blockIdx.x;
+                                                               __nv_bfloat16* __restrict__ out, int64_t ldo,
+                                                               int64_t t0) {
+  const int64_t t = t0 + blockIdx.x;
   const int64_t plane = (int64_t)mh * nh;
   const int64_t hbm = bm / 2;
   const int64_t blk = t / hbm;
@@ -2015,14 +2016,124 @@ int launch_planes_gemm(cudaStream_t stream, const CUtensorMap& ta, const CUtenso
   return SB_OK;
 }
 
-// Operand passes, the seven product GEMMs and the recombination, in stream
-// order.  `stages` selects them (bit 0 the operand passes, bit 1 the product
-// GEMM, bit 2 the recombination; 7 = all) so a caller can time the GEMM alone;
-// the workspace carries the intermediate results between separate calls.
+// One row range [t0, t1) of product rows (multiples of 256) through one step
+// of the planes path, on `stream`.
+int planes_a_pass(cudaStream_t stream, const void* a, int64_t lda, int64_t m, int64_t k, int32_t bm, int32_t bk,
+                  __nv_bfloat16* aop, int64_t t0, int64_t t1) {
+  const int64_t items = (t1 - t0) * (k / 2 / 8);
+  const unsigned grid = (unsigned)std::max<int64_t>(1, std::min<int64_t>((items + 255) / 256, 148 * 16));
+  a_operand_planes_kernel<<<grid, 256, 0, stream>>>(reinterpret_cast<const __nv_bfloat16*>(a), lda, (int32_t)m,
+                                                    (int32_t)k, bm, bk, aop, t0, t1);
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return fail(SB_ERR_CUDA, std::string("A planes launch: ") + cudaGetErrorString(e));
+  return SB_OK;
+}
+
+int planes_gemm(cudaStream_t stream, const CUtensorMap& ta, const CUtensorMap& tb, int64_t m, int64_t n, int64_t k,
+                int32_t raster, float* prod, int64_t t0, int64_t t1) {
+  PlanesParams p;
+  std::memset(&p, 0, sizeof(p));
+  p.mh = (int32_t)(m / 2);
+  p.nh = (int32_t)(n / 2);
+  p.kh = (int32_t)(k / 2);
+  p.tile_m0 = (int32_t)(t0 / planes::kTileM);
+  p.tiles_m = (int32_t)((t1 - t0) / planes::kTileM);
+  p.tiles_n = p.nh / planes::kTileN;
+  p.num_tiles = 7 * p.tiles_m * p.tiles_n;
+  p.k_steps = p.kh / planes::kBK;
+  p.raster = raster;
+  p.prod = prod;
+  p.err = t_error_word;
+  return launch_planes_gemm(stream, ta, tb, p);
+}
+
+int planes_recombine(cudaStream_t stream, const float* prod, int64_t m, int64_t n, int64_t k, int32_t bm, int32_t bn,
+                     int32_t bk, void* c, int64_t ldc, int32_t out_dtype, int epi, const sb_epilogue* ep, int64_t t0,
+                     int64_t t1) {
+  const int32_t mh = (int32_t)(m / 2), nh = (int32_t)(n / 2);
+  const int64_t items = (t1 - t0) * (nh / 8);
+  const unsigned grid = (unsigned)std::max<int64_t>(1, std::min<int64_t>((items + 255) / 256, 148 * 16));
+  GemmParams ep_p = base_params(m, n, k, bm, bn, bk, c, ldc, 16);
+  fill_epilogue(ep_p, ep, epi);
+  if (epi == SB_EPI_NORM_RESIDUAL_ADD) {
+    const bool vec = aligned16(ep->norm_scale) && aligned16(ep->residual) && aligned16(c) && ldc % 8 == 0 &&
+                     ep->ld_residual % (ep->residual_dtype == SB_F32 ? 4 : 8) == 0;
+    if (!vec || n > kPlanesNormMaxN)
+      return fail(SB_ERR_ALIGNMENT, "norm_residual_add on the planes path needs N <= 8192 and 16-byte aligned "
+                                    "scale, residual and output rows");
+    auto kernel = (nh / 8 <= 256) ? planes_norm_rows_kernel<1> : planes_norm_rows_kernel<2>;
+    kernel<<<(unsigned)(t1 - t0), 256, 0, stream>>>(prod, mh, nh, bm, ep->norm_scale, ep->aux_dtype == SB_F32,
+                                                    ep->residual, ep->ld_residual, ep->residual_dtype == SB_F32,
+                                                    ep->norm_eps, reinterpret_cast<__nv_bfloat16*>(c), ldc, t0);
+  } else {
+    switch (epi) {
+      case SB_EPI_RESIDUAL_ADD:
+        planes_recombine_kernel<SB_EPI_RESIDUAL_ADD, false><<<grid, 256, 0, stream>>>(prod, mh, nh, ep_p, t0, t1);
+        break;
+      case SB_EPI_BIAS_ADD:
+        planes_recombine_kernel<SB_EPI_BIAS_ADD, false><<<grid, 256, 0, stream>>>(prod, mh, nh, ep_p, t0, t1);
+        break;
+      case SB_EPI_SWIGLU:
+        planes_recombine_kernel<SB_EPI_SWIGLU, false><<<grid, 256, 0, stream>>>(prod, mh, nh, ep_p, t0, t1);
+        break;
+      case SB_EPI_GEGLU:
+        planes_recombine_kernel<SB_EPI_GEGLU, false><<<grid, 256, 0, stream>>>(prod, mh, nh, ep_p, t0, t1);
+        break;
+      case SB_EPI_QK_NORM_ROPE:
+        planes_recombine_kernel<SB_EPI_QK_NORM_ROPE, false><<<grid, 256, 0, stream>>>(prod, mh, nh, ep_p, t0, t1);
+        break;
+      default:
+        if (out_dtype == SB_F32)
+          planes_recombine_kernel<SB_EPI_NONE, true><<<grid, 256, 0, stream>>>(prod, mh, nh, ep_p, t0, t1);
+        else
+          planes_recombine_kernel<SB_EPI_NONE, false><<<grid, 256, 0, stream>>>(prod, mh, nh, ep_p, t0, t1);
+    }
+  }
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return fail(SB_ERR_CUDA, std::string("recombination launch: ") + cudaGetErrorString(e));
+  return SB_OK;
+}
+
+// A second stream and fork/join events per device and host thread, created on
+// first use: the planes path runs its second row half there.
+struct PlanesSide {
+  cudaStream_t aux = nullptr;
+  cudaEvent_t fork = nullptr, b_done = nullptr, join = nullptr;
+};
+
+int planes_side(PlanesSide** out) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return fail(SB_ERR_DEVICE, "no usable current device");
+  thread_local PlanesSide side[64];
+  PlanesSide& s = side[dev];
+  if (!s.aux) {
+    cudaError_t e = cudaStreamCreateWithFlags(&s.aux, cudaStreamNonBlocking);
+    if (e == cudaSuccess) e = cudaEventCreateWithFlags(&s.fork, cudaEventDisableTiming);
+    if (e == cudaSuccess) e = cudaEventCreateWithFlags(&s.b_done, cudaEventDisableTiming);
+    if (e == cudaSuccess) e = cudaEventCreateWithFlags(&s.join, cudaEventDisableTiming);
+    if (e != cudaSuccess) {
+      s.aux = nullptr;
+      return fail(SB_ERR_CUDA, std::string("planes side stream: ") + cudaGetErrorString(e));
+    }
+  }
+  *out = &s;
+  return SB_OK;
+}
+
+// Operand passes, the seven product GEMMs and the recombination.  `stages`
+// selects them (bit 0 the operand passes, bit 1 the product GEMM, bit 2 the
+// recombination) so a caller can time the GEMM alone; the workspace carries
+// the intermediate results between separate calls.  The whole product
+// (stages 7) runs in two halves of product rows: the second half's A pass,
+// GEMM and recombination on a second stream, so the passes and the
+// recombination of one half overlap the other half's GEMM (their kernels need
+// no shared memory and fit on an SM beside a GEMM CTA) and the two GEMMs fill
+// each other's last wave.  `timing` (optional, four cudaEvent_t): recorded
+// around the two GEMM launches, on the stream each runs on.
 int run_planes(cudaStream_t stream, const void* a, const void* b, void* c, int64_t m, int64_t n, int64_t k,
                int64_t lda, int64_t ldb, int64_t ldc, int32_t bm, int32_t bn, int32_t bk, int32_t out_dtype,
                void* workspace, size_t workspace_bytes, int32_t raster, int32_t stages = 7,
-               int epi = SB_EPI_NONE, const sb_epilogue* ep = nullptr) {
+               int epi = SB_EPI_NONE, const sb_epilogue* ep = nullptr, void* const* timing = nullptr) {
   const bool gated = epi == SB_EPI_SWIGLU || epi == SB_EPI_GEGLU;  // output [M, N/2]
   if (ldc < (gated ? n / 2 : n)) return fail(SB_ERR_ALIGNMENT, gated ? "ldc must be >= N/2" : "ldc must be >= N");
   if (raster < 0) return fail(SB_ERR_UNSUPPORTED, "raster must be >= 0 (0 = the kernel's default)");
@@ -2043,80 +2154,55 @@ int run_planes(cudaStream_t stream, const void* a, const void* b, void* c, int64
   __nv_bfloat16* aop = reinterpret_cast<__nv_bfloat16*>(ws);
   void* bop = ws + a_bytes;
   float* prod = reinterpret_cast<float*>(ws + a_bytes + b_bytes);
+  const int64_t mh = m / 2;
+  CUtensorMap ta, tb;
+  if (stages & 2) {
+    st = make_planes_maps(aop, bop, m, n, k, &ta, &tb);
+    if (st != SB_OK) return st;
+  }
+  auto ev = [&](int i) { return timing ? static_cast<cudaEvent_t>(timing[i]) : nullptr; };
+  auto chk = [&](cudaError_t e, const char* what) {
+    return e == cudaSuccess ? SB_OK : fail(SB_ERR_CUDA, std::string(what) + ": " + cudaGetErrorString(e));
+  };
+
+  if (stages == 7 && mh >= 2 * planes::kTileM) {
+    PlanesSide* side = nullptr;
+    st = planes_side(&side);
+    if (st != SB_OK) return st;
+    const int64_t half = (mh / planes::kTileM / 2) * planes::kTileM;  // first half's product rows
+    cudaStream_t aux = side->aux;
+    if ((st = chk(cudaEventRecord(side->fork, stream), "fork")) != SB_OK) return st;
+    if ((st = chk(cudaStreamWaitEvent(aux, side->fork, 0), "fork wait")) != SB_OK) return st;
+    st = sb_strassen_b_operands(reinterpret_cast<sb_stream_t>(stream), b, bop, k, n, ldb, bn, bk);
+    if (st != SB_OK) return st;
+    if ((st = chk(cudaEventRecord(side->b_done, stream), "B planes event")) != SB_OK) return st;
+    if ((st = planes_a_pass(stream, a, lda, m, k, bm, bk, aop, 0, half)) != SB_OK) return st;
+    if ((st = planes_a_pass(aux, a, lda, m, k, bm, bk, aop, half, mh)) != SB_OK) return st;
+    if ((st = chk(cudaStreamWaitEvent(aux, side->b_done, 0), "B planes wait")) != SB_OK) return st;
+    if (ev(0) && (st = chk(cudaEventRecord(ev(0), stream), "timing event")) != SB_OK) return st;
+    if ((st = planes_gemm(stream, ta, tb, m, n, k, raster, prod, 0, half)) != SB_OK) return st;
+    if (ev(1) && (st = chk(cudaEventRecord(ev(1), stream), "timing event")) != SB_OK) return st;
+    if (ev(2) && (st = chk(cudaEventRecord(ev(2), aux), "timing event")) != SB_OK) return st;
+    if ((st = planes_gemm(aux, ta, tb, m, n, k, raster, prod, half, mh)) != SB_OK) return st;
+    if (ev(3) && (st = chk(cudaEventRecord(ev(3), aux), "timing event")) != SB_OK) return st;
+    if ((st = planes_recombine(stream, prod, m, n, k, bm, bn, bk, c, ldc, out_dtype, epi, ep, 0, half)) != SB_OK)
+      return st;
+    if ((st = planes_recombine(aux, prod, m, n, k, bm, bn, bk, c, ldc, out_dtype, epi, ep, half, mh)) != SB_OK)
+      return st;
+    if ((st = chk(cudaEventRecord(side->join, aux), "join")) != SB_OK) return st;
+    return chk(cudaStreamWaitEvent(stream, side->join, 0), "join wait");
+  }
   if (stages & 1) {
     st = sb_strassen_b_operands(reinterpret_cast<sb_stream_t>(stream), b, bop, k, n, ldb, bn, bk);
     if (st != SB_OK) return st;
-    const int64_t items = (m / 2) * (k / 2 / 8);
-    const unsigned grid = (unsigned)std::min<int64_t>((items + 255) / 256, 148 * 16);
-    a_operand_planes_kernel<<<grid, 256, 0, stream>>>(reinterpret_cast<const __nv_bfloat16*>(a), lda, (int32_t)m,
-                                                      (int32_t)k, bm, bk, aop);
-    const cudaError_t e = cudaGetLastError();
-    if (e != cudaSuccess) return fail(SB_ERR_CUDA, std::string("A planes launch: ") + cudaGetErrorString(e));
+    if ((st = planes_a_pass(stream, a, lda, m, k, bm, bk, aop, 0, mh)) != SB_OK) return st;
   }
-  const int32_t mh = (int32_t)(m / 2), nh = (int32_t)(n / 2);
   if (stages & 2) {
-    CUtensorMap ta, tb;
-    st = make_planes_maps(aop, bop, m, n, k, &ta, &tb);
-    if (st != SB_OK) return st;
-    PlanesParams p;
-    std::memset(&p, 0, sizeof(p));
-    p.mh = mh;
-    p.nh = nh;
-    p.kh = (int32_t)(k / 2);
-    p.tiles_m = p.mh / planes::kTileM;
-    p.tiles_n = p.nh / planes::kTileN;
-    p.num_tiles = 7 * p.tiles_m * p.tiles_n;
-    p.k_steps = p.kh / planes::kBK;
-    p.raster = raster;
-    p.prod = prod;
-    p.err = t_error_word;
-    st = launch_planes_gemm(stream, ta, tb, p);
-    if (st != SB_OK) return st;
+    if (ev(0) && (st = chk(cudaEventRecord(ev(0), stream), "timing event")) != SB_OK) return st;
+    if ((st = planes_gemm(stream, ta, tb, m, n, k, raster, prod, 0, mh)) != SB_OK) return st;
+    if (ev(1) && (st = chk(cudaEventRecord(ev(1), stream), "timing event")) != SB_OK) return st;
   }
-  if (stages & 4) {
-    const int64_t items = (int64_t)mh * (nh / 8);
-    const unsigned grid = (unsigned)std::min<int64_t>((items + 255) / 256, 148 * 16);
-    GemmParams ep_p = base_params(m, n, k, bm, bn, bk, c, ldc, 16);
-    fill_epilogue(ep_p, ep, epi);
-    if (epi == SB_EPI_NORM_RESIDUAL_ADD) {
-      const bool vec = aligned16(ep->norm_scale) && aligned16(ep->residual) && aligned16(c) && ldc % 8 == 0 &&
-                       ep->ld_residual % (ep->residual_dtype == SB_F32 ? 4 : 8) == 0;
-      if (!vec || n > kPlanesNormMaxN)
-        return fail(SB_ERR_ALIGNMENT, "norm_residual_add on the planes path needs N <= 8192 and 16-byte aligned "
-                                      "scale, residual and output rows");
-      auto kernel = (nh / 8 <= 256) ? planes_norm_rows_kernel<1> : planes_norm_rows_kernel<2>;
-      kernel<<<(unsigned)mh, 256, 0, stream>>>(prod, mh, nh, bm, ep->norm_scale, ep->aux_dtype == SB_F32,
-                                               ep->residual, ep->ld_residual, ep->residual_dtype == SB_F32,
-                                               ep->norm_eps, reinterpret_cast<__nv_bfloat16*>(c), ldc);
-      const cudaError_t e = cudaGetLastError();
-      if (e != cudaSuccess) return fail(SB_ERR_CUDA, std::string("planes norm rows launch: ") + cudaGetErrorString(e));
-      return SB_OK;
-    }
-    switch (epi) {
-      case SB_EPI_RESIDUAL_ADD:
-        planes_recombine_kernel<SB_EPI_RESIDUAL_ADD, false><<<grid, 256, 0, stream>>>(prod, mh, nh, ep_p);
-        break;
-      case SB_EPI_BIAS_ADD:
-        planes_recombine_kernel<SB_EPI_BIAS_ADD, false><<<grid, 256, 0, stream>>>(prod, mh, nh, ep_p);
-        break;
-      case SB_EPI_SWIGLU:
-        planes_recombine_kernel<SB_EPI_SWIGLU, false><<<grid, 256, 0, stream>>>(prod, mh, nh, ep_p);
-        break;
-      case SB_EPI_GEGLU:
-        planes_recombine_kernel<SB_EPI_GEGLU, false><<<grid, 256, 0, stream>>>(prod, mh, nh, ep_p);
-        break;
-      case SB_EPI_QK_NORM_ROPE:
-        planes_recombine_kernel<SB_EPI_QK_NORM_ROPE, false><<<grid, 256, 0, stream>>>(prod, mh, nh, ep_p);
-        break;
-      default:
-        if (out_dtype == SB_F32)
-          planes_recombine_kernel<SB_EPI_NONE, true><<<grid, 256, 0, stream>>>(prod, mh, nh, ep_p);
-        else
-          planes_recombine_kernel<SB_EPI_NONE, false><<<grid, 256, 0, stream>>>(prod, mh, nh, ep_p);
-    }
-    const cudaError_t e = cudaGetLastError();
-    if (e != cudaSuccess) return fail(SB_ERR_CUDA, std::string("recombination launch: ") + cudaGetErrorString(e));
-  }
+  if (stages & 4) return planes_recombine(stream, prod, m, n, k, bm, bn, bk, c, ldc, out_dtype, epi, ep, 0, mh);
   return SB_OK;
 }
 
@@ -2521,11 +2607,11 @@ size_t sb_planes_workspace_bytes(int64_t m, int64_t n, int64_t k) {
 int sb_strassen_gemm_planes(sb_stream_t stream_, const void* a, const void* b, void* c, int64_t m, int64_t n,
                             int64_t k, int64_t lda, int64_t ldb, int64_t ldc, int32_t bm, int32_t bn, int32_t bk,
                             int32_t out_dtype, void* workspace, size_t workspace_bytes, int32_t raster,
-                            int32_t stages) {
+                            int32_t stages, void* const* timing_events) {
   int st = validate_core(a, b, c, m, n, k, lda, ldb, ldc, bm, bn, bk, out_dtype);
   if (st != SB_OK) return st;
   return run_planes(reinterpret_cast<cudaStream_t>(stream_), a, b, c, m, n, k, lda, ldb, ldc, bm, bn, bk, out_dtype,
-                    workspace, workspace_bytes, raster, stages);
+                    workspace, workspace_bytes, raster, stages, SB_EPI_NONE, nullptr, timing_events);
 }
 
 int sb_strassen_gemm_quad(sb_stream_t stream_, const void* a, const void* b, void* c, int64_t m, int64_t n,

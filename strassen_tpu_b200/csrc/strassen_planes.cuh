@@ -77,6 +77,7 @@ struct PlanesParams {
   int32_t num_tiles;         // 7 * tiles_m * tiles_n
   int32_t k_steps;           // kh / kBK
   int32_t raster;
+  int32_t tile_m0;           // first product-row tile of this launch (tiles_m tiles from there)
   float* prod;               // [7][mh][nh] fp32
   int* err;
 };
@@ -87,16 +88,19 @@ struct PlanesParams {
 //   P1 a0+a3, P2 a2+a3, P3 a0, P4 a3, P5 a0+a1, P6 a2-a0, P7 a1-a3,
 // each sum rounded once to bf16 (strassen_pallas.py:324-379).  aop is
 // [7][M/2][K/2] bf16, contiguous.  One thread per 8 consecutive kappa.
+// Product rows t0 <= t < t1 only (the whole array when t0 = 0, t1 = M/2).
 __global__ void __launch_bounds__(256) a_operand_planes_kernel(const __nv_bfloat16* __restrict__ a, int64_t lda,
                                                                int32_t m, int32_t k, int32_t bm, int32_t bk,
-                                                               __nv_bfloat16* __restrict__ aop) {
+                                                               __nv_bfloat16* __restrict__ aop, int64_t t0,
+                                                               int64_t t1) {
   const int64_t mh = m / 2, kh = k / 2, hbm = bm / 2, hbk = bk / 2;
   const int64_t per_row = kh / 8;
-  const int64_t items = mh * per_row;
+  const int64_t items = (t1 - t0) * per_row;
   const int64_t plane = mh * kh / 8;  // one plane, in uint4 units
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < items; i += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t t = i / per_row;
-    const int64_t kap = (i - t * per_row) * 8;
+    const int64_t tl = i / per_row;
+    const int64_t t = t0 + tl;
+    const int64_t kap = (i - tl * per_row) * 8;
     const int64_t blk = t / hbm, pnl = kap / hbk;
     const int64_t row0 = blk * bm + (t - blk * hbm);
     const int64_t col0 = pnl * bk + (kap - pnl * hbk);
@@ -129,14 +133,15 @@ __global__ void __launch_bounds__(256) a_operand_planes_kernel(const __nv_bfloat
 // half_bm, half_bn and the epilogue operands as the one-CTA kernel takes them.
 template <int kEpi, bool kOutF32>
 __global__ void __launch_bounds__(256) planes_recombine_kernel(const float* __restrict__ prod, int32_t mh, int32_t nh,
-                                                               const GemmParams p) {
+                                                               const GemmParams p, int64_t t0, int64_t t1) {
   const int64_t plane = (int64_t)mh * nh;
   const int64_t per_row = nh / 8;
-  const int64_t items = (int64_t)mh * per_row;
+  const int64_t items = (t1 - t0) * per_row;
   const int64_t hbm = p.half_bm, hbn = p.half_bn;
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < items; i += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t t = i / per_row;
-    const int64_t u = (i - t * per_row) * 8;
+    const int64_t tl = i / per_row;
+    const int64_t t = t0 + tl;
+    const int64_t u = (i - tl * per_row) * 8;
     const int64_t off = t * nh + u;
     float mv[7][8];
 #pragma unroll
@@ -272,7 +277,7 @@ __global__ void __launch_bounds__(planes::kThreads, 1)
     const int first_m = group * raster;
     const int rows_in_group = min(p.tiles_m - first_m, raster);
     const int in_group = rem - group * per_group;
-    row0 = (first_m + in_group % rows_in_group) * kTileM;
+    row0 = (p.tile_m0 + first_m + in_group % rows_in_group) * kTileM;
     col0 = (in_group / rows_in_group) * kTileN;
   };
 

@@ -723,7 +723,7 @@ def quad_matmul(a, b, *, bm=TUNED_BM, bn=TUNED_BN, bk=TUNED_BK, output_dtype=Non
 
 
 def planes_matmul(a, b, *, bm=TUNED_BM, bn=TUNED_BN, bk=TUNED_BK, output_dtype=None, out=None, workspace=None,
-                  raster=0, stages=7):
+                  raster=0, stages=7, timing_events=None):
     """``strassen_matmul(a, b, bm=, bn=, bk=, output_dtype=)`` without an epilogue,
     as seven full-width product GEMMs (``sb_strassen_gemm_planes``): the A and
     B operand planes of every Strassen block (the reference's pre-adds,
@@ -738,6 +738,12 @@ def planes_matmul(a, b, *, bm=TUNED_BM, bn=TUNED_BN, bk=TUNED_BK, output_dtype=N
     ``stages``: bit 0 the operand passes, bit 1 the product GEMM, bit 2 the
     recombination (7 = all); separate calls with the same ``workspace`` and
     operands give the same result as one call (used to time the GEMM alone).
+    The whole product runs in two halves of product rows on two streams so the
+    passes and recombination of one half overlap the other's GEMM (joined back
+    into the current stream before the call returns).  ``timing_events``: four
+    ``torch.cuda.Event(enable_timing=True)`` the call records around its GEMM
+    launches (the two halves; with ``stages=2`` events 0 and 1 around the one
+    launch).
     """
     if a.ndim != 2 or b.ndim != 2:
         raise ValueError("planes_matmul expects two rank-2 matrices")
@@ -768,10 +774,18 @@ def planes_matmul(a, b, *, bm=TUNED_BM, bn=TUNED_BN, bk=TUNED_BK, output_dtype=N
     elif workspace.dtype != torch.uint8 or workspace.numel() < need or workspace.device != device:
         raise ValueError(f"workspace must be a uint8 tensor of at least {need} bytes on {device}")
     od = SB_F32 if out_dt == torch.float32 else SB_BF16
+    events = None
+    if timing_events is not None:
+        if len(timing_events) != 4:
+            raise ValueError("timing_events must be four torch.cuda.Event(enable_timing=True)")
+        for e in timing_events:
+            e.record()  # materialise the CUDA event on this device (records nothing useful yet)
+        events = (ctypes.c_void_p * 4)(*[e.cuda_event for e in timing_events])
     with torch.cuda.device(device):
         status = lib.sb_strassen_gemm_planes(_stream_handle(device), a.data_ptr(), b.data_ptr(), out.data_ptr(),
                                              m, n, k, _ld(a), _ld(b), _ld(out), bm, bn, bk, od,
-                                             workspace.data_ptr(), workspace.numel(), int(raster), int(stages))
+                                             workspace.data_ptr(), workspace.numel(), int(raster), int(stages),
+                                             events)
     _native.check(status)
     return out
 
