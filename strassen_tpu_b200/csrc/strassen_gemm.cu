@@ -2101,12 +2101,18 @@ struct PlanesSide {
   cudaEvent_t fork = nullptr, b_done = nullptr, join = nullptr;
 };
 
-int planes_side(PlanesSide** out) {
+// *out stays null (the caller runs the halves in sequence) when the side
+// stream does not exist yet and `stream` is being captured into a CUDA graph,
+// where creating streams and events may be refused.
+int planes_side(cudaStream_t stream, PlanesSide** out) {
+  *out = nullptr;
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return fail(SB_ERR_DEVICE, "no usable current device");
   thread_local PlanesSide side[64];
   PlanesSide& s = side[dev];
   if (!s.aux) {
+    cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+    if (cudaStreamIsCapturing(stream, &cap) != cudaSuccess || cap != cudaStreamCaptureStatusNone) return SB_OK;
     cudaError_t e = cudaStreamCreateWithFlags(&s.aux, cudaStreamNonBlocking);
     if (e == cudaSuccess) e = cudaEventCreateWithFlags(&s.fork, cudaEventDisableTiming);
     if (e == cudaSuccess) e = cudaEventCreateWithFlags(&s.b_done, cudaEventDisableTiming);
@@ -2165,10 +2171,12 @@ int run_planes(cudaStream_t stream, const void* a, const void* b, void* c, int64
     return e == cudaSuccess ? SB_OK : fail(SB_ERR_CUDA, std::string(what) + ": " + cudaGetErrorString(e));
   };
 
+  PlanesSide* side = nullptr;
   if (stages == 7 && mh >= 2 * planes::kTileM) {
-    PlanesSide* side = nullptr;
-    st = planes_side(&side);
+    st = planes_side(stream, &side);
     if (st != SB_OK) return st;
+  }
+  if (side) {
     const int64_t half = (mh / planes::kTileM / 2) * planes::kTileM;  // first half's product rows
     cudaStream_t aux = side->aux;
     if ((st = chk(cudaEventRecord(side->fork, stream), "fork")) != SB_OK) return st;

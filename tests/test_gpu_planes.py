@@ -154,3 +154,46 @@ def test_planes_epilogues_match_one_cta_kernel(epilogue):
     torch.cuda.synchronize()
     assert seven.shape == one.shape
     assert_parity(host(seven), host(one), rounding_step=True)
+
+
+def _capture_and_replay(fn):
+    g = torch.cuda.CUDAGraph()
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        with torch.cuda.graph(g):
+            out = fn()
+    torch.cuda.current_stream().wait_stream(s)
+    g.replay()
+    torch.cuda.synchronize()
+    return out, g
+
+
+def test_planes_path_in_a_cuda_graph():
+    """The two-half schedule (a fork onto the library's side stream and a join)
+    captures into a CUDA graph; a host thread that has never run the planes path
+    captures the halves in sequence instead.  Both replay the eager result."""
+    import threading
+    import strassen_tpu_b200 as sb
+    m, k, n = 8192, 4096, 4096
+    g = torch.Generator(device="cuda").manual_seed(12)
+    a = torch.randn(m, k, device="cuda", generator=g).to(torch.bfloat16)
+    b = torch.randn(k, n, device="cuda", generator=g).to(torch.bfloat16)
+    tile = dict(bm=1024, bn=1024, bk=512)
+    want = sb.strassen_matmul(a, b, **tile)
+    ws = torch.empty(sb.workspace_bytes(m, n, k), dtype=torch.uint8, device="cuda")
+    out, graph = _capture_and_replay(lambda: sb.strassen_matmul(a, b, workspace=ws, **tile))
+    assert torch.equal(out, want)
+    del graph
+    result = {}
+
+    def fresh_thread():
+        torch.cuda.set_device(a.device)
+        o, gr = _capture_and_replay(lambda: sb.strassen_matmul(a, b, workspace=ws, **tile))
+        result["equal"] = torch.equal(o, want)
+        del gr
+
+    t = threading.Thread(target=fresh_thread)
+    t.start()
+    t.join()
+    assert result.get("equal") is True
