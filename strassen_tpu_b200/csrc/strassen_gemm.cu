@@ -2095,7 +2095,9 @@ int planes_recombine(cudaStream_t stream, const float* prod, int64_t m, int64_t 
 }
 
 // A second stream and fork/join events per device and host thread, created on
-// first use: the planes path runs its second row half there.
+// first use and kept for the thread's life (not destroyed at thread exit, where
+// the CUDA runtime may already be shutting down): the planes path runs its
+// second row half there.
 struct PlanesSide {
   cudaStream_t aux = nullptr;
   cudaEvent_t fork = nullptr, b_done = nullptr, join = nullptr;
@@ -2181,24 +2183,29 @@ int run_planes(cudaStream_t stream, const void* a, const void* b, void* c, int64
     cudaStream_t aux = side->aux;
     if ((st = chk(cudaEventRecord(side->fork, stream), "fork")) != SB_OK) return st;
     if ((st = chk(cudaStreamWaitEvent(aux, side->fork, 0), "fork wait")) != SB_OK) return st;
-    st = sb_strassen_b_operands(reinterpret_cast<sb_stream_t>(stream), b, bop, k, n, ldb, bn, bk);
-    if (st != SB_OK) return st;
-    if ((st = chk(cudaEventRecord(side->b_done, stream), "B planes event")) != SB_OK) return st;
-    if ((st = planes_a_pass(stream, a, lda, m, k, bm, bk, aop, 0, half)) != SB_OK) return st;
-    if ((st = planes_a_pass(aux, a, lda, m, k, bm, bk, aop, half, mh)) != SB_OK) return st;
-    if ((st = chk(cudaStreamWaitEvent(aux, side->b_done, 0), "B planes wait")) != SB_OK) return st;
-    if (ev(0) && (st = chk(cudaEventRecord(ev(0), stream), "timing event")) != SB_OK) return st;
-    if ((st = planes_gemm(stream, ta, tb, m, n, k, raster, prod, 0, half)) != SB_OK) return st;
-    if (ev(1) && (st = chk(cudaEventRecord(ev(1), stream), "timing event")) != SB_OK) return st;
-    if (ev(2) && (st = chk(cudaEventRecord(ev(2), aux), "timing event")) != SB_OK) return st;
-    if ((st = planes_gemm(aux, ta, tb, m, n, k, raster, prod, half, mh)) != SB_OK) return st;
-    if (ev(3) && (st = chk(cudaEventRecord(ev(3), aux), "timing event")) != SB_OK) return st;
-    if ((st = planes_recombine(stream, prod, m, n, k, bm, bn, bk, c, ldc, out_dtype, epi, ep, 0, half)) != SB_OK)
-      return st;
-    if ((st = planes_recombine(aux, prod, m, n, k, bm, bn, bk, c, ldc, out_dtype, epi, ep, half, mh)) != SB_OK)
-      return st;
-    if ((st = chk(cudaEventRecord(side->join, aux), "join")) != SB_OK) return st;
-    return chk(cudaStreamWaitEvent(stream, side->join, 0), "join wait");
+    // Everything issued to the side stream is joined back into `stream`, on
+    // failure too, so no later call overlaps this one's work.
+    auto halves = [&]() -> int {
+      int s2 = sb_strassen_b_operands(reinterpret_cast<sb_stream_t>(stream), b, bop, k, n, ldb, bn, bk);
+      if (s2 != SB_OK) return s2;
+      if ((s2 = chk(cudaEventRecord(side->b_done, stream), "B planes event")) != SB_OK) return s2;
+      if ((s2 = planes_a_pass(stream, a, lda, m, k, bm, bk, aop, 0, half)) != SB_OK) return s2;
+      if ((s2 = planes_a_pass(aux, a, lda, m, k, bm, bk, aop, half, mh)) != SB_OK) return s2;
+      if ((s2 = chk(cudaStreamWaitEvent(aux, side->b_done, 0), "B planes wait")) != SB_OK) return s2;
+      if (ev(0) && (s2 = chk(cudaEventRecord(ev(0), stream), "timing event")) != SB_OK) return s2;
+      if ((s2 = planes_gemm(stream, ta, tb, m, n, k, raster, prod, 0, half)) != SB_OK) return s2;
+      if (ev(1) && (s2 = chk(cudaEventRecord(ev(1), stream), "timing event")) != SB_OK) return s2;
+      if (ev(2) && (s2 = chk(cudaEventRecord(ev(2), aux), "timing event")) != SB_OK) return s2;
+      if ((s2 = planes_gemm(aux, ta, tb, m, n, k, raster, prod, half, mh)) != SB_OK) return s2;
+      if (ev(3) && (s2 = chk(cudaEventRecord(ev(3), aux), "timing event")) != SB_OK) return s2;
+      if ((s2 = planes_recombine(stream, prod, m, n, k, bm, bn, bk, c, ldc, out_dtype, epi, ep, 0, half)) != SB_OK)
+        return s2;
+      return planes_recombine(aux, prod, m, n, k, bm, bn, bk, c, ldc, out_dtype, epi, ep, half, mh);
+    };
+    st = halves();
+    const int joined = chk(cudaEventRecord(side->join, aux), "join");
+    const int waited = joined == SB_OK ? chk(cudaStreamWaitEvent(stream, side->join, 0), "join wait") : joined;
+    return st != SB_OK ? st : waited;
   }
   if (stages & 1) {
     st = sb_strassen_b_operands(reinterpret_cast<sb_stream_t>(stream), b, bop, k, n, ldb, bn, bk);
