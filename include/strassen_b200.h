@@ -258,8 +258,10 @@ SB_API int sb_strassen_gemm_quad(sb_stream_t stream,
  * stream of the library's (forked from and joined back into `stream`), so each
  * half's passes and recombination overlap the other half's GEMM.
  * `timing_events`: NULL, or four cudaEvent_t the call records around its GEMM
- * launches (stages 7: first half on `stream`, second half on the side stream;
- * stages 2: the one launch, events 0 and 1).
+ * launches: 0/1 around the first half's on `stream`, 2/3 around the second
+ * half's on the side stream; when the GEMM runs as one launch (`stages` 2, a
+ * product under two 256-row tiles, or a first use inside a graph capture)
+ * 0/1 around it and 2/3 at its end.
  * sb_strassen_gemm / sb_strassen_gemm_ex take this path (no research option;
  * no epilogue or residual_add / bias_add / swiglu / geglu / qk_norm_rope) when
  * sb_workspace_bytes asks for the planes workspace and the caller passes it.

@@ -2216,6 +2216,9 @@ int run_planes(cudaStream_t stream, const void* a, const void* b, void* c, int64
     if (ev(0) && (st = chk(cudaEventRecord(ev(0), stream), "timing event")) != SB_OK) return st;
     if ((st = planes_gemm(stream, ta, tb, m, n, k, raster, prod, 0, mh)) != SB_OK) return st;
     if (ev(1) && (st = chk(cudaEventRecord(ev(1), stream), "timing event")) != SB_OK) return st;
+    // One launch: events 2 and 3 mark the same end, so every span stays defined.
+    if (ev(2) && (st = chk(cudaEventRecord(ev(2), stream), "timing event")) != SB_OK) return st;
+    if (ev(3) && (st = chk(cudaEventRecord(ev(3), stream), "timing event")) != SB_OK) return st;
   }
   if (stages & 4) return planes_recombine(stream, prod, m, n, k, bm, bn, bk, c, ldc, out_dtype, epi, ep, 0, mh);
   return SB_OK;
