@@ -41,8 +41,30 @@ def _concat(parts):
     return np.concatenate(parts)
 
 
+def _paired_halves(width: int, bn: int, partner_offset, source_of) -> list[int]:
+    """Column order that puts, per ``bn`` block of the output, ``h = bn/2``
+    consecutive "left" columns in the block's first half and their partners in
+    its second half.
+
+    Output column ``j`` lies in block ``j // bn`` at offset ``o = j % bn``; it
+    takes the left list's entry ``i = (j // bn) * h + o % h``, and the partner
+    of that entry when ``o >= h``.  ``source_of(i)`` maps list entries to
+    source columns and ``partner_offset(i)`` gives the partner's distance.
+    """
+    j = np.arange(width, dtype=np.int64)
+    h = bn // 2
+    i = (j // bn) * h + (j % bn) % h
+    return (source_of(i) + np.where((j % bn) >= h, partner_offset(i), 0)).tolist()
+
+
 def rope_weight_order(n: int, bn: int, head_dim: int = 128) -> list[int]:
-    """Column order of :func:`rope_weight_layout` (strassen_pallas.py:1315-1349)."""
+    """Column order of :func:`rope_weight_layout` (strassen_pallas.py:1315-1349).
+
+    The left list holds every head's first ``head_dim/2`` channels in head
+    order (entry ``i`` is channel ``i % (head_dim/2)`` of head
+    ``i // (head_dim/2)``); each partner is the channel ``head_dim/2`` further
+    on, its rotation pair.  Checks and messages follow the reference.
+    """
     if n % head_dim:
         raise ValueError(f"width {n} is not a multiple of head_dim {head_dim}")
     if bn % (2 * head_dim):
@@ -50,18 +72,10 @@ def rope_weight_order(n: int, bn: int, head_dim: int = 128) -> list[int]:
             f"bn={bn} must be a multiple of 2*head_dim={2 * head_dim} so each "
             "tile half holds whole heads")
     half_head = head_dim // 2
-    heads = n // head_dim
-    a_cols = [h * head_dim + j for h in range(heads) for j in range(half_head)]
-    b_cols = [h * head_dim + half_head + j for h in range(heads) for j in range(half_head)]
-    half = bn // 2
-    if (n // 2) % half:
-        raise ValueError(f"half width {n // 2} is not divisible by bn//2={half}")
-    order: list[int] = []
-    for block in range((n // 2) // half):
-        lo, hi = block * half, (block + 1) * half
-        order.extend(a_cols[lo:hi])
-        order.extend(b_cols[lo:hi])
-    return order
+    if (n // 2) % (bn // 2):
+        raise ValueError(f"half width {n // 2} is not divisible by bn//2={bn // 2}")
+    return _paired_halves(n, bn, lambda i: half_head,
+                          lambda i: (i // half_head) * head_dim + i % half_head)
 
 
 def rope_weight_layout(weight, bn: int, head_dim: int = 128):
@@ -92,19 +106,17 @@ def rope_scale_layout(scale, bn: int, head_dim: int = 128):
 
 
 def swiglu_weight_order(two_i: int, bn: int) -> list[int]:
-    """Column order of :func:`swiglu_weight_layout` (strassen_pallas.py:1381-1411)."""
+    """Column order of :func:`swiglu_weight_layout` (strassen_pallas.py:1381-1411).
+
+    The left list is the gate columns ``0 .. I-1`` in order; each partner is
+    the up column ``I`` further on.  Checks and messages follow the reference.
+    """
     if two_i % 2:
         raise ValueError(f"combined gate/up width {two_i} is not even")
     intermediate = two_i // 2
-    half = bn // 2
-    if intermediate % half:
-        raise ValueError(f"intermediate {intermediate} is not divisible by bn//2={half}")
-    order: list[int] = []
-    for block in range(intermediate // half):
-        start = block * half
-        order.extend(range(start, start + half))
-        order.extend(range(intermediate + start, intermediate + start + half))
-    return order
+    if intermediate % (bn // 2):
+        raise ValueError(f"intermediate {intermediate} is not divisible by bn//2={bn // 2}")
+    return _paired_halves(two_i, bn, lambda i: intermediate, lambda i: i)
 
 
 def swiglu_weight_layout(gate_up, bn: int):
