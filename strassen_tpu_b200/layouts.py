@@ -13,7 +13,7 @@ from __future__ import annotations
 
 import numpy as np
 
-try:  # torch is optional for the pure-numpy users (the oracle, fixtures)
+try:  # torch is optional: the helpers also serve numpy callers (tests, fixture scripts)
     import torch
 except ImportError:  # pragma: no cover
     torch = None
