@@ -119,9 +119,11 @@ def strassen_matmul(
     ``workspace`` (a caller-owned uint8 CUDA buffer of at least
     :func:`workspace_bytes` bytes; allocated from torch's caching allocator
     when omitted -- for a large product without research options and with no
-    epilogue or a residual_add / bias_add / swiglu / geglu / qk_norm_rope
-    epilogue that is the planes path's workspace, and a smaller buffer keeps
-    the product on the one-CTA kernel, see :func:`planes_matmul`) and
+    epilogue, a residual_add / bias_add / swiglu / geglu / qk_norm_rope
+    epilogue, or norm_residual_add at N <= 8192, that is the planes path's
+    workspace, and a smaller buffer keeps the product on the one-CTA kernel,
+    which needs none except M*N*4 bytes of fp32 rows for norm_residual_add;
+    see :func:`planes_matmul`) and
     ``narrow_bn`` (B200 extension, no reference counterpart:
     bn may be any multiple of 128 instead of the reference's TPU lane rule of
     256, and qk_norm_rope then needs bn % rope_head_dim == 0 -- each half block
@@ -274,6 +276,9 @@ def strassen_matmul(
         raise ValueError("strassen_matmul runs on a CUDA device; got CPU tensors (no CPU fallback)")
 
     device = a.device
+    if workspace is not None and (not isinstance(workspace, torch.Tensor) or workspace.device != device
+                                  or not workspace.is_contiguous()):
+        raise ValueError(f"workspace must be a contiguous tensor on {device} (the kernels write it)")
     a = _rowmajor(a)
     b = _rowmajor(b.to(device))
     gated = epilogue in ("swiglu", "geglu")
