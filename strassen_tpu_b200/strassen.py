@@ -79,6 +79,27 @@ def _stream_handle(device: torch.device) -> ctypes.c_void_p:
     return ctypes.c_void_p(torch.cuda.current_stream(device).cuda_stream)
 
 
+def _out_tensor(out, shape, dtype, device):
+    """``out`` checked for what the kernels write (or allocated when None)."""
+    if out is None:
+        return torch.empty(shape, dtype=dtype, device=device)
+    if tuple(out.shape) != tuple(shape) or out.dtype != dtype or out.device != device:
+        raise ValueError(f"out must be a {tuple(shape)} {_dtype_name(dtype)} tensor on {device}")
+    if out.stride(1) != 1 or (out.stride(0) * out.element_size()) % 16 or out.data_ptr() % 16:
+        raise ValueError("out must be row-major with a 16-byte aligned row stride")
+    return out
+
+
+def _workspace_tensor(workspace, need: int, device):
+    """A caller's uint8 workspace checked against ``need`` bytes (or allocated when None)."""
+    if workspace is None:
+        return torch.empty(need, dtype=torch.uint8, device=device)
+    if (workspace.dtype != torch.uint8 or workspace.numel() < need or workspace.device != device
+            or not workspace.is_contiguous()):
+        raise ValueError(f"workspace must be a contiguous uint8 tensor of at least {need} bytes on {device}")
+    return workspace
+
+
 def strassen_matmul(
     a,
     b,
@@ -658,8 +679,7 @@ def pair_matmul(a, b, *, bm=TUNED_BM, bn=TUNED_BN, bk=TUNED_BK, output_dtype=Non
     out_dt = _as_torch_dtype(output_dtype) or torch.bfloat16
     device = a.device
     a = _rowmajor(a)
-    if out is None:
-        out = torch.empty((m, n), dtype=out_dt, device=device)
+    out = _out_tensor(out, (m, n), out_dt, device)
     lib = _native.load()
     od = SB_F32 if out_dt == torch.float32 else SB_BF16
     with torch.cuda.device(device):
@@ -710,14 +730,9 @@ def quad_matmul(a, b, *, bm=TUNED_BM, bn=TUNED_BN, bk=TUNED_BK, output_dtype=Non
     device = a.device
     a = _rowmajor(a)
     b = _rowmajor(b)
-    if out is None:
-        out = torch.empty((m, n), dtype=out_dt, device=device)
+    out = _out_tensor(out, (m, n), out_dt, device)
     lib = _native.load()
-    need = int(lib.sb_quad_workspace_bytes(m, n, k))
-    if workspace is None:
-        workspace = torch.empty(need, dtype=torch.uint8, device=device)
-    elif workspace.dtype != torch.uint8 or workspace.numel() < need or workspace.device != device:
-        raise ValueError(f"workspace must be a uint8 tensor of at least {need} bytes on {device}")
+    workspace = _workspace_tensor(workspace, int(lib.sb_quad_workspace_bytes(m, n, k)), device)
     od = SB_F32 if out_dt == torch.float32 else SB_BF16
     with torch.cuda.device(device):
         status = lib.sb_strassen_gemm_quad(_stream_handle(device), a.data_ptr(), b.data_ptr(), out.data_ptr(),
@@ -747,8 +762,10 @@ def planes_matmul(a, b, *, bm=TUNED_BM, bn=TUNED_BN, bk=TUNED_BK, output_dtype=N
     passes and recombination of one half overlap the other's GEMM (joined back
     into the current stream before the call returns).  ``timing_events``: four
     ``torch.cuda.Event(enable_timing=True)`` the call records around its GEMM
-    launches (the two halves; with ``stages=2`` events 0 and 1 around the one
-    launch).
+    launches: 0/1 around the first half's, 2/3 around the second half's; when
+    the GEMM runs as one launch (``stages=2``, fewer than two 256-row product
+    tiles, or a first call inside a graph capture) 0/1 around it and 2/3 at its
+    end.
     """
     if a.ndim != 2 or b.ndim != 2:
         raise ValueError("planes_matmul expects two rank-2 matrices")
@@ -770,23 +787,18 @@ def planes_matmul(a, b, *, bm=TUNED_BM, bn=TUNED_BN, bk=TUNED_BK, output_dtype=N
     device = a.device
     a = _rowmajor(a)
     b = _rowmajor(b)
-    if out is None:
-        out = torch.empty((m, n), dtype=out_dt, device=device)
+    out = _out_tensor(out, (m, n), out_dt, device)
     lib = _native.load()
-    need = int(lib.sb_planes_workspace_bytes(m, n, k))
-    if workspace is None:
-        workspace = torch.empty(need, dtype=torch.uint8, device=device)
-    elif workspace.dtype != torch.uint8 or workspace.numel() < need or workspace.device != device:
-        raise ValueError(f"workspace must be a uint8 tensor of at least {need} bytes on {device}")
+    workspace = _workspace_tensor(workspace, int(lib.sb_planes_workspace_bytes(m, n, k)), device)
     od = SB_F32 if out_dt == torch.float32 else SB_BF16
     events = None
-    if timing_events is not None:
-        if len(timing_events) != 4:
-            raise ValueError("timing_events must be four torch.cuda.Event(enable_timing=True)")
-        for e in timing_events:
-            e.record()  # materialise the CUDA event on this device (records nothing useful yet)
-        events = (ctypes.c_void_p * 4)(*[e.cuda_event for e in timing_events])
+    if timing_events is not None and len(timing_events) != 4:
+        raise ValueError("timing_events must be four torch.cuda.Event(enable_timing=True)")
     with torch.cuda.device(device):
+        if timing_events is not None:
+            for e in timing_events:
+                e.record()  # creates the CUDA event on this device; the call records it again
+            events = (ctypes.c_void_p * 4)(*[e.cuda_event for e in timing_events])
         status = lib.sb_strassen_gemm_planes(_stream_handle(device), a.data_ptr(), b.data_ptr(), out.data_ptr(),
                                              m, n, k, _ld(a), _ld(b), _ld(out), bm, bn, bk, od,
                                              workspace.data_ptr(), workspace.numel(), int(raster), int(stages),
