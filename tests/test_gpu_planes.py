@@ -116,6 +116,10 @@ def test_planes_validation():
     b = torch.zeros(256, 512, dtype=torch.bfloat16, device="cuda")
     with pytest.raises(ValueError, match="workspace"):
         sb.planes_matmul(a, b, bm=256, bn=256, bk=256, workspace=torch.empty(16, dtype=torch.uint8, device="cuda"))
+    with pytest.raises(ValueError, match="out must be"):
+        sb.planes_matmul(a, b, bm=256, bn=256, bk=256, out=torch.empty(512, 256, dtype=torch.bfloat16, device="cuda"))
+    with pytest.raises(ValueError, match="workspace must be a contiguous"):
+        sb.planes_matmul(a, b, bm=256, bn=256, bk=256, workspace=torch.empty(16, dtype=torch.uint8))
     # strassen_matmul refuses a workspace the kernels could not write.
     for bad in (torch.empty(16, dtype=torch.uint8), torch.empty(32, dtype=torch.uint8, device="cuda")[::2]):
         with pytest.raises(ValueError, match="workspace must be a contiguous tensor"):
