@@ -815,13 +815,23 @@ def rms_norm(x, scale, eps: float = 1e-6, out=None):
     """
     if x.dtype != torch.bfloat16:
         raise ValueError("rms_norm expects a bf16 input")
+    if not x.is_cuda:
+        raise ValueError("rms_norm runs on a CUDA device (no CPU fallback)")
     n = x.shape[-1]
+    if scale.numel() != n:
+        raise ValueError(f"scale must hold {n} values (the row width), got {scale.numel()}")
     x2 = x.reshape(-1, n).contiguous()
-    w = scale.to(device=x.device)
+    w = scale.to(device=x.device).reshape(n)
     if w.dtype not in (torch.bfloat16, torch.float32):
         w = w.float()
     w = w.contiguous()
-    y = torch.empty_like(x2) if out is None else out.reshape(-1, n)
+    if out is None:
+        y = torch.empty_like(x2)
+    else:
+        if tuple(out.shape) != tuple(x.shape) or out.dtype != torch.bfloat16 or out.device != x.device \
+                or not out.is_contiguous():
+            raise ValueError(f"out must be a contiguous {tuple(x.shape)} bfloat16 tensor on {x.device}")
+        y = out.view(-1, n)
     lib = _native.load()
     with torch.cuda.device(x.device):
         status = lib.sb_rms_norm(_stream_handle(x.device), x2.data_ptr(), w.data_ptr(), y.data_ptr(),

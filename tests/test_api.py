@@ -233,3 +233,14 @@ def test_planes_matmul_value_errors(kw, match):
     kw.setdefault("bk", 256)
     with pytest.raises(ValueError, match=match):
         sb.planes_matmul(a, b, **kw)
+
+
+# --- rms_norm (the row kernel the decoder's norms run on) -----------------------
+
+@pytest.mark.parametrize("x, scale, match", [
+    (torch.zeros(4, 256), torch.ones(256), "expects a bf16 input"),
+    (torch.zeros(4, 256, dtype=BF), torch.ones(256), "no CPU fallback"),
+])
+def test_rms_norm_value_errors(x, scale, match):
+    with pytest.raises(ValueError, match=match):
+        sb.rms_norm(x, scale)
