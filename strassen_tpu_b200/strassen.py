@@ -815,11 +815,11 @@ def rms_norm(x, scale, eps: float = 1e-6, out=None):
     """
     if x.dtype != torch.bfloat16:
         raise ValueError("rms_norm expects a bf16 input")
-    if not x.is_cuda:
-        raise ValueError("rms_norm runs on a CUDA device (no CPU fallback)")
     n = x.shape[-1]
     if scale.numel() != n:
         raise ValueError(f"scale must hold {n} values (the row width), got {scale.numel()}")
+    if not x.is_cuda:
+        raise ValueError("rms_norm runs on a CUDA device (no CPU fallback)")
     x2 = x.reshape(-1, n).contiguous()
     w = scale.to(device=x.device).reshape(n)
     if w.dtype not in (torch.bfloat16, torch.float32):

@@ -239,6 +239,7 @@ def test_planes_matmul_value_errors(kw, match):
 
 @pytest.mark.parametrize("x, scale, match", [
     (torch.zeros(4, 256), torch.ones(256), "expects a bf16 input"),
+    (torch.zeros(4, 256, dtype=BF), torch.ones(128), "scale must hold 256 values"),
     (torch.zeros(4, 256, dtype=BF), torch.ones(256), "no CPU fallback"),
 ])
 def test_rms_norm_value_errors(x, scale, match):
