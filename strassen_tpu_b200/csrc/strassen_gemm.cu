@@ -2120,6 +2120,12 @@ int planes_side(cudaStream_t stream, PlanesSide** out) {
     if (e == cudaSuccess) e = cudaEventCreateWithFlags(&s.b_done, cudaEventDisableTiming);
     if (e == cudaSuccess) e = cudaEventCreateWithFlags(&s.join, cudaEventDisableTiming);
     if (e != cudaSuccess) {
+      // Release whatever was created so the next call starts from scratch.
+      for (cudaEvent_t* ev : {&s.fork, &s.b_done, &s.join}) {
+        if (*ev) cudaEventDestroy(*ev);
+        *ev = nullptr;
+      }
+      if (s.aux) cudaStreamDestroy(s.aux);
       s.aux = nullptr;
       return fail(SB_ERR_CUDA, std::string("planes side stream: ") + cudaGetErrorString(e));
     }
