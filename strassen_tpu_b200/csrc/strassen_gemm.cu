@@ -13,25 +13,41 @@
 // P = kappa / (bk/2).  The reference's quadrant q of block (I, J) is the
 // matrix element (I*bm + qr*bm/2 + r', J*bn + qc*bn/2 + c').
 //
-// B200 mapping (one CTA per SM, persistent over nothing -- one output tile):
+// This file holds two layouts of that computation and the C ABI over both.
+//
+// The planes path (strassen_planes.cuh; the default for large products):
+// operand passes write the seven A and seven B operands of every block as
+// planes in a caller workspace, one persistent kernel runs the seven product
+// GEMMs on CTA pairs (tcgen05 cta_group::2, 256 x 256 tiles) into fp32
+// products, and a recombination pass applies the fused epilogue; two halves
+// of the product rows run on two streams.  sb_workspace_bytes asks for its
+// workspace where a cost model predicts it wins.
+//
+// The one-CTA fused kernel below (small products, the research options,
+// narrow tiles, the no-allocation entry point), one CTA per SM and one output
+// tile per CTA:
 //   * CTA tile: 128 product rows x 64 product columns, i.e. a 256 x 128 patch
 //     of C made of four 128 x 64 quadrant pieces.
 //   * TMEM: seven fp32 accumulators M1..M7 of 128 lanes x 64 columns
-//     (448 of the 512 columns).
-//   * Warp 0: TMA producer.  Per K-chunk it loads the four raw A quadrant
-//     tiles (128 x 32, K-major, 64B swizzle) and four raw B quadrant tiles
-//     (32 x 64, N-major, 128B swizzle) into one pipeline stage.
-//   * Warps 4..11: operand-sum warps.  They form the five A sums and five B
-//     sums in place in shared memory with bf16x2 adds (round-to-nearest-even,
-//     exactly the reference's bf16 pre-add rounding).  All tiles of a stage
-//     share one shape and swizzle, so the sums are plain elementwise ops over
-//     the raw 16-byte chunks.
-//   * Warp 1: TMEM allocator and single-thread tcgen05.mma issuer (7 products
-//     x BLOCK_K/16 MMAs of 128x64x16 per chunk), committing to mbarriers.
+//     (448 of the 512 columns) plus a two-step ring of A sums (448..511).
+//   * Warp 0: TMA producer.  Per 16-deep K step ONE copy lands the four raw A
+//     quadrant tiles (128 x 16, 32-byte swizzle) and ONE copy the four raw B
+//     quadrant tiles (16 x 64, 128-byte swizzle), through tensor maps whose
+//     extra dimensions are the quadrant offsets.
+//   * Warps 4..11: two sets of four operand-sum warps on alternate K steps.
+//     They form the A and B sums with bf16x2 adds (round-to-nearest-even,
+//     exactly the reference's bf16 pre-add rounding): a0+a1 and the five B
+//     sums in place in shared memory, the other four A sums into the TMEM
+//     ring for A-from-TMEM MMAs.
+//   * Warp 1: TMEM allocator and single-thread tcgen05.mma issuer: per step
+//     one wait, seven 128x64x16 MMAs and one commit that frees the stage.
 //   * Warps 4..11 again, after the K loop: epilogue.  Each thread owns one
 //     TMEM lane (= one product row), reads M1..M7 with tcgen05.ld, recombines
 //     C11 = M1+M4-M5+M7, C12 = M3+M5, C21 = M2+M4, C22 = M1-M2+M3+M6 in fp32,
 //     applies the fused epilogue and stores bf16 (or fp32).
+//
+// The opt-in two-CTA (strassen_pair.cuh) and four-CTA (strassen_quad.cuh)
+// kernels split the seven products over the CTAs of a cluster.
 //
 // The same skeleton also runs the matched-tile classical control (eight
 // sub-block products into four accumulators, no operand sums), which mirrors
