@@ -22,7 +22,13 @@ whose per-rank width no 256-multiple tile divides (k and v at TP=8: one
 128-wide kv head, below the reference's bn = 2*head_dim) runs on 128-wide tiles
 (strassen_matmul(narrow_bn=True), a B200 extension: one head per tile, so the
 weight needs no relayout); a site that fits neither uses the native arm, the
-same per-site choice the reference's harness makes.
+same per-site choice the reference's harness makes.  ``native_sites`` moves
+named sites to the native arm as well; :func:`measured_native_sites` chooses
+them by timing every site of one layer of the shard on both arms (rank 0
+times, every rank receives the choice), as the reference's harness picks
+sites from its measurements.  Large Strassen sites run on the planes path
+(``strassen_matmul`` takes the workspace it asks for from torch's caching
+allocator); small-K shards stay on the one-CTA kernel.
 
 Weights are random (N(0, 0.02); norm weights 1 + N(0, 0.02)) from per-tensor
 seeds: every rank generates the same full tensor and keeps its shard.
