@@ -104,3 +104,38 @@ def test_planes_path_choice_follows_the_cost_model():
     assert lib.sb_workspace_bytes(8192, 8192, 8192, 6) == lib.sb_planes_workspace_bytes(8192, 8192, 8192)
     assert lib.sb_workspace_bytes(8192, 16384, 8192, 6) == 8192 * 16384 * 4
     assert lib.sb_workspace_bytes(1024, 1024, 1024, 6) == 1024 * 1024 * 4
+
+
+def _planes(lib, m=512, n=512, k=256, ws=4096, ws_bytes=None, raster=0, stages=7, ptr=4096):
+    p = ctypes.c_void_p(ptr)
+    need = lib.sb_planes_workspace_bytes(m, n, k)
+    return lib.sb_strassen_gemm_planes(None, p, p, p, m, n, k, k, n, n, 256, 256, 256, 0,
+                                       ctypes.c_void_p(ws) if ws else None,
+                                       need if ws_bytes is None else ws_bytes, raster, stages, None)
+
+
+@pytest.mark.parametrize("kw, status, text", [
+    (dict(m=256), 5, "M and N divisible by 512"),
+    (dict(k=64), 4, "K=64 is not divisible by 256"),
+    (dict(ws=0), 10, "sb_planes_workspace_bytes"),
+    (dict(ws_bytes=16), 10, "needs a workspace of"),
+    (dict(ws=4100), 9, "workspace must be 16-byte aligned"),
+    (dict(raster=-1), 8, "raster must be >= 0"),
+    (dict(stages=0), 8, "stages must be a nonzero mask"),
+    (dict(stages=8), 8, "stages must be a nonzero mask"),
+])
+def test_planes_entry_validation_codes(kw, status, text):
+    """sb_strassen_gemm_planes refuses bad arguments on the host, before any
+    device call, with the status and message a caller can act on."""
+    lib = _native.load()
+    assert _planes(lib, **kw) == status
+    assert text in lib.sb_last_error_message().decode()
+
+
+def test_planes_workspace_bytes_formula():
+    """Operand planes (bf16) plus the seven fp32 products, per the header."""
+    lib = _native.load()
+    for m, n, k in ((512, 512, 128), (8192, 8192, 8192), (16384, 24576, 4096)):
+        planes = 7 * (m // 2 * k // 2 + k // 2 * n // 2) * 2
+        products = 7 * (m // 2) * (n // 2) * 4
+        assert lib.sb_planes_workspace_bytes(m, n, k) == planes + products
