@@ -11,7 +11,9 @@
  * that passes less gets the one-CTA kernel, which needs none); the one
  * exception is
  * sb_strassen_gemm_norm_residual_noalloc, whose scratch is a fixed 32 MiB
- * device array built into the library (see its declaration).
+ * device array built into the library (see its declaration).  Besides
+ * memory, the planes path creates one side stream and three events per device
+ * and host thread on first use and keeps them for the thread's life.
  *
  * The single operator mirrors strassen_pallas.strassen_matmul
  * (reference: strassen_pallas.py:882-1221).  Matrix semantics follow the
